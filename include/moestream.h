@@ -1,0 +1,203 @@
+/*
+ * moestream.h -- C ABI of libmoestream.so, the B200 (sm_100a) implementation
+ * of moe-stream's per-token MoE expert block and its shared slot pool.
+ *
+ * Every entry point returns an int status: MS_OK (0) or a negative MS_E_*
+ * code; ms_last_error() gives the message of the most recent failure on the
+ * calling thread. No C++ exception crosses this boundary. Device buffers are
+ * caller-owned and passed as raw pointers plus a CUDA stream (cudaStream_t,
+ * passed as void*); the library owns the slot arena, the slot table and its
+ * scratch buffers. One host thread at a time may use a pool handle.
+ *
+ * Reference interfaces each entry point replaces are cited as file:line in
+ * the reference repository (agastya-choudhary123/moe-stream).
+ */
+#ifndef MOESTREAM_H
+#define MOESTREAM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status codes */
+#define MS_OK             0
+#define MS_E_INVALID     -1   /* bad argument (ValueError-like)                    */
+#define MS_E_CUDA        -2   /* a CUDA call failed                                */
+#define MS_E_EXHAUSTED   -3   /* "pool exhausted: every slot pinned or pending"
+                                 (engine_v3.py:355-356, RuntimeError)              */
+#define MS_E_TIMEOUT     -4   /* a bounded wait ran out                            */
+#define MS_E_NOMEM       -5   /* allocation failed                                 */
+#define MS_E_STATE       -6   /* call not valid in the handle's current state      */
+#define MS_E_IO          -7   /* store read out of range / short (IOError,
+                                 engine_v3.py:283-284)                             */
+
+/* ------------------------------------------------------------- enumerations */
+#define MS_MODEL_QWEN3    0   /* engine_v3.py: softmax over E, top-k, renormalise  */
+#define MS_MODEL_GPTOSS   1   /* engine_120b.py: top-k logits, softmax over k,
+                                 per-projection bias, clamped SwiGLU               */
+
+#define MS_EVICT_LFU      0   /* MOE_EVICT=lfu  (engine_v3.py:103, 347-348)        */
+#define MS_EVICT_LRU      1   /* MOE_EVICT=lru  (engine_v3.py:345-346)             */
+#define MS_EVICT_ASIS     2   /* MOE_EVICT=asis (engine_v3.py:343-344)             */
+
+#define MS_PROJ_GATE      0
+#define MS_PROJ_UP        1
+#define MS_PROJ_DOWN      2
+#define MS_PART_WEIGHT    0   /* U32 [out, in/8]  4-bit codes, low nibble first    */
+#define MS_PART_SCALES    1   /* BF16 [out, in/group]                              */
+#define MS_PART_BIASES    2   /* BF16 [out, in/group]  (quantisation biases)       */
+#define MS_PART_BIAS      3   /* BF16 [out]  gpt-oss projection bias               */
+
+#define MS_MAX_DEPTHS     4
+
+/* ---------------------------------------------------------------- structures */
+/* Geometry of one model's expert blobs: experts_index.json (repack.py:137-146,
+ * repack_gptoss.py:159-166) plus the model config fields the block reads. */
+typedef struct ms_geom {
+    int32_t model;            /* MS_MODEL_*                                        */
+    int32_t d_model;          /* hidden size (2048 / 2880)                         */
+    int32_t d_ff;             /* expert intermediate size (768 / 2880)             */
+    int32_t n_experts;        /* experts per layer (128)                           */
+    int32_t n_layers;         /* 48 / 36                                           */
+    int32_t top_k;            /* 8 / 4                                             */
+    int32_t group_size;       /* quantisation group (64)                           */
+    int32_t bits;             /* 4                                                 */
+    int32_t norm_topk_prob;   /* Qwen3 renormalisation flag                        */
+    int32_t proj_bias;        /* 1 if blobs carry the gpt-oss `bias` component     */
+    int64_t blob_bytes;       /* padded blob size, a multiple of 16 KiB            */
+    int64_t comp_offset[3][4];/* byte offset of [proj][part] in a blob, -1 if none */
+} ms_geom;
+
+/* Pool configuration: PF_SLOTS, MOE_EVICT, PF_DEPTH, PF_WIDEN
+ * (engine_v3.py:59-62, 84, 103). */
+typedef struct ms_pool_config {
+    int32_t n_slots;                  /* slots in the HBM arena                    */
+    int32_t evict;                    /* MS_EVICT_*                                */
+    int32_t n_depths;                 /* entries used in depths[] (0 = no prefetch)*/
+    int32_t depths[MS_MAX_DEPTHS];    /* prefetch distances; depths[0] sets the
+                                         young-entry window 24*depth (:310-311)    */
+    int32_t pf_widen;                 /* speculate top (k * pf_widen) (:84)        */
+    int32_t max_tokens;               /* largest T any block call will pass        */
+} ms_pool_config;
+
+/* ExpertPool.stats() (engine_v3.py:456-464). Counts, not timings: the
+ * reference's blocked/busy_s/depth fields have no device-side equivalent. */
+typedef struct ms_stats {
+    int64_t total;            /* prefetch + cache + miss                           */
+    int64_t prefetch;         /* hits on a slot filled by a prefetch               */
+    int64_t cache;            /* true cache hits                                   */
+    int64_t miss;             /* demand misses (read on the critical path)         */
+    int64_t bail;             /* prefetches abandoned on exhaustion                */
+    int64_t issued;           /* prefetch reads issued                             */
+    int64_t reads;            /* completed slot fills                              */
+    int64_t exposed;          /* demand-miss fills                                 */
+    int64_t bytes_read;       /* reads * blob_bytes                                */
+    int64_t bytes_exposed;    /* exposed * blob_bytes                              */
+} ms_stats;
+
+typedef struct ms_pool ms_pool;
+
+/* ------------------------------------------------------------------ errors */
+/* Copies the last error message of this thread into buf (NUL-terminated). */
+int ms_last_error(char* buf, size_t n);
+
+/* ---------------------------------------------------------------- the pool */
+/* ExpertPool.__init__ (engine_v3.py:128-252): one contiguous HBM arena of
+ * n_slots * blob_bytes, slot s at arena + s*blob_bytes, laid out exactly like
+ * a store blob, plus the device slot table and scratch for max_tokens. */
+int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device,
+                   ms_pool** out);
+int ms_pool_destroy(ms_pool* pool);
+
+/* The expert store: (layer, expert) at (layer*n_experts + expert)*blob_bytes
+ * (repack.py:141). ms_store_register maps caller memory (pinned or pageable;
+ * it is page-locked and mapped for the device); ms_store_alloc allocates
+ * mapped pinned memory the pool owns. Replaces the experts.bin fd + preadv
+ * worker threads (engine_v3.py:138, 255-301). */
+int ms_store_register(ms_pool* pool, void* host, size_t bytes);
+int ms_store_alloc(ms_pool* pool, size_t bytes, void** host_out);
+
+/* Router weights of one layer: bf16 [n_experts, d_model] and optional bf16
+ * bias [n_experts] (the gate / router Linear the block reads as self.gate /
+ * self.router, engine_v3.py:507, engine_120b.py:84). Device pointers. */
+int ms_set_router(ms_pool* pool, int layer, const void* w_r, const void* b_r);
+
+/* ExpertPool.prefetch (engine_v3.py:383-396): non-blocking; experts is a
+ * host array. Allocation and fills are enqueued on `stream`. */
+int ms_pool_prefetch(ms_pool* pool, int layer, const int32_t* experts, int n,
+                     void* stream);
+
+/* ExpertPool.acquire (engine_v3.py:398-454): blocking; writes the slot of
+ * each expert to the host array slots_out. Returns MS_E_EXHAUSTED when the
+ * reference would raise "pool exhausted". */
+int ms_pool_acquire(ms_pool* pool, int layer, const int32_t* experts, int n,
+                    int32_t* slots_out, void* stream);
+
+/* ExpertPool._read (engine_v3.py:255-290): copy one blob from the store
+ * into a slot, bypassing the table (verify_pool.py:200, 212 use it so). */
+int ms_pool_read(ms_pool* pool, int slot, int layer, int expert, void* stream);
+
+/* ExpertPool.stats (engine_v3.py:456-464). Synchronises the pool. */
+int ms_pool_stats(ms_pool* pool, ms_stats* out);
+
+/* ExpertPool.key_of as layer*n_experts+expert per slot, -1 when empty
+ * (engine_v3.py:216). out has n_slots entries. Synchronises the pool. */
+int ms_pool_slot_table(ms_pool* pool, int32_t* out);
+
+/* ExpertPool.views[name] base (engine_v3.py:180-194): device address of
+ * component [proj][part] of slot 0; slot s is at + s*blob_bytes. */
+int ms_pool_component_ptr(ms_pool* pool, int proj, int part, void** out);
+
+/* Whole arena: base address and size in bytes. */
+int ms_pool_arena(ms_pool* pool, void** base, size_t* bytes);
+
+/* ------------------------------------------------------------- the block */
+/* top_k_experts / top_k_route + top_k_indices (engine_v3.py:467-483,
+ * engine_120b.py:65-75) without touching the pool: x bf16 [T, d_model] ->
+ * inds int32 [T, top_k], scores bf16 [T, top_k] (descending, exact ties to
+ * the lower expert), and, when pred != NULL and layer+depths[0] has a
+ * router, pred int32 [T, top_k*pf_widen] for that layer. */
+int ms_route(ms_pool* pool, int layer, const void* x, int T, int32_t* inds,
+             void* scores, int32_t* pred, void* stream);
+
+/* streaming_call (engine_v3.py:493-609, engine_120b.py:78-149): route,
+ * prefetch layer+d for every configured depth, acquire this layer's experts,
+ * fill misses from the store, run the 4-bit expert MLPs and the weighted
+ * combine. x, y bf16 [T, d_model] device buffers; T <= max_tokens.
+ * Enqueued on `stream`; does not synchronise. Pool exhaustion is reported by
+ * the next ms_pool_status / ms_pool_stats call. */
+int ms_moe_block(ms_pool* pool, int layer, const void* x, int T, void* y,
+                 void* stream);
+
+/* Sticky device-side status of asynchronous block calls (MS_OK or the first
+ * MS_E_* seen since the last call); clears it. Synchronises `stream`. */
+int ms_pool_status(ms_pool* pool, void* stream);
+
+/* kernels.moe_expert_mlp (kernels.py:231-252), generalised to T tokens:
+ * slots int32 [T, k] and scores f32 [T, k] (device), x bf16 [T, d_model],
+ * y bf16 [T, d_model]. Reads the arena only; no routing, no table. */
+int ms_expert_mlp(ms_pool* pool, const int32_t* slots, const float* scores,
+                  const void* x, int T, int k, void* y, void* stream);
+
+/* Device-side routing/slot buffers of the most recent ms_moe_block call
+ * (valid until the next call): inds int32 [T,k], scores bf16 [T,k],
+ * slots int32 [T,k]. For parity dumps. */
+int ms_block_debug(ms_pool* pool, const int32_t** inds, const void** scores,
+                   const int32_t** slots);
+
+/* Per-layer CUDA-event timing of ms_moe_block (off by default). When on,
+ * every block call records four events on its stream -- before the router,
+ * after the router/table step, after the fills, after the expert kernels --
+ * also inside a CUDA graph capture (they become event nodes). ms_pool_timing
+ * reads the last recorded interval of `layer`, in milliseconds:
+ * out[0] router+table, out[1] fills, out[2] expert kernels. */
+int ms_pool_profile(ms_pool* pool, int enable);
+int ms_pool_timing(ms_pool* pool, int layer, float* out3);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOESTREAM_H */

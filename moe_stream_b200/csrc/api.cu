@@ -1,0 +1,626 @@
+// Host side of libmoestream: the C ABI declared in include/moestream.h.
+// Owns the slot arena, the device slot table, the mapped store and every
+// scratch buffer; launches the kernels of route.cu and expert.cu.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/moestream.h"
+#include "kernels.h"
+
+using namespace ms;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define CK(call)                                                                       \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      return fail(MS_E_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                  __FILE__, __LINE__);                                                 \
+  } while (0)
+
+template <typename T>
+int dalloc(T** p, size_t count) {
+  *p = nullptr;
+  if (count == 0) count = 1;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T));
+  if (e != cudaSuccess)
+    return fail(MS_E_NOMEM, "cudaMalloc(%zu bytes): %s", count * sizeof(T), cudaGetErrorString(e));
+  return MS_OK;
+}
+
+}  // namespace
+
+struct ms_pool {
+  int device = 0;
+  ms_geom geom{};
+  ms_pool_config cfg{};
+  Geo geo{};
+  long long n_keys = 0;
+  int max_pairs = 0;
+  int max_groups = 0;
+  int sm_count = 148;
+  // arena
+  uint8_t* arena = nullptr;
+  size_t arena_bytes = 0;
+  // table
+  DevTable tab{};
+  std::vector<void*> dev_blocks;
+  // store
+  uint8_t* store_host = nullptr;
+  const uint8_t* store_dev = nullptr;
+  size_t store_bytes = 0;
+  bool store_owned = false, store_registered = false;
+  // routers
+  std::vector<const uint16_t*> w_r, b_r;
+  // scratch
+  float* logits = nullptr;
+  unsigned* ticket = nullptr;
+  int* inds = nullptr;
+  uint16_t* scores = nullptr;
+  float* scores_f = nullptr;
+  int* pair_slot = nullptr;
+  __half* xfrag = nullptr;
+  float* xsum = nullptr;
+  __half* hfrag = nullptr;
+  float* hpart = nullptr;
+  float* ypart = nullptr;
+  unsigned* cnt = nullptr;
+  Groups grp{};
+  int* d_slots = nullptr;
+  int* d_opstatus = nullptr;
+  int* h_pinned = nullptr;   // [MS_MAX_REQ + 1]
+  int* mlp_keys = nullptr;     // sanitised slot keys of ms_expert_mlp
+  bool profile = false;
+  std::vector<cudaEvent_t> prof_ev;   // [n_layers][4]
+};
+
+namespace {
+
+template <typename T>
+int palloc(ms_pool* p, T** out, size_t count) {
+  int rc = dalloc(out, count);
+  if (rc == MS_OK) p->dev_blocks.push_back(*out);
+  return rc;
+}
+
+int check_geom(const ms_geom* g) {
+  if (!g) return fail(MS_E_INVALID, "geom is NULL");
+  if (g->model != MS_MODEL_QWEN3 && g->model != MS_MODEL_GPTOSS)
+    return fail(MS_E_INVALID, "unknown model %d", g->model);
+  if (g->bits != 4 || g->group_size != 64)
+    return fail(MS_E_INVALID, "only 4-bit codes in groups of 64 are supported (got %d bits, group %d)",
+                g->bits, g->group_size);
+  if (g->d_model <= 0 || g->d_model % 64 || g->d_ff <= 0 || g->d_ff % 64)
+    return fail(MS_E_INVALID, "d_model and d_ff must be positive multiples of 64");
+  if (g->d_ff > 4096 || g->d_model > 16384)
+    return fail(MS_E_INVALID, "d_ff must be <= 4096 and d_model <= 16384");
+  if (g->n_experts <= 0 || g->n_experts > 256)
+    return fail(MS_E_INVALID, "n_experts must be in [1, 256]");
+  if (g->top_k <= 0 || g->top_k > 32 || g->top_k > g->n_experts)
+    return fail(MS_E_INVALID, "top_k must be in [1, min(32, n_experts)]");
+  if (g->n_layers <= 0) return fail(MS_E_INVALID, "n_layers must be positive");
+  if (g->blob_bytes <= 0 || g->blob_bytes % 16384)
+    return fail(MS_E_INVALID, "blob_bytes must be a positive multiple of 16384");
+  for (int pr = 0; pr < 3; ++pr) {
+    const int n_out = pr == 2 ? g->d_model : g->d_ff;
+    const int n_in = pr == 2 ? g->d_ff : g->d_model;
+    const long long sz[4] = {(long long)n_out * n_in / 2, (long long)n_out * (n_in / 64) * 2,
+                             (long long)n_out * (n_in / 64) * 2, (long long)n_out * 2};
+    for (int pt = 0; pt < 4; ++pt) {
+      const long long off = g->comp_offset[pr][pt];
+      if (pt == 3 && !g->proj_bias) continue;
+      if (off < 0 || off + sz[pt] > g->blob_bytes)
+        return fail(MS_E_INVALID, "component [%d][%d] at %lld (+%lld) lies outside the blob",
+                    pr, pt, off, sz[pt]);
+      if (off % 16) return fail(MS_E_INVALID, "component [%d][%d] is not 16-byte aligned", pr, pt);
+    }
+  }
+  return MS_OK;
+}
+
+Geo make_geo(const ms_geom& g) {
+  Geo o{};
+  o.model = g.model;
+  o.d_model = g.d_model;
+  o.d_ff = g.d_ff;
+  o.n_experts = g.n_experts;
+  o.top_k = g.top_k;
+  o.group_size = g.group_size;
+  o.norm_topk = g.norm_topk_prob;
+  o.proj_bias = g.proj_bias;
+  o.blob = g.blob_bytes;
+  for (int a = 0; a < 3; ++a)
+    for (int b = 0; b < 4; ++b) o.off[a][b] = g.comp_offset[a][b];
+  return o;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int ms_last_error(char* buf, size_t n) {
+  if (!buf || n == 0) return MS_E_INVALID;
+  snprintf(buf, n, "%s", g_err.c_str());
+  return MS_OK;
+}
+
+int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, ms_pool** out) {
+  if (!out) return fail(MS_E_INVALID, "out is NULL");
+  *out = nullptr;
+  int rc = check_geom(geom);
+  if (rc) return rc;
+  if (!cfg) return fail(MS_E_INVALID, "cfg is NULL");
+  if (cfg->n_slots <= 0 || cfg->n_slots > 262144)
+    return fail(MS_E_INVALID, "n_slots must be in [1, 262144]");
+  if (cfg->evict < 0 || cfg->evict > 2) return fail(MS_E_INVALID, "unknown evict mode %d", cfg->evict);
+  if (cfg->n_depths < 0 || cfg->n_depths > MS_MAX_DEPTHS)
+    return fail(MS_E_INVALID, "n_depths must be in [0, %d]", MS_MAX_DEPTHS);
+  for (int i = 0; i < cfg->n_depths; ++i)
+    if (cfg->depths[i] <= 0) return fail(MS_E_INVALID, "prefetch depths must be positive");
+  if (cfg->pf_widen <= 0) return fail(MS_E_INVALID, "pf_widen must be positive");
+  if ((long long)geom->top_k * cfg->pf_widen > geom->n_experts && cfg->n_depths > 0) {
+    // engine_v3.py:513 clamps to n_experts
+  }
+  if (cfg->max_tokens <= 0) return fail(MS_E_INVALID, "max_tokens must be positive");
+
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(MS_E_INVALID, "device %d out of range", device);
+  CK(cudaSetDevice(device));
+
+  ms_pool* p = new ms_pool();
+  p->device = device;
+  p->geom = *geom;
+  p->cfg = *cfg;
+  p->geo = make_geo(*geom);
+  p->n_keys = (long long)geom->n_layers * geom->n_experts;
+  p->max_pairs = cfg->max_tokens * geom->top_k;
+  p->max_groups = std::min(p->max_pairs, geom->n_experts);
+  cudaDeviceGetAttribute(&p->sm_count, cudaDevAttrMultiProcessorCount, device);
+  p->w_r.assign(geom->n_layers, nullptr);
+  p->b_r.assign(geom->n_layers, nullptr);
+
+  auto bail = [&](int code) {
+    ms_pool_destroy(p);
+    return code;
+  };
+
+  // arena: n_slots blobs, slot s at s*blob (16 KiB aligned: cudaMalloc is 256 B
+  // aligned and blob is a multiple of 16 KiB, so every component keeps its
+  // store alignment)
+  p->arena_bytes = (size_t)cfg->n_slots * (size_t)geom->blob_bytes;
+  if ((rc = palloc(p, &p->arena, p->arena_bytes))) return bail(rc);
+  if (cudaMemset(p->arena, 0, p->arena_bytes) != cudaSuccess)
+    return bail(fail(MS_E_CUDA, "arena memset failed"));
+
+  // slot table
+  DevTable& t = p->tab;
+  t.n_slots = cfg->n_slots;
+  t.n_keys = (int)p->n_keys;
+  t.n_experts = geom->n_experts;
+  t.evict = cfg->evict;
+  t.window = 24 * std::max(1, cfg->n_depths > 0 ? cfg->depths[0] : 1);
+  const int kp = std::min(geom->top_k * cfg->pf_widen, geom->n_experts);
+  t.max_fills = geom->n_experts * (1 + cfg->n_depths) + 1;
+  if ((rc = palloc(p, &t.key_of, t.n_slots))) return bail(rc);
+  if ((rc = palloc(p, &t.slot_of, t.n_keys))) return bail(rc);
+  if ((rc = palloc(p, &t.freq, t.n_keys))) return bail(rc);
+  if ((rc = palloc(p, &t.born, t.n_keys))) return bail(rc);
+  if ((rc = palloc(p, &t.last_use, t.n_keys))) return bail(rc);
+  if ((rc = palloc(p, &t.kflags, t.n_keys))) return bail(rc);
+  if ((rc = palloc(p, &t.pinned, t.n_slots))) return bail(rc);
+  if ((rc = palloc(p, &t.pin_list, t.n_slots))) return bail(rc);
+  if ((rc = palloc(p, &t.pend_list, t.n_slots))) return bail(rc);
+  if ((rc = palloc(p, &t.fills, t.max_fills))) return bail(rc);
+  if ((rc = palloc(p, &t.ctr, 1))) return bail(rc);
+  CK(cudaMemset(t.key_of, 0xff, sizeof(int) * t.n_slots));
+  CK(cudaMemset(t.slot_of, 0xff, sizeof(int) * t.n_keys));
+  CK(cudaMemset(t.freq, 0, sizeof(int) * t.n_keys));
+  CK(cudaMemset(t.born, 0, sizeof(long long) * t.n_keys));
+  CK(cudaMemset(t.last_use, 0, sizeof(long long) * t.n_keys));
+  CK(cudaMemset(t.kflags, 0, t.n_keys));
+  CK(cudaMemset(t.pinned, 0, t.n_slots));
+  TableCtr c0{};
+  c0.n_free = t.n_slots;
+  CK(cudaMemcpy(t.ctr, &c0, sizeof(c0), cudaMemcpyHostToDevice));
+
+  // scratch for up to max_tokens
+  const long long T = cfg->max_tokens, P = p->max_pairs;
+  const int E = geom->n_experts, D = geom->d_model, F = geom->d_ff;
+  if ((rc = palloc(p, &p->logits, T * E * (1 + cfg->n_depths)))) return bail(rc);
+  if ((rc = palloc(p, &p->ticket, 1))) return bail(rc);
+  CK(cudaMemset(p->ticket, 0, sizeof(unsigned)));
+  if ((rc = palloc(p, &p->inds, P))) return bail(rc);
+  if ((rc = palloc(p, &p->scores, P))) return bail(rc);
+  if ((rc = palloc(p, &p->scores_f, P))) return bail(rc);
+  if ((rc = palloc(p, &p->pair_slot, P))) return bail(rc);
+  if ((rc = palloc(p, &p->xfrag, T * D))) return bail(rc);
+  if ((rc = palloc(p, &p->xsum, T * (D / 64) * 2))) return bail(rc);
+  if ((rc = palloc(p, &p->hfrag, P * F))) return bail(rc);
+  if ((rc = palloc(p, &p->hpart, P * (F / 16) * 2))) return bail(rc);
+  if ((rc = palloc(p, &p->ypart, P * D))) return bail(rc);
+  if ((rc = palloc(p, &p->cnt, D / 16))) return bail(rc);
+  CK(cudaMemset(p->cnt, 0, sizeof(unsigned) * (D / 16)));
+  const long long key_range = std::max<long long>(E, cfg->n_slots + 1);
+  if ((rc = palloc(p, &p->mlp_keys, std::min<long long>(P, MS_MLP_MAX_PAIRS)))) return bail(rc);
+  if ((rc = palloc(p, &p->grp.n_groups, 1))) return bail(rc);
+  if ((rc = palloc(p, &p->grp.grp_key, std::max<long long>(P, E)))) return bail(rc);
+  if ((rc = palloc(p, &p->grp.grp_slot, std::max<long long>(P, E)))) return bail(rc);
+  if ((rc = palloc(p, &p->grp.grp_start, std::max<long long>(P, E)))) return bail(rc);
+  if ((rc = palloc(p, &p->grp.grp_count, std::max<long long>(P, E)))) return bail(rc);
+  if ((rc = palloc(p, &p->grp.grp_pairs, P))) return bail(rc);
+  if ((rc = palloc(p, &p->grp.map, key_range))) return bail(rc);
+  CK(cudaMemset(p->grp.n_groups, 0, sizeof(int)));
+  if ((rc = palloc(p, &p->d_slots, MS_MAX_REQ))) return bail(rc);
+  if ((rc = palloc(p, &p->d_opstatus, 1))) return bail(rc);
+  if (cudaMallocHost(reinterpret_cast<void**>(&p->h_pinned), sizeof(int) * (MS_MAX_REQ + 1)) !=
+      cudaSuccess)
+    return bail(fail(MS_E_NOMEM, "cudaMallocHost failed"));
+  (void)kp;
+  CK(cudaDeviceSynchronize());
+  *out = p;
+  return MS_OK;
+}
+
+int ms_pool_destroy(ms_pool* p) {
+  if (!p) return MS_OK;
+  cudaSetDevice(p->device);
+  cudaDeviceSynchronize();
+  for (void* b : p->dev_blocks) cudaFree(b);
+  for (cudaEvent_t e : p->prof_ev) cudaEventDestroy(e);
+  if (p->h_pinned) cudaFreeHost(p->h_pinned);
+  if (p->store_owned && p->store_host) cudaFreeHost(p->store_host);
+  if (p->store_registered && p->store_host) cudaHostUnregister(p->store_host);
+  delete p;
+  return MS_OK;
+}
+
+int ms_store_register(ms_pool* p, void* host, size_t bytes) {
+  if (!p || !host) return fail(MS_E_INVALID, "NULL argument");
+  const size_t need = (size_t)p->n_keys * (size_t)p->geom.blob_bytes;
+  if (bytes < (size_t)p->geom.blob_bytes)
+    return fail(MS_E_INVALID, "store of %zu bytes is smaller than one blob", bytes);
+  (void)need;
+  CK(cudaSetDevice(p->device));
+  if (p->store_host) return fail(MS_E_STATE, "a store is already attached");
+  cudaPointerAttributes attr{};
+  void* dptr = nullptr;
+  if (cudaPointerGetAttributes(&attr, host) == cudaSuccess && attr.type == cudaMemoryTypeHost &&
+      attr.devicePointer) {
+    dptr = attr.devicePointer;
+  } else {
+    cudaGetLastError();
+    CK(cudaHostRegister(host, bytes, cudaHostRegisterMapped | cudaHostRegisterPortable));
+    CK(cudaHostGetDevicePointer(&dptr, host, 0));
+    p->store_registered = true;
+  }
+  p->store_host = static_cast<uint8_t*>(host);
+  p->store_dev = static_cast<const uint8_t*>(dptr);
+  p->store_bytes = bytes;
+  return MS_OK;
+}
+
+int ms_store_alloc(ms_pool* p, size_t bytes, void** host_out) {
+  if (!p || !host_out) return fail(MS_E_INVALID, "NULL argument");
+  if (p->store_host) return fail(MS_E_STATE, "a store is already attached");
+  CK(cudaSetDevice(p->device));
+  void* h = nullptr;
+  cudaError_t e = cudaHostAlloc(&h, bytes, cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e != cudaSuccess) return fail(MS_E_NOMEM, "cudaHostAlloc(%zu): %s", bytes, cudaGetErrorString(e));
+  void* d = nullptr;
+  CK(cudaHostGetDevicePointer(&d, h, 0));
+  p->store_host = static_cast<uint8_t*>(h);
+  p->store_dev = static_cast<const uint8_t*>(d);
+  p->store_bytes = bytes;
+  p->store_owned = true;
+  *host_out = h;
+  return MS_OK;
+}
+
+int ms_set_router(ms_pool* p, int layer, const void* w_r, const void* b_r) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (layer < 0 || layer >= p->geom.n_layers) return fail(MS_E_INVALID, "layer %d out of range", layer);
+  if (w_r && !aligned16(w_r)) return fail(MS_E_INVALID, "router weights must be 16-byte aligned");
+  p->w_r[layer] = static_cast<const uint16_t*>(w_r);
+  p->b_r[layer] = static_cast<const uint16_t*>(b_r);
+  return MS_OK;
+}
+
+static FillArgs fill_args(ms_pool* p) {
+  FillArgs f{};
+  f.store = p->store_dev;
+  f.arena = p->arena;
+  f.blob = p->geom.blob_bytes;
+  f.store_keys = (long long)(p->store_bytes / (size_t)p->geom.blob_bytes);
+  f.fills = p->tab.fills;
+  f.max_fills = p->tab.max_fills;
+  f.ctr = p->tab.ctr;
+  return f;
+}
+
+static int pool_op(ms_pool* p, int op, int layer, const int32_t* experts, int n, cudaStream_t s) {
+  if (layer < 0 || layer >= p->geom.n_layers) return fail(MS_E_INVALID, "layer %d out of range", layer);
+  if (n < 0 || n > MS_MAX_REQ) return fail(MS_E_INVALID, "n=%d: at most %d experts per call", n, MS_MAX_REQ);
+  if (n > 0 && !experts) return fail(MS_E_INVALID, "experts is NULL");
+  if (!p->store_dev) return fail(MS_E_STATE, "no store attached (ms_store_register / ms_store_alloc)");
+  PoolReq r{};
+  r.op = op;
+  r.layer = layer;
+  r.n = n;
+  for (int i = 0; i < n; ++i) {
+    if (experts[i] < 0 || experts[i] >= p->geom.n_experts)
+      return fail(MS_E_INVALID, "expert %d out of range", experts[i]);
+    r.experts[i] = experts[i];
+  }
+  CK(cudaSetDevice(p->device));
+  CK(launch_pool_op(p->tab, r, p->d_slots, p->d_opstatus, s));
+  CK(launch_fill(fill_args(p), p->sm_count * 2, s));
+  return MS_OK;
+}
+
+int ms_pool_prefetch(ms_pool* p, int layer, const int32_t* experts, int n, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  return pool_op(p, 0, layer, experts, n, static_cast<cudaStream_t>(stream));
+}
+
+int ms_pool_acquire(ms_pool* p, int layer, const int32_t* experts, int n, int32_t* slots_out,
+                    void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (n > 0 && !slots_out) return fail(MS_E_INVALID, "slots_out is NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = pool_op(p, 1, layer, experts, n, s);
+  if (rc) return rc;
+  if (n > 0) CK(cudaMemcpyAsync(p->h_pinned, p->d_slots, sizeof(int) * n, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(p->h_pinned + MS_MAX_REQ, p->d_opstatus, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if (p->h_pinned[MS_MAX_REQ] == MS_E_EXHAUSTED)
+    return fail(MS_E_EXHAUSTED, "pool exhausted: every slot pinned or pending");
+  for (int i = 0; i < n; ++i) slots_out[i] = p->h_pinned[i];
+  return MS_OK;
+}
+
+int ms_pool_read(ms_pool* p, int slot, int layer, int expert, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (slot < 0 || slot >= p->cfg.n_slots) return fail(MS_E_INVALID, "slot %d out of range", slot);
+  if (layer < 0 || layer >= p->geom.n_layers || expert < 0 || expert >= p->geom.n_experts)
+    return fail(MS_E_INVALID, "(layer %d, expert %d) out of range", layer, expert);
+  if (!p->store_host) return fail(MS_E_STATE, "no store attached");
+  const size_t blob = (size_t)p->geom.blob_bytes;
+  const size_t off = ((size_t)layer * p->geom.n_experts + expert) * blob;
+  if (off + blob > p->store_bytes)
+    return fail(MS_E_IO, "short read: blob (%d, %d) lies past the end of the store", layer, expert);
+  CK(cudaSetDevice(p->device));
+  CK(cudaMemcpyAsync(p->arena + (size_t)slot * blob, p->store_host + off, blob,
+                     cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream)));
+  return MS_OK;
+}
+
+int ms_pool_stats(ms_pool* p, ms_stats* out) {
+  if (!p || !out) return fail(MS_E_INVALID, "NULL argument");
+  CK(cudaSetDevice(p->device));
+  CK(cudaDeviceSynchronize());
+  TableCtr c{};
+  CK(cudaMemcpy(&c, p->tab.ctr, sizeof(c), cudaMemcpyDeviceToHost));
+  out->prefetch = c.st[ST_PREFETCH];
+  out->cache = c.st[ST_CACHE];
+  out->miss = c.st[ST_MISS];
+  out->total = out->prefetch + out->cache + out->miss;
+  out->bail = c.st[ST_BAIL];
+  out->issued = c.st[ST_ISSUED];
+  out->reads = c.st[ST_READS];
+  out->exposed = c.st[ST_EXPOSED];
+  out->bytes_read = c.st[ST_READS] * p->geom.blob_bytes;
+  out->bytes_exposed = c.st[ST_EXPOSED] * p->geom.blob_bytes;
+  return MS_OK;
+}
+
+int ms_pool_slot_table(ms_pool* p, int32_t* out) {
+  if (!p || !out) return fail(MS_E_INVALID, "NULL argument");
+  CK(cudaSetDevice(p->device));
+  CK(cudaDeviceSynchronize());
+  CK(cudaMemcpy(out, p->tab.key_of, sizeof(int) * p->cfg.n_slots, cudaMemcpyDeviceToHost));
+  return MS_OK;
+}
+
+int ms_pool_component_ptr(ms_pool* p, int proj, int part, void** out) {
+  if (!p || !out) return fail(MS_E_INVALID, "NULL argument");
+  if (proj < 0 || proj > 2 || part < 0 || part > 3) return fail(MS_E_INVALID, "bad component");
+  const long long off = p->geom.comp_offset[proj][part];
+  if (off < 0 || (part == 3 && !p->geom.proj_bias)) return fail(MS_E_INVALID, "component absent");
+  *out = p->arena + off;
+  return MS_OK;
+}
+
+int ms_pool_arena(ms_pool* p, void** base, size_t* bytes) {
+  if (!p || !base || !bytes) return fail(MS_E_INVALID, "NULL argument");
+  *base = p->arena;
+  *bytes = p->arena_bytes;
+  return MS_OK;
+}
+
+static int route_common(ms_pool* p, int layer, const void* x, int T, cudaStream_t s, bool block,
+                        int32_t* inds_out, void* scores_out, int32_t* pred_out) {
+  if (layer < 0 || layer >= p->geom.n_layers) return fail(MS_E_INVALID, "layer %d out of range", layer);
+  if (T <= 0 || T > p->cfg.max_tokens)
+    return fail(MS_E_INVALID, "T=%d outside [1, max_tokens=%d]", T, p->cfg.max_tokens);
+  if (!x || !aligned16(x)) return fail(MS_E_INVALID, "x must be a 16-byte aligned device pointer");
+  if (!p->w_r[layer]) return fail(MS_E_STATE, "no router set for layer %d", layer);
+  RouteArgs a{};
+  a.geo = p->geo;
+  a.x = static_cast<const uint16_t*>(x);
+  a.T = T;
+  a.w_r = p->w_r[layer];
+  a.b_r = p->b_r[layer];
+  a.n_pred = 0;
+  for (int i = 0; i < p->cfg.n_depths; ++i) {
+    if (!block && (i > 0 || !pred_out)) break;
+    const int tgt = layer + p->cfg.depths[i];
+    // targets past the last layer are skipped (engine_v3.py:511-512)
+    if (tgt >= p->geom.n_layers) continue;
+    if (!p->w_r[tgt]) return fail(MS_E_STATE, "no router set for prefetch target layer %d", tgt);
+    a.w_p[a.n_pred] = p->w_r[tgt];
+    a.b_p[a.n_pred] = p->b_r[tgt];
+    a.pred_layer[a.n_pred] = tgt;
+    a.n_pred++;
+  }
+  if (!block && pred_out && a.n_pred == 0)
+    return fail(MS_E_INVALID, "layer %d has no prefetch target", layer);
+  a.kp = std::min(p->geom.top_k * p->cfg.pf_widen, p->geom.n_experts);
+  a.logits = p->logits;
+  a.ticket = p->ticket;
+  a.inds = inds_out ? inds_out : p->inds;
+  a.scores = scores_out ? static_cast<uint16_t*>(scores_out) : p->scores;
+  a.scores_f = p->scores_f;
+  a.pred_out = pred_out;
+  a.xfrag = block ? p->xfrag : nullptr;
+  a.xsum = p->xsum;
+  a.do_pool = block ? 1 : 0;
+  a.tab = p->tab;
+  a.layer = layer;
+  a.do_groups = block ? 1 : 0;
+  a.grp = p->grp;
+  a.pair_slot = block ? p->pair_slot : nullptr;
+  const int rows = p->geom.n_experts * (1 + a.n_pred);
+  int grid = (rows + 7) / 8;
+  const int xt = block ? (T * (p->geom.d_model / 64) + 255) / 256 : 0;
+  grid = std::max(grid, xt);
+  grid = std::min(grid, p->sm_count * 4);
+  CK(cudaSetDevice(p->device));
+  CK(launch_route_step(a, grid, s));
+  return MS_OK;
+}
+
+int ms_route(ms_pool* p, int layer, const void* x, int T, int32_t* inds, void* scores,
+             int32_t* pred, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (!inds || !scores) return fail(MS_E_INVALID, "inds/scores are NULL");
+  if (pred && p->cfg.n_depths == 0) return fail(MS_E_INVALID, "pred requested but no prefetch depth configured");
+  return route_common(p, layer, x, T, static_cast<cudaStream_t>(stream), false, inds, scores, pred);
+}
+
+static ExpArgs exp_args(ms_pool* p, const void* x, int T, void* y, const float* scores) {
+  (void)x;
+  ExpArgs e{};
+  e.geo = p->geo;
+  e.arena = p->arena;
+  e.grp = p->grp;
+  e.T = T;
+  e.xfrag = p->xfrag;
+  e.xsum = p->xsum;
+  e.hfrag = p->hfrag;
+  e.hpart = p->hpart;
+  e.ypart = p->ypart;
+  e.scores = scores;
+  e.cnt = p->cnt;
+  e.y = static_cast<uint16_t*>(y);
+  return e;
+}
+
+int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (!y || !aligned16(y)) return fail(MS_E_INVALID, "y must be a 16-byte aligned device pointer");
+  if (!p->store_dev) return fail(MS_E_STATE, "no store attached (ms_store_register / ms_store_alloc)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaEvent_t* ev = (p->profile && layer >= 0 && layer < p->geom.n_layers)
+                        ? &p->prof_ev[(size_t)layer * 4] : nullptr;
+  if (ev) CK(cudaEventRecord(ev[0], s));
+  int rc = route_common(p, layer, x, T, s, true, nullptr, nullptr, nullptr);
+  if (rc) return rc;
+  if (ev) CK(cudaEventRecord(ev[1], s));
+  CK(launch_fill(fill_args(p), p->sm_count * 2, s));
+  if (ev) CK(cudaEventRecord(ev[2], s));
+  const int max_groups = std::min(T * p->geom.top_k, p->geom.n_experts);
+  CK(launch_expert(exp_args(p, x, T, y, p->scores_f), max_groups, s));
+  if (ev) CK(cudaEventRecord(ev[3], s));
+  return MS_OK;
+}
+
+int ms_pool_status(ms_pool* p, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaSetDevice(p->device));
+  CK(cudaStreamSynchronize(s));
+  int st = 0;
+  CK(cudaMemcpy(&st, &p->tab.ctr->status, sizeof(int), cudaMemcpyDeviceToHost));
+  int zero = 0;
+  CK(cudaMemcpy(&p->tab.ctr->status, &zero, sizeof(int), cudaMemcpyHostToDevice));
+  if (st == MS_E_EXHAUSTED) return fail(st, "pool exhausted: every slot pinned or pending");
+  if (st) return fail(st, "device-side error %d in an earlier block call", st);
+  return MS_OK;
+}
+
+int ms_expert_mlp(ms_pool* p, const int32_t* slots, const float* scores, const void* x, int T,
+                  int k, void* y, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (!slots || !scores || !x || !y) return fail(MS_E_INVALID, "NULL argument");
+  if (k != p->geom.top_k) return fail(MS_E_INVALID, "k=%d must equal top_k=%d", k, p->geom.top_k);
+  if (T <= 0 || T > p->cfg.max_tokens || T * k > MS_MLP_MAX_PAIRS)
+    return fail(MS_E_INVALID, "T=%d outside [1, min(max_tokens, %d/k)]", T, MS_MLP_MAX_PAIRS);
+  if (!aligned16(x) || !aligned16(y)) return fail(MS_E_INVALID, "x and y must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaSetDevice(p->device));
+  MlpPrepArgs a{};
+  a.x = static_cast<const uint16_t*>(x);
+  a.T = T;
+  a.k = k;
+  a.d_model = p->geom.d_model;
+  a.n_slots = p->cfg.n_slots;
+  a.slots = slots;
+  a.keys = p->mlp_keys;
+  a.ctr = p->tab.ctr;
+  a.xfrag = p->xfrag;
+  a.xsum = p->xsum;
+  a.grp = p->grp;
+  CK(launch_mlp_prep(a, s));
+  CK(launch_expert(exp_args(p, x, T, y, scores), std::min(T * k, p->cfg.n_slots), s));
+  return MS_OK;
+}
+
+int ms_pool_profile(ms_pool* p, int enable) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  CK(cudaSetDevice(p->device));
+  if (enable && p->prof_ev.empty()) {
+    p->prof_ev.resize((size_t)p->geom.n_layers * 4, nullptr);
+    for (auto& e : p->prof_ev) CK(cudaEventCreate(&e));
+  }
+  p->profile = enable != 0;
+  return MS_OK;
+}
+
+int ms_pool_timing(ms_pool* p, int layer, float* out3) {
+  if (!p || !out3) return fail(MS_E_INVALID, "NULL argument");
+  if (p->prof_ev.empty()) return fail(MS_E_STATE, "profiling was never enabled");
+  if (layer < 0 || layer >= p->geom.n_layers) return fail(MS_E_INVALID, "layer out of range");
+  cudaEvent_t* ev = &p->prof_ev[(size_t)layer * 4];
+  CK(cudaEventSynchronize(ev[3]));
+  for (int i = 0; i < 3; ++i) CK(cudaEventElapsedTime(&out3[i], ev[i], ev[i + 1]));
+  return MS_OK;
+}
+
+int ms_block_debug(ms_pool* p, const int32_t** inds, const void** scores, const int32_t** slots) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (inds) *inds = p->inds;
+  if (scores) *scores = p->scores;
+  if (slots) *slots = p->pair_slot;
+  return MS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,99 @@
+// Tensor-core dequant-dot for 4-bit affine weights (mma.sync m16n8k16, f16
+// inputs, f32 accumulate).
+//
+// A (weights) never goes through a dequantised copy. A 32-bit word holds the
+// codes q0..q7 of 8 consecutive inputs of one row (low nibble first,
+// kernels.py:137-139). One LOP3 per register ORs two nibbles into the
+// mantissas of an f16x2 whose exponent is that of 1024:
+//   R0 = (u & 0x000F000F) | 0x64006400 -> {1024 + q0,    1024 + q4}
+//   R1 = (u & 0x00F000F0) | 0x64006400 -> {1024 + 16*q1, 1024 + 16*q5}
+//   R2 = R0 of (u >> 8)                -> {1024 + q2,    1024 + q6}
+//   R3 = R1 of (u >> 8)                -> {1024 + 16*q3, 1024 + 16*q7}
+// The activation operand is stored pre-divided by 16 at the odd positions,
+// so an MMA over a 64-input quantisation group g gives
+//   acc_g = 1024 * X'_g + sum_k q_k x_k,     X'_g = sum_k x'_k,
+// and the row output is sum_g s_g * (acc_g - 1024 X'_g) + b_g * X_g with
+// X_g = sum_k x_k -- the scale/bias factoring of kernels.py:104-112, applied
+// once per group instead of once per weight.
+//
+// Activation layout ("frag" layout, f16): per (row of activations r, group
+// kg) 64 halves = 128 B, ordered [p][c][8] where word w = 2c + p of the
+// group and the 8 halves are the B-operand registers {MMA1.b0, MMA1.b1,
+// MMA2.b0, MMA2.b1} of lane c: element i of word w lands at half index
+// ((i & 3) << 1) | (i >> 2), divided by 16 when i is odd. Per (r, kg) two
+// floats X_g, X'_g are kept beside it.
+#pragma once
+#include "ms_common.cuh"
+
+namespace ms {
+
+__device__ __forceinline__ uint32_t lop_or(uint32_t u, uint32_t mask) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(u), "r"(mask), "r"(0x64006400u));
+  return r;
+}
+
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One quantisation group of a 16-row tile: words ra (row g) and rb (row g+8)
+// of this lane (uint2 = words 2c and 2c+1 of the group), activation
+// fragments b0 (p = 0) and b1 (p = 1). Accumulates into c[4].
+__device__ __forceinline__ void mma_group(float* c, uint2 ra, uint2 rb, uint4 b0, uint4 b1) {
+  const uint32_t M0 = 0x000F000Fu, M1 = 0x00F000F0u;
+  {
+    const uint32_t u = ra.x, v = rb.x, us = u >> 8, vs = v >> 8;
+    mma16816(c, lop_or(u, M0), lop_or(v, M0), lop_or(u, M1), lop_or(v, M1), b0.x, b0.y);
+    mma16816(c, lop_or(us, M0), lop_or(vs, M0), lop_or(us, M1), lop_or(vs, M1), b0.z, b0.w);
+  }
+  {
+    const uint32_t u = ra.y, v = rb.y, us = u >> 8, vs = v >> 8;
+    mma16816(c, lop_or(u, M0), lop_or(v, M0), lop_or(u, M1), lop_or(v, M1), b1.x, b1.y);
+    mma16816(c, lop_or(us, M0), lop_or(vs, M0), lop_or(us, M1), lop_or(vs, M1), b1.z, b1.w);
+  }
+}
+
+// Offset (in halves) of input element k of activation row r in frag layout.
+__device__ __forceinline__ long long frag_off(long long r, int G, int k) {
+  const int kg = k >> 6, w = (k >> 3) & 7, i = k & 7;
+  const int p = w & 1, cc = w >> 1, hidx = ((i & 3) << 1) | (i >> 2);
+  return ((r * G + kg) * 2 + p) * 32 + cc * 8 + hidx;
+}
+
+// Write activation row group (r, kg) in frag layout from 64 bf16 values.
+// One thread per (r, kg).
+__device__ __forceinline__ void frag_write_group(const uint16_t* src64, __half* frag, float* sums,
+                                                 long long r, int G, int kg) {
+  __half vals[64];
+  float xs = 0.f, xp = 0.f;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src64);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint4 v = s4[q];
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint16_t b = (uint16_t)((w4[e >> 1] >> ((e & 1) * 16)) & 0xffffu);
+      const int k = q * 8 + e;                       // element within the group
+      const __half h = __float2half_rn(bf2f(b));
+      const __half hs = (k & 1) ? __hmul(h, __float2half(0.0625f)) : h;
+      xs += __half2float(h);
+      xp += __half2float(hs);
+      const int w = k >> 3, i = k & 7;
+      vals[((w & 1) * 4 + (w >> 1)) * 8 + (((i & 3) << 1) | (i >> 2))] = hs;
+    }
+  }
+  uint4* dst = reinterpret_cast<uint4*>(frag + (r * G + kg) * 64);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) dst[q] = reinterpret_cast<const uint4*>(vals)[q];
+  sums[(r * G + kg) * 2] = xs;
+  sums[(r * G + kg) * 2 + 1] = xp;
+}
+
+}  // namespace ms

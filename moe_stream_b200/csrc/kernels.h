@@ -1,0 +1,91 @@
+// Kernel argument structures and launchers (host <-> device boundary inside
+// libmoestream; not part of the public C ABI).
+#pragma once
+#include "ms_common.cuh"
+
+#ifndef MS_MAX_DEPTHS
+#define MS_MAX_DEPTHS 4
+#endif
+#define MS_MAX_REQ 256
+#define MS_MLP_MAX_PAIRS 2048
+
+namespace ms {
+
+struct RouteArgs {
+  Geo geo;
+  const uint16_t* x;          // bf16 [T, d_model]
+  int T;
+  const uint16_t* w_r;        // bf16 [E, d_model]
+  const uint16_t* b_r;        // bf16 [E] or null
+  int n_pred;                 // prefetch targets (0..MS_MAX_DEPTHS)
+  const uint16_t* w_p[MS_MAX_DEPTHS];
+  const uint16_t* b_p[MS_MAX_DEPTHS];
+  int pred_layer[MS_MAX_DEPTHS];   // -1: past the last layer, no prefetch
+  int kp;                     // top_k * pf_widen
+  float* logits;              // [T, E*(1+n_pred)]
+  unsigned* ticket;
+  int* inds;                  // [T, k]
+  uint16_t* scores;           // [T, k] bf16
+  float* scores_f;            // [T, k]
+  int* pred_out;              // [T, kp] (depth 0) or null
+  __half* xfrag;              // frag layout of x, or null
+  float* xsum;
+  int do_pool;
+  DevTable tab;
+  int layer;
+  int do_groups;
+  Groups grp;
+  int* pair_slot;             // [T, k] or null
+};
+
+struct PoolReq {
+  int op;                     // 0 prefetch, 1 acquire
+  int layer;
+  int n;
+  int experts[MS_MAX_REQ];
+};
+
+struct FillArgs {
+  const uint8_t* store;       // device-mapped pinned host store
+  uint8_t* arena;
+  long long blob;
+  long long store_keys;       // blobs present in the store
+  const int2* fills;
+  int max_fills;
+  TableCtr* ctr;
+};
+
+struct MlpPrepArgs {
+  const uint16_t* x;
+  int T, k, d_model, n_slots;
+  const int* slots;           // [T, k]
+  int* keys;                  // [T, k] scratch: slot, or n_slots when invalid
+  TableCtr* ctr;              // status sink for invalid slots
+  __half* xfrag;
+  float* xsum;
+  Groups grp;
+};
+
+struct ExpArgs {
+  Geo geo;
+  const uint8_t* arena;
+  Groups grp;
+  int T;
+  const __half* xfrag;        // [T][d_model/64][64]
+  const float* xsum;          // [T][d_model/64][2]
+  __half* hfrag;              // [P][d_ff/64][64]
+  float* hpart;               // [P][d_ff/16][2]
+  float* ypart;               // [P][d_model]
+  const float* scores;        // [P]
+  unsigned* cnt;              // [d_model/16]
+  uint16_t* y;                // bf16 [T, d_model]
+};
+
+cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s);
+cudaError_t launch_pool_op(const DevTable& t, const PoolReq& r, int* slots_out, int* st,
+                           cudaStream_t s);
+cudaError_t launch_fill(const FillArgs& f, int grid, cudaStream_t s);
+cudaError_t launch_mlp_prep(const MlpPrepArgs& a, cudaStream_t s);
+cudaError_t launch_expert(const ExpArgs& a, int max_groups, cudaStream_t s);
+
+}  // namespace ms

@@ -1,0 +1,89 @@
+// Shared device-side structures of libmoestream (sm_100a).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#define MS_FULL 0xffffffffu
+
+namespace ms {
+
+// ------------------------------------------------------------ slot table
+// Per-key flags (key = layer * n_experts + expert).
+constexpr uint8_t KF_PENDING = 1;   // ExpertPool.pending   (engine_v3.py:219)
+constexpr uint8_t KF_FROMPF = 2;    // ExpertPool.from_prefetch (:220)
+
+constexpr int EVICT_LFU = 0, EVICT_LRU = 1, EVICT_ASIS = 2;
+constexpr int SAMPLE = 24;                    // engine_v3.py:322
+constexpr long long STRIDE = 7919;            // engine_v3.py:336
+constexpr long long YOUNG = 1LL << 30;        // engine_v3.py:349
+
+// stats slots (ms_stats order minus totals)
+enum { ST_PREFETCH = 0, ST_CACHE, ST_MISS, ST_BAIL, ST_ISSUED, ST_READS, ST_EXPOSED, ST_N };
+
+// Mutable scalars of the table, resident in device memory.
+struct TableCtr {
+  long long clock;       // allocation counter (engine_v3.py:222)
+  long long use_clock;   // access counter (:225)
+  int n_free;            // free list is [0, n_free): pop() takes n_free-1 (:218, 325)
+  int n_pend;            // pend_list length
+  int n_pin;             // pin_list length
+  int n_fill;            // fills produced by the current call
+  int status;            // sticky error code (0 / negative MS_E_*)
+  int pad;
+  long long st[ST_N];
+};
+
+struct DevTable {
+  int n_slots, n_keys, n_experts, evict, window;
+  int* key_of;           // [n_slots]  key or -1   (engine_v3.py:216)
+  int* slot_of;          // [n_keys]   slot or -1  (:215)
+  int* freq;             // [n_keys]               (:217)
+  long long* born;       // [n_keys]               (:223)
+  long long* last_use;   // [n_keys]               (:224)
+  uint8_t* kflags;       // [n_keys]   KF_*
+  uint8_t* pinned;       // [n_slots]              (:221)
+  int* pin_list;         // [n_slots]  slots with pinned=1
+  int* pend_list;        // [n_slots]  keys that went pending, in issue order
+  int2* fills;           // [max_fills] (slot, key) to copy store -> arena
+  int max_fills;
+  TableCtr* ctr;
+};
+
+// ---------------------------------------------------------------- groups
+// Token/expert pairs p = t*k + j grouped by the slot they read. Groups are
+// ordered by ascending key (expert id on the routed path, slot id on the
+// ms_expert_mlp path); pairs inside a group by ascending p.
+struct Groups {
+  int* n_groups;         // [1]
+  int* grp_key;          // [max_groups]
+  int* grp_slot;         // [max_groups]  -1 when the pool could not place it
+  int* grp_start;        // [max_groups]
+  int* grp_count;        // [max_groups]
+  int* grp_pairs;        // [max_pairs]
+  int* map;              // [key_range] scratch: key -> group
+};
+
+// Geometry as the kernels need it.
+struct Geo {
+  int model;             // 0 qwen3, 1 gpt-oss
+  int d_model, d_ff, n_experts, top_k, group_size;
+  int norm_topk, proj_bias;
+  long long blob;
+  long long off[3][4];
+};
+
+__device__ __forceinline__ float bf2f(uint16_t b) {
+  return __uint_as_float(((uint32_t)b) << 16);
+}
+// round-to-nearest-even float -> bf16 bits (finite inputs)
+__device__ __forceinline__ uint16_t f2bf(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7f800000u) == 0x7f800000u) return (uint16_t)((u >> 16) | ((u & 0xffff) ? 0x40 : 0));
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+__device__ __forceinline__ float bfr(float f) { return bf2f(f2bf(f)); }
+
+}  // namespace ms

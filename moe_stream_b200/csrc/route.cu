@@ -1,0 +1,343 @@
+// K1: router + slot-table step, one launch per MoE block call.
+//
+// Phase 1 (every CTA): router logits x . W_r^T (+ bias) for this layer and
+// for each prefetch target layer (engine_v3.py:507-514), one warp per router
+// row, fp32 accumulation; and the frag-layout copy of x that the expert
+// kernels read.
+// Phase 2 (the last CTA to finish phase 1, picked by an arrival counter; no
+// CTA ever waits on another): per-token softmax / top-k in the reference's
+// bf16 rounding order, the sorted unions of routed and predicted experts,
+// the device slot-table step (prefetch each target layer, then acquire this
+// layer's experts, engine_v3.py:522-548) and the grouping of token/expert
+// pairs by slot for the expert kernels.
+#include "ms_common.cuh"
+#include "pool_table.cuh"
+#include "groups.cuh"
+#include "frag.cuh"
+#include "kernels.h"
+
+namespace ms {
+
+constexpr int MAX_E = 256;
+constexpr int RT_THREADS = 256;
+
+__device__ __forceinline__ uint32_t mono_key(uint16_t b) {
+  // order-preserving map of bf16 bits to unsigned
+  return (b & 0x8000u) ? (uint32_t)(~b & 0xffffu) : (uint32_t)(b | 0x8000u);
+}
+
+// top-k of vals[0..E) (bf16 bit patterns, one warp): descending, exact
+// ties to the lower index. Writes indices to out[0..k).
+__device__ void warp_topk(const uint16_t* vals, int E, int k, int* out, int lane) {
+  // candidates held by this lane: e = lane + 32*i
+  unsigned taken = 0;
+  for (int r = 0; r < k; ++r) {
+    unsigned long long best = 0;
+    for (int i = 0; lane + 32 * i < E; ++i) {
+      if (taken & (1u << i)) continue;
+      const int e = lane + 32 * i;
+      const unsigned long long key =
+          ((unsigned long long)mono_key(vals[e]) << 16) | (unsigned long long)(0xffff - e);
+      if (key > best) best = key;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const unsigned long long v = __shfl_xor_sync(MS_FULL, best, o);
+      if (v > best) best = v;
+    }
+    const int e = 0xffff - (int)(best & 0xffff);
+    if ((e & 31) == lane) taken |= 1u << (e >> 5);
+    if (lane == 0) out[r] = e;
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
+  const int E = A.geo.n_experts, d = A.geo.d_model, T = A.T, k = A.geo.top_k;
+  const int rows = E * (1 + A.n_pred);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps_total = gridDim.x * (RT_THREADS / 32);
+  const int gw = blockIdx.x * (RT_THREADS / 32) + warp;
+  const int nchunk = d / 8;  // 16-byte chunks of a row
+
+  // ---------------------------------------------------------------- phase 1
+  for (int r = gw; r < rows; r += nwarps_total) {
+    const int which = r / E, e = r % E;
+    const uint16_t* w = (which == 0 ? A.w_r : A.w_p[which - 1]) + (long long)e * d;
+    const uint16_t* b = (which == 0 ? A.b_r : A.b_p[which - 1]);
+    const float bias = b ? bf2f(b[e]) : 0.f;
+    for (int t = 0; t < T; ++t) {
+      const uint16_t* x = A.x + (long long)t * d;
+      float acc = 0.f;
+      for (int ch = lane; ch < nchunk; ch += 32) {
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w) + ch);
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x) + ch);
+        const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w};
+        const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc = fmaf(__uint_as_float(wa[q] << 16), __uint_as_float(xa[q] << 16), acc);
+          acc = fmaf(__uint_as_float(wa[q] & 0xffff0000u), __uint_as_float(xa[q] & 0xffff0000u), acc);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(MS_FULL, acc, o);
+      if (lane == 0) A.logits[(long long)t * rows + r] = acc + bias;
+    }
+  }
+  if (A.xfrag) {
+    const int G = d / 64;
+    const int tasks = T * G;
+    for (int i = blockIdx.x * RT_THREADS + threadIdx.x; i < tasks; i += gridDim.x * RT_THREADS) {
+      const int t = i / G, kg = i % G;
+      frag_write_group(A.x + (long long)t * d + kg * 64, A.xfrag, A.xsum, t, G, kg);
+    }
+  }
+
+  // ----------------------------------------------------- arrival: last CTA
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(A.ticket, 1u);
+    s_last = (prev == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  // ---------------------------------------------------------------- phase 2
+  __shared__ unsigned s_acq_mask[MAX_E / 32];
+  __shared__ unsigned s_pred_mask[MS_MAX_DEPTHS][MAX_E / 32];
+  __shared__ uint16_t s_vals[RT_THREADS / 32][MAX_E];
+  __shared__ int s_sel[RT_THREADS / 32][MAX_E];
+  __shared__ int s_acq[MAX_E];
+  __shared__ int s_pred[MS_MAX_DEPTHS][MAX_E];
+  __shared__ int s_n_pred[MS_MAX_DEPTHS];
+  __shared__ int s_slots[MAX_E];
+  __shared__ int s_waits[MAX_E];
+  __shared__ int s_cnt[MAX_E], s_run[MAX_E];
+  __shared__ int s_n_acq;
+  __shared__ OpCtx s_op;
+
+  for (int i = threadIdx.x; i < MAX_E / 32; i += RT_THREADS) {
+    s_acq_mask[i] = 0;
+    for (int dd = 0; dd < MS_MAX_DEPTHS; ++dd) s_pred_mask[dd][i] = 0;
+  }
+  __syncthreads();
+
+  const int kp = A.kp;
+  for (int t = warp; t < T; t += RT_THREADS / 32) {
+    const float* lg = A.logits + (long long)t * rows;
+    uint16_t* vals = s_vals[warp];
+    int* sel = s_sel[warp];
+    // logits rounded to bf16 as the Linear's output (engine_v3.py:468)
+    float lmax = -INFINITY;
+    for (int e = lane; e < E; e += 32) {
+      const uint16_t b = f2bf(lg[e]);
+      vals[e] = b;
+      lmax = fmaxf(lmax, bf2f(b));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(MS_FULL, lmax, o));
+    __syncwarp();
+    if (A.geo.model == 0) {
+      // softmax(precise) over all experts, bf16 out (engine_v3.py:468)
+      float s = 0.f;
+      for (int e = lane; e < E; e += 32) s += expf(bf2f(vals[e]) - lmax);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(MS_FULL, s, o);
+      __syncwarp();
+      for (int e = lane; e < E; e += 32) vals[e] = f2bf(expf(bf2f(vals[e]) - lmax) / s);
+      __syncwarp();
+      warp_topk(vals, E, k, sel, lane);
+      if (lane == 0) {
+        float p[32];
+        float ssum = 0.f;
+        for (int j = 0; j < k; ++j) { p[j] = bf2f(vals[sel[j]]); ssum += p[j]; }
+        const float den = bfr(ssum);
+        for (int j = 0; j < k; ++j) {
+          const float sc = A.geo.norm_topk ? bfr(p[j] / den) : p[j];
+          A.inds[t * k + j] = sel[j];
+          A.scores[t * k + j] = f2bf(sc);
+          A.scores_f[t * k + j] = sc;
+          atomicOr(&s_acq_mask[sel[j] >> 5], 1u << (sel[j] & 31));
+        }
+      }
+    } else {
+      // gpt-oss: top-k of the logits, softmax over the k (engine_120b.py:67-70)
+      warp_topk(vals, E, k, sel, lane);
+      if (lane == 0) {
+        float m = -INFINITY;
+        for (int j = 0; j < k; ++j) m = fmaxf(m, bf2f(vals[sel[j]]));
+        float ex[32], s = 0.f;
+        for (int j = 0; j < k; ++j) { ex[j] = expf(bf2f(vals[sel[j]]) - m); s += ex[j]; }
+        for (int j = 0; j < k; ++j) {
+          const float sc = bfr(ex[j] / s);
+          A.inds[t * k + j] = sel[j];
+          A.scores[t * k + j] = f2bf(sc);
+          A.scores_f[t * k + j] = sc;
+          atomicOr(&s_acq_mask[sel[j] >> 5], 1u << (sel[j] & 31));
+        }
+      }
+    }
+    __syncwarp();
+    // speculation: top-(k*widen) of the target layer's raw logits
+    // (engine_v3.py:476-483, 509-514)
+    for (int dd = 0; dd < A.n_pred; ++dd) {
+      for (int e = lane; e < E; e += 32) vals[e] = f2bf(lg[(dd + 1) * E + e]);
+      __syncwarp();
+      warp_topk(vals, E, kp, sel, lane);
+      if (lane == 0) {
+        for (int j = 0; j < kp; ++j) {
+          atomicOr(&s_pred_mask[dd][sel[j] >> 5], 1u << (sel[j] & 31));
+          if (dd == 0 && A.pred_out) A.pred_out[t * kp + j] = sel[j];
+        }
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    const int n_acq = warp_mask_to_list(s_acq_mask, (E + 31) / 32, s_acq, lane);
+    if (lane == 0) s_n_acq = n_acq;
+    for (int dd = 0; dd < A.n_pred; ++dd) {
+      const int n = warp_mask_to_list(s_pred_mask[dd], (E + 31) / 32, s_pred[dd], lane);
+      if (lane == 0) s_n_pred[dd] = n;
+    }
+    __syncwarp();
+    if (A.do_pool) {
+      const DevTable& Tb = A.tab;
+      op_load(Tb, &s_op, lane);
+      // ExpertPool.prefetch for each target layer, then acquire
+      // (engine_v3.py:522-526, 548); np.unique sorts both lists.
+      for (int dd = 0; dd < A.n_pred; ++dd)
+        if (A.pred_layer[dd] >= 0)
+          warp_prefetch(Tb, &s_op, A.pred_layer[dd], s_pred[dd], s_n_pred[dd], lane);
+      if (lane == 0)
+        for (int i = 0; i < n_acq; ++i) s_slots[i] = -1;
+      __syncwarp();
+      warp_acquire(Tb, &s_op, A.layer, s_acq, n_acq, s_slots, s_waits, lane);
+      op_store(Tb, &s_op, lane);
+    } else if (lane == 0) {
+      for (int i = 0; i < n_acq; ++i) s_slots[i] = -1;
+    }
+  }
+  __syncthreads();
+
+  if (A.do_groups) {
+    cta_build_groups(A.inds, T * k, s_acq, s_n_acq, A.grp, s_cnt, s_run,
+                     [&](int g) { return s_slots[g]; });
+    if (A.pair_slot)
+      for (int p = threadIdx.x; p < T * k; p += RT_THREADS)
+        A.pair_slot[p] = s_slots[A.grp.map[A.inds[p]]];
+  }
+  if (threadIdx.x == 0) *A.ticket = 0u;
+}
+
+// Host API table operation (ExpertPool.prefetch / .acquire called directly):
+// one warp, the request passed by value.
+__global__ void k_pool_op(DevTable Tb, PoolReq R, int* slots_out, int* op_status) {
+  __shared__ OpCtx s_op;
+  __shared__ int s_exp[MS_MAX_REQ];
+  __shared__ int s_slots[MS_MAX_REQ];
+  __shared__ int s_waits[MS_MAX_REQ];
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x >= 32) return;
+  for (int i = lane; i < R.n; i += 32) s_exp[i] = R.experts[i];
+  __syncwarp();
+  op_load(Tb, &s_op, lane);
+  int st = 0;
+  if (R.op == 0) {
+    warp_prefetch(Tb, &s_op, R.layer, s_exp, R.n, lane);
+  } else {
+    if (lane == 0)
+      for (int i = 0; i < R.n; ++i) s_slots[i] = -1;
+    __syncwarp();
+    st = warp_acquire(Tb, &s_op, R.layer, s_exp, R.n, s_slots, s_waits, lane);
+    for (int i = lane; i < R.n; i += 32) slots_out[i] = s_slots[i];
+  }
+  op_store(Tb, &s_op, lane);
+  if (lane == 0) *op_status = st;
+}
+
+// Store -> arena copy of the fills the last table step produced. The store
+// is mapped pinned host memory read directly by the SMs, so the fill list
+// never has to travel to the host.
+__global__ void __launch_bounds__(256) k_fill(FillArgs F) {
+  const int n = min(F.ctr->n_fill, F.max_fills);
+  const long long chunks = F.blob / 16384;
+  const long long total = (long long)n * chunks;
+  for (long long i = blockIdx.x; i < total; i += gridDim.x) {
+    const int2 f = F.fills[i / chunks];
+    const long long part = i % chunks;
+    if (f.y < 0 || (long long)f.y >= F.store_keys) {
+      if (threadIdx.x == 0) atomicCAS(&F.ctr->status, 0, -7);
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(F.store + (long long)f.y * F.blob + part * 16384);
+    uint4* dst = reinterpret_cast<uint4*>(F.arena + (long long)f.x * F.blob + part * 16384);
+    uint4 v[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = src[threadIdx.x + q * 256];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[threadIdx.x + q * 256] = v[q];
+  }
+}
+
+// ms_expert_mlp preparation: frag layout of x and groups keyed by slot.
+__global__ void __launch_bounds__(RT_THREADS) k_mlp_prep(MlpPrepArgs A) {
+  __shared__ int s_uniq[MS_MLP_MAX_PAIRS];
+  __shared__ int s_cnt[MS_MLP_MAX_PAIRS], s_run[MS_MLP_MAX_PAIRS];
+  extern __shared__ unsigned s_mask[];
+  const int G = A.d_model / 64;
+  for (int i = threadIdx.x; i < A.T * G; i += RT_THREADS)
+    frag_write_group(A.x + (long long)(i / G) * A.d_model + (i % G) * 64, A.xfrag, A.xsum, i / G, G, i % G);
+  // key n_slots collects out-of-range slots: its group reads nothing and
+  // yields zeros, and the pool status records MS_E_INVALID
+  const int nw = (A.n_slots + 1 + 31) / 32;
+  for (int i = threadIdx.x; i < nw; i += RT_THREADS) s_mask[i] = 0;
+  __syncthreads();
+  const int P = A.T * A.k;
+  for (int p = threadIdx.x; p < P; p += RT_THREADS) {
+    int s = A.slots[p];
+    if (s < 0 || s >= A.n_slots) {
+      s = A.n_slots;
+      atomicCAS(&A.ctr->status, 0, -1);
+    }
+    A.keys[p] = s;
+    atomicOr(&s_mask[s >> 5], 1u << (s & 31));
+  }
+  __syncthreads();
+  __shared__ int s_n;
+  if (threadIdx.x < 32) {
+    const int n = warp_mask_to_list(s_mask, nw, s_uniq, threadIdx.x);
+    if (threadIdx.x == 0) s_n = n;
+  }
+  __syncthreads();
+  cta_build_groups(A.keys, P, s_uniq, s_n, A.grp, s_cnt, s_run,
+                   [&](int g) { return s_uniq[g] < A.n_slots ? s_uniq[g] : -1; });
+}
+
+// ----------------------------------------------------------------- launchers
+cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s) {
+  k_route_step<<<grid, RT_THREADS, 0, s>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_pool_op(const DevTable& t, const PoolReq& r, int* slots_out, int* st,
+                           cudaStream_t s) {
+  k_pool_op<<<1, 32, 0, s>>>(t, r, slots_out, st);
+  return cudaGetLastError();
+}
+cudaError_t launch_fill(const FillArgs& f, int grid, cudaStream_t s) {
+  k_fill<<<grid, 256, 0, s>>>(f);
+  return cudaGetLastError();
+}
+cudaError_t launch_mlp_prep(const MlpPrepArgs& a, cudaStream_t s) {
+  const size_t smem = ((a.n_slots + 1 + 31) / 32) * sizeof(unsigned);
+  k_mlp_prep<<<1, RT_THREADS, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace ms

@@ -1,0 +1,231 @@
+"""ExpertPool: the reference's slot pool (engine_v3.py:125-464) on B200.
+
+Same public surface -- ``prefetch(layer, experts)``, ``acquire(layer,
+experts) -> [slot]``, ``stats()``, ``views[name]``, ``_read(slot, layer,
+expert)``, ``key_of``, ``slot_of``, ``n_slots``, ``blob``, ``group_size``,
+``bits``, ``n_layers``, ``n_experts``, ``top_k`` -- over a different
+machine:
+
+* the slots are one contiguous HBM arena (slot s at s*blob_bytes, laid out as
+  a store blob), not one MLX array per component; offsets are 64-bit, which
+  removes by construction the int32 wrap the reference fixed at
+  engine_v3.py:144-167;
+* the store is pinned, device-mapped host memory; fills are copies issued on
+  the GPU (the SMs read the mapped store), so no host thread and no host
+  round trip sit between a table decision and its fill;
+* the LFU table (freq / born / last_use / pending / from_prefetch / pinned,
+  clocks and counters) lives in device memory and is updated by one warp per
+  call, in exactly the reference's order.
+
+Everything here is a thin ctypes wrapper over libmoestream.so; there is no
+Python or CPU implementation of any of it.
+"""
+import ctypes
+import json
+import os
+
+import numpy as np
+import torch
+
+from . import _lib
+from .geometry import PROJS, PARTS, Geometry, from_index
+
+
+def _stream_ptr(stream):
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+class _DevArray:
+    """__cuda_array_interface__ over arena memory, so torch can view it."""
+
+    def __init__(self, ptr, shape, typestr, strides):
+        self.__cuda_array_interface__ = dict(shape=tuple(shape), typestr=typestr,
+                                             data=(ptr, False), strides=tuple(strides),
+                                             version=3)
+
+
+_TYPESTR = {"U32": ("<u4", torch.int32, 4), "BF16": ("<u2", torch.bfloat16, 2)}
+
+
+class ExpertPool:
+    """Fixed HBM pool of expert slots with device-side LFU residency."""
+
+    def __init__(self, geom: Geometry, n_slots, evict="lfu", depths=(1,), pf_widen=1,
+                 max_tokens=16, device=None, store=None):
+        self._lib = _lib.load()
+        if device is None:
+            device = torch.cuda.current_device()
+        self.device = int(device)
+        self.geom = geom
+        self.blob = geom.blob_bytes
+        self.n_experts = geom.n_experts
+        self.n_layers = geom.n_layers
+        self.top_k = geom.top_k
+        self.group_size = geom.group_size
+        self.bits = geom.bits
+        self.n_slots = int(n_slots)
+        self.payload = geom.payload_bytes
+        self.pad = self.blob - self.payload
+        self.evict = evict
+        self.depths = tuple(depths)
+        self.pf_widen = pf_widen
+        self.max_tokens = max_tokens
+        # stream ordering replaces the reference's per-layer barrier
+        # (engine_v3.py:228-231, 601-607): a slot is refilled only after the
+        # kernels that read it, so no barrier is ever needed
+        self.needs_barrier = False
+        cfg = _lib.MsPoolConfig()
+        cfg.n_slots = self.n_slots
+        cfg.evict = _lib.EVICT[evict]
+        cfg.n_depths = len(self.depths)
+        for i, d in enumerate(self.depths):
+            cfg.depths[i] = d
+        cfg.pf_widen = pf_widen
+        cfg.max_tokens = max_tokens
+        self._geom_c = geom.to_c()
+        h = ctypes.c_void_p()
+        _lib.check(self._lib.ms_pool_create(ctypes.byref(self._geom_c), ctypes.byref(cfg),
+                                            self.device, ctypes.byref(h)))
+        self._h = h
+        base, size = ctypes.c_void_p(), ctypes.c_size_t()
+        _lib.check(self._lib.ms_pool_arena(h, ctypes.byref(base), ctypes.byref(size)))
+        self.arena_ptr, self.pool_bytes = base.value, size.value
+        self.views = self._make_views()
+        self.store = None
+        if store is not None:
+            self.attach_store(store)
+
+    # ------------------------------------------------------------- store
+    def alloc_store(self, n_blobs=None):
+        """Pinned, device-mapped host store for n_blobs blobs (default: every
+        (layer, expert)); returns it as a numpy uint8 array to be filled."""
+        n_blobs = self.geom.n_keys if n_blobs is None else n_blobs
+        nbytes = n_blobs * self.blob
+        p = ctypes.c_void_p()
+        _lib.check(self._lib.ms_store_alloc(self._h, nbytes, ctypes.byref(p)))
+        buf = (ctypes.c_uint8 * nbytes).from_address(p.value)
+        self.store = np.frombuffer(buf, dtype=np.uint8)
+        return self.store
+
+    def attach_store(self, arr):
+        """Register an existing host array (numpy uint8) as the store."""
+        arr = np.ascontiguousarray(arr, dtype=np.uint8)
+        _lib.check(self._lib.ms_store_register(self._h, ctypes.c_void_p(arr.ctypes.data), arr.nbytes))
+        self.store = arr
+        return arr
+
+    @classmethod
+    def open(cls, model_dir, model, d_model, d_ff, n_slots, **kw):
+        """Pool over an on-disk store (experts_index.json + experts.bin,
+        repack.py:137-146): the whole file is read once into pinned memory."""
+        idx = json.load(open(os.path.join(model_dir, "experts_index.json")))
+        geom = from_index(idx, model, d_model, d_ff)
+        pool = cls(geom, n_slots, **kw)
+        path = os.path.join(model_dir, "experts.bin")
+        size = os.path.getsize(path)
+        n_blobs = size // geom.blob_bytes
+        store = pool.alloc_store(n_blobs)
+        fd = os.open(path, os.O_RDONLY)
+        try:
+            mv = memoryview(store)
+            off, step = 0, 1 << 28
+            while off < n_blobs * geom.blob_bytes:
+                got = os.preadv(fd, [mv[off:off + step]], off)
+                if got <= 0:
+                    raise IOError(f"short read at {off} of {path}")
+                off += got
+        finally:
+            os.close(fd)
+        return pool
+
+    # ------------------------------------------------------------- views
+    def _make_views(self):
+        views = {}
+        for proj_i, proj in enumerate(PROJS):
+            for part_i, part in enumerate(PARTS):
+                try:
+                    c = self.geom.comp(proj, part)
+                except KeyError:
+                    continue
+                typestr, tdt, isz = _TYPESTR[c["dtype"]]
+                shape = [self.n_slots, *c["shape"]]
+                inner = []
+                acc = isz
+                for s in reversed(c["shape"]):
+                    inner.insert(0, acc)
+                    acc *= s
+                strides = [self.blob, *inner]
+                arr = _DevArray(self.arena_ptr + c["offset"], shape, typestr, strides)
+                t = torch.as_tensor(arr, device=f"cuda:{self.device}")
+                views[f"{proj}.{part}"] = t.view(tdt) if tdt == torch.bfloat16 else t.view(torch.int32)
+        return views
+
+    # ------------------------------------------------------- reference API
+    def prefetch(self, layer, experts, stream=None):
+        """Non-blocking (engine_v3.py:383-396)."""
+        e = np.ascontiguousarray(np.asarray(experts, dtype=np.int32).reshape(-1))
+        _lib.check(self._lib.ms_pool_prefetch(
+            self._h, int(layer), e.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), e.size,
+            _stream_ptr(stream)))
+
+    def acquire(self, layer, experts, stream=None):
+        """Blocking: the slot of each expert (engine_v3.py:398-454). Raises
+        PoolExhausted (a RuntimeError) like the reference."""
+        e = np.ascontiguousarray(np.asarray(experts, dtype=np.int32).reshape(-1))
+        out = np.empty(e.size, dtype=np.int32)
+        _lib.check(self._lib.ms_pool_acquire(
+            self._h, int(layer), e.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), e.size,
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), _stream_ptr(stream)))
+        return [int(s) for s in out]
+
+    def _read(self, slot, layer, expert, stream=None):
+        """Copy blob (layer, expert) into slot, bypassing the table
+        (engine_v3.py:255-290)."""
+        _lib.check(self._lib.ms_pool_read(self._h, int(slot), int(layer), int(expert),
+                                          _stream_ptr(stream)))
+
+    def stats(self):
+        """engine_v3.py:456-464; blocked/busy_s/depth are host timings of the
+        reference's I/O threads and have no counterpart (reported as 0)."""
+        s = _lib.MsStats()
+        _lib.check(self._lib.ms_pool_stats(self._h, ctypes.byref(s)))
+        return dict(total=s.total, prefetch=s.prefetch, cache=s.cache, miss=s.miss,
+                    blocked=0.0, gb=s.bytes_read / 2 ** 30, busy_s=0.0, depth=0.0,
+                    bail=s.bail, issued=s.issued, exposed_gb=s.bytes_exposed / 2 ** 30,
+                    reads=s.reads)
+
+    def table(self):
+        """Slot -> key (layer*n_experts+expert, -1 empty) as an int32 array."""
+        out = np.empty(self.n_slots, dtype=np.int32)
+        _lib.check(self._lib.ms_pool_slot_table(self._h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
+        return out
+
+    @property
+    def key_of(self):
+        """engine_v3.py:216: (layer, expert) per slot, None when empty."""
+        return [None if k < 0 else (int(k) // self.n_experts, int(k) % self.n_experts)
+                for k in self.table()]
+
+    @property
+    def slot_of(self):
+        """engine_v3.py:215: {(layer, expert): slot}."""
+        return {(int(k) // self.n_experts, int(k) % self.n_experts): s
+                for s, k in enumerate(self.table()) if k >= 0}
+
+    def status(self, stream=None):
+        """Raise the first device-side error of earlier asynchronous calls."""
+        _lib.check(self._lib.ms_pool_status(self._h, _stream_ptr(stream)))
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self.views = {}
+            self._lib.ms_pool_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

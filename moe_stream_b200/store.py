@@ -1,0 +1,172 @@
+"""Synthetic expert stores in the reference's blob format.
+
+There are no checkpoints here, so stores are generated from seeded normal
+weights (N(0, 0.02), the configs' distribution) and quantised with MLX's
+affine scheme (group 64, 4 bits, bf16 scales/biases). The quantiser runs in
+torch so that it can run on the GPU for multi-GB stores; tests check it
+bit-exactly against the numpy oracle's restatement.
+
+Random streams: blob (layer, expert) uses its own torch Generator seeded
+with ``seed * 1_000_003 + layer * 1009 + expert``, so any subset of blobs can
+be regenerated independently and identically on the CPU and on the GPU
+(torch's CPU and CUDA generators differ, so the device is part of the
+recipe: ``device`` below).
+"""
+import numpy as np
+import torch
+
+from .geometry import PROJS
+
+
+def quantize(w, group_size=64, bits=4):
+    """MLX affine quantisation of w [..., K] (float32, bf16-valued).
+    Returns (packed uint32 as int32 tensor [..., K/8], scales bf16, biases bf16)."""
+    w = w.to(torch.float32)
+    shp = w.shape
+    K = shp[-1]
+    n_bins = torch.tensor(float((1 << bits) - 1), dtype=torch.float32, device=w.device)
+    eps = torch.tensor(1e-7, dtype=torch.float32, device=w.device)
+    g = w.reshape(-1, K // group_size, group_size)
+    w_max = g.amax(dim=-1, keepdim=True)
+    w_min = g.amin(dim=-1, keepdim=True)
+    mask = w_min.abs() > w_max.abs()
+    scales = torch.maximum((w_max - w_min) / n_bins, eps)
+    scales = torch.where(mask, scales, -scales)
+    edge = torch.where(mask, w_min, w_max)
+    q0 = torch.round(edge / scales)
+    scales = torch.where(q0 != 0, edge / q0, scales)
+    biases = torch.where(q0 == 0, torch.zeros_like(edge), edge)
+    q = torch.clamp(torch.round((g - biases) / scales), 0, float((1 << bits) - 1)).to(torch.int64)
+    per = 32 // bits
+    q = q.reshape(*shp[:-1], K // per, per)
+    shifts = (torch.arange(per, device=w.device, dtype=torch.int64) * bits)
+    packed = (q << shifts).sum(dim=-1)                       # < 2**32
+    packed = (packed - ((packed >> 31) << 32)).to(torch.int32)  # reinterpret as int32
+    sshape = (*shp[:-1], K // group_size)
+    return (packed, scales.reshape(sshape).to(torch.bfloat16),
+            biases.reshape(sshape).to(torch.bfloat16))
+
+
+def _gen(seed, layer, expert, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1_000_003 + layer * 1009 + expert)
+    return g
+
+
+def expert_weights(geom, seed, layer, expert, device="cpu", std=0.02):
+    """bf16-valued float32 weights of one expert: {proj: [out, in]} plus the
+    gpt-oss projection biases {proj + '.bias': [out]}."""
+    gen = _gen(seed, layer, expert, device)
+    out = {}
+    for proj in PROJS:
+        n_out, n_in = (geom.d_model, geom.d_ff) if proj == "down_proj" else (geom.d_ff, geom.d_model)
+        w = torch.randn(n_out, n_in, generator=gen, device=device, dtype=torch.float32) * std
+        out[proj] = w.to(torch.bfloat16).to(torch.float32)
+        if geom.proj_bias:
+            b = torch.randn(n_out, generator=gen, device=device, dtype=torch.float32) * std
+            out[proj + ".bias"] = b.to(torch.bfloat16)
+    return out
+
+
+def pack_blob(geom, weights):
+    """One expert's blob (uint8 tensor [blob_bytes]) from its weights."""
+    dev = next(iter(weights.values())).device
+    blob = torch.zeros(geom.blob_bytes, dtype=torch.uint8, device=dev)
+    for proj in PROJS:
+        q, s, b = quantize(weights[proj], geom.group_size, geom.bits)
+        parts = {"weight": q, "scales": s, "biases": b}
+        if geom.proj_bias:
+            parts["bias"] = weights[proj + ".bias"]
+        for part, t in parts.items():
+            c = geom.comp(proj, part)
+            raw = t.contiguous().view(torch.uint8).reshape(-1)
+            assert raw.numel() == c["nbytes"], (proj, part, raw.numel(), c["nbytes"])
+            blob[c["offset"]:c["offset"] + c["nbytes"]] = raw
+    return blob
+
+
+def make_blob(geom, seed, layer, expert, device="cpu"):
+    return pack_blob(geom, expert_weights(geom, seed, layer, expert, device))
+
+
+def fill_store(geom, host_u8, seed, layers=None, experts=None, device="cpu", batch=16):
+    """Write blobs into a host uint8 array laid out as the store. layers /
+    experts restrict which blobs are generated (others are left as they are)."""
+    layers = range(geom.n_layers) if layers is None else layers
+    experts = range(geom.n_experts) if experts is None else experts
+    view = torch.from_numpy(host_u8) if isinstance(host_u8, np.ndarray) else host_u8
+    for layer in layers:
+        for e in experts:
+            key = layer * geom.n_experts + e
+            blob = make_blob(geom, seed, layer, e, device)
+            view[key * geom.blob_bytes:(key + 1) * geom.blob_bytes].copy_(blob, non_blocking=False)
+
+
+def router_weights(geom, seed, layer, device="cpu", std=0.02, zipf_s=None, bias_std=None):
+    """Router (gate) of one layer: w bf16 [E, d] ~ N(0, std). With zipf_s, a
+    bias log(p_{pi(e)}) with p_r ~ r^-s over a seeded permutation pi (the
+    skewed-routing configs); with bias_std, a N(0, bias_std) bias (gpt-oss
+    routers carry one). Returns (w, b or None) as bf16 tensors."""
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed * 7_000_003 + layer * 131 + 17)
+    w = (torch.randn(geom.n_experts, geom.d_model, generator=g) * std).to(torch.bfloat16)
+    b = None
+    if zipf_s is not None:
+        perm = torch.randperm(geom.n_experts, generator=g)
+        r = torch.arange(1, geom.n_experts + 1, dtype=torch.float64)
+        p = r ** (-zipf_s)
+        p = p / p.sum()
+        b = torch.empty(geom.n_experts, dtype=torch.float64)
+        b[perm] = torch.log(p)
+        b = b.to(torch.bfloat16)
+    elif bias_std is not None:
+        b = (torch.randn(geom.n_experts, generator=g) * bias_std).to(torch.bfloat16)
+    return w.to(device), (None if b is None else b.to(device))
+
+
+def rms_norm_tokens(T, d, seed, device="cpu"):
+    """x ~ N(0,1), RMS-normalised (no weight), bf16 [T, d] (config 0)."""
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed * 3_000_017 + 5)
+    x = torch.randn(T, d, generator=g, dtype=torch.float32)
+    x = x * torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + 1e-6)
+    return x.to(torch.bfloat16).to(device)
+
+
+def make_layer_blobs(geom, seed, layer, device="cuda", std=0.02, chunk=32):
+    """All n_experts blobs of one layer at once (uint8 [n_experts, blob_bytes]
+    on `device`), for multi-GB stores. One generator per (seed, layer); a
+    different recipe from make_blob, so the two are not interchangeable."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1_000_003 + layer * 1009 + 977)
+    E = geom.n_experts
+    out = torch.zeros(E, geom.blob_bytes, dtype=torch.uint8, device=device)
+    for e0 in range(0, E, chunk):
+        n = min(chunk, E - e0)
+        for proj in PROJS:
+            n_out, n_in = (geom.d_model, geom.d_ff) if proj == "down_proj" else (geom.d_ff, geom.d_model)
+            w = (torch.randn(n, n_out, n_in, generator=g, device=device) * std)
+            w = w.to(torch.bfloat16).to(torch.float32)
+            q, s, b = quantize(w, geom.group_size, geom.bits)
+            parts = {"weight": q, "scales": s, "biases": b}
+            if geom.proj_bias:
+                parts["bias"] = (torch.randn(n, n_out, generator=g, device=device) * std).to(torch.bfloat16)
+            for part, t in parts.items():
+                c = geom.comp(proj, part)
+                raw = t.contiguous().view(torch.uint8).reshape(n, -1)
+                out[e0:e0 + n, c["offset"]:c["offset"] + c["nbytes"]] = raw
+            del w, q, s, b, parts
+    return out
+
+
+def decode_inputs(n_steps, n_layers, d, seed, step_sigma=0.1):
+    """Config-1 hidden states: per decode step an i.i.d. h_0 ~ N(0,1), then
+    h_{l+1} = h_l + step_sigma * N(0,1); the block input of layer l is
+    RMS-normalised h_l in bf16. Returns bf16 [n_steps, n_layers, d] (CPU)."""
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed * 5_000_011 + 23)
+    h = torch.randn(n_steps, 1, d, generator=g)
+    steps = torch.randn(n_steps, n_layers - 1, d, generator=g) * step_sigma
+    hs = torch.cat([h, h + torch.cumsum(steps, dim=1)], dim=1)
+    x = hs * torch.rsqrt(hs.pow(2).mean(dim=-1, keepdim=True) + 1e-6)
+    return x.to(torch.bfloat16)
