@@ -42,7 +42,44 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-sample-layers", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", choices=["stack", "layer"], default="stack",
+                    help="layer: a 2-layer Qwen3 stack with every expert resident (a small "
+                         "case for ncu section captures); prints per-call timings only")
+    ap.add_argument("--tokens", type=int, default=1)
     return ap.parse_args()
+
+
+def layer_case(args):
+    """Layer 0 of a 2-layer Qwen3 stack, all 256 experts resident (680 MB
+    arena), next-layer prediction on, T tokens per call, repeated block
+    calls. For profiling captures."""
+    import torch
+    from moe_stream_b200 import geometry, store as S
+    from moe_stream_b200.block import MoEBlock
+    from moe_stream_b200.pool import ExpertPool
+    torch.cuda.set_device(0)
+    geom = geometry.qwen3(2)
+    pool = ExpertPool(geom, geom.n_keys, depths=(1,), max_tokens=max(1, args.tokens))
+    st = torch.from_numpy(pool.alloc_store()).view(geom.n_keys, geom.blob_bytes)
+    for layer in range(2):
+        st[layer * 128:(layer + 1) * 128].copy_(S.make_layer_blobs(geom, SEED, layer))
+    blocks = [MoEBlock(pool, l, *S.router_weights(geom, SEED, l, zipf_s=1.1)) for l in range(2)]
+    T = args.tokens
+    n = args.warmup + args.steps
+    x = S.decode_inputs(n * T, 1, geom.d_model, SEED).cuda().reshape(-1, geom.d_model)
+    for i in range(args.warmup):
+        blocks[0](x[i * T:(i + 1) * T])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.warmup, n):
+        blocks[0](x[i * T:(i + 1) * T])
+    e1.record()
+    torch.cuda.synchronize()
+    pool.status()
+    print(json.dumps({"case": "layer", "tokens": T, "calls": args.steps,
+                      "us_per_call": e0.elapsed_time(e1) * 1e3 / args.steps}))
+    pool.close()
 
 
 # ------------------------------------------------------------------ clocks
@@ -354,6 +391,9 @@ def main():
         if int(os.environ.get("RANK", "0")) != 0:
             return
         reference_arm(args)
+        return
+    if args.case == "layer":
+        layer_case(args)
         return
     gpu_arm(args)
 

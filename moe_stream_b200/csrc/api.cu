@@ -176,6 +176,8 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   for (int i = 0; i < cfg->n_depths; ++i)
     if (cfg->depths[i] <= 0) return fail(MS_E_INVALID, "prefetch depths must be positive");
   if (cfg->pf_widen <= 0) return fail(MS_E_INVALID, "pf_widen must be positive");
+  if (geom->n_experts * (1 + cfg->n_depths) > 640)
+    return fail(MS_E_INVALID, "n_experts * (1 + n_depths) must be <= 640");
   if ((long long)geom->top_k * cfg->pf_widen > geom->n_experts && cfg->n_depths > 0) {
     // engine_v3.py:513 clamps to n_experts
   }
@@ -531,6 +533,7 @@ static ExpArgs exp_args(ms_pool* p, const void* x, int T, void* y, const float* 
   e.scores = scores;
   e.cnt = p->cnt;
   e.y = static_cast<uint16_t*>(y);
+  e.status = &p->tab.ctr->status;
   return e;
 }
 
@@ -541,15 +544,23 @@ int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* str
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaEvent_t* ev = (p->profile && layer >= 0 && layer < p->geom.n_layers)
                         ? &p->prof_ev[(size_t)layer * 4] : nullptr;
-  if (ev) CK(cudaEventRecord(ev[0], s));
+  // inside a stream capture an event record must be an external node to be
+  // timeable after replay
+  unsigned rec_flags = cudaEventRecordDefault;
+  if (ev) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    CK(cudaStreamIsCapturing(s, &cs));
+    if (cs == cudaStreamCaptureStatusActive) rec_flags = cudaEventRecordExternal;
+    CK(cudaEventRecordWithFlags(ev[0], s, rec_flags));
+  }
   int rc = route_common(p, layer, x, T, s, true, nullptr, nullptr, nullptr);
   if (rc) return rc;
-  if (ev) CK(cudaEventRecord(ev[1], s));
+  if (ev) CK(cudaEventRecordWithFlags(ev[1], s, rec_flags));
   CK(launch_fill(fill_args(p), p->sm_count * 2, s));
-  if (ev) CK(cudaEventRecord(ev[2], s));
+  if (ev) CK(cudaEventRecordWithFlags(ev[2], s, rec_flags));
   const int max_groups = std::min(T * p->geom.top_k, p->geom.n_experts);
   CK(launch_expert(exp_args(p, x, T, y, p->scores_f), max_groups, s));
-  if (ev) CK(cudaEventRecord(ev[3], s));
+  if (ev) CK(cudaEventRecordWithFlags(ev[3], s, rec_flags));
   return MS_OK;
 }
 

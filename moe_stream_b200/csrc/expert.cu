@@ -1,23 +1,27 @@
-// K3: 4-bit expert MLP for decode and small batches (tokens per expert <= a
-// few dozen): the batched replacement of the three gather_qmm calls, the
-// SwiGLU and the weighted sum (engine_v3.py:588-600, engine_120b.py:130-145;
-// kernels.py:87-186 is the reference's own fused attempt).
+// K3: 4-bit expert MLP for decode and small batches: the batched replacement
+// of the three gather_qmm calls, the SwiGLU and the weighted sum
+// (engine_v3.py:588-600, engine_120b.py:130-145; kernels.py:87-186 is the
+// reference's own fused attempt).
 //
 //   k_up   one CTA per (16-row tile of d_ff, group of pairs sharing a slot):
-//          gate and up rows of the tile for up to 8 tokens per MMA pass,
-//          the input dimension split over the CTA's 8 warps, SwiGLU (or
-//          gpt-oss's clamped SwiGLU with the projection biases) in the
-//          epilogue; h goes out in frag layout, ready to be the next
-//          kernel's MMA operand, with its per-group sums.
-//   k_down one CTA per (16-row tile of d_model, group): down rows, bias,
-//          then the weighted combine over each token's k experts is done
-//          by the last CTA to finish a row tile (arrival counter, fixed j
-//          order, so the sum is deterministic), writing bf16 y.
+//          gate and up rows for up to 8 tokens per MMA pass, the input
+//          dimension split over 8 warps, SwiGLU (or gpt-oss's clamped SwiGLU
+//          with the projection biases) in the epilogue; h leaves in the frag
+//          layout, ready to be k_down's MMA operand, with per-tile sums.
+//   k_down one CTA per (RT row tiles of d_model, group): down rows and bias;
+//          the last CTA to finish a row tile then does the weighted combine
+//          over each token's k experts in a fixed order (deterministic).
 //
-// Weights stream straight from the slot arena with 8-byte non-allocating
-// loads; every lane's 32 bytes of a quantisation group are one sector.
+// Staging: one thread per CTA issues TMA bulk copies (cp.async.bulk) of the
+// tile's weight rows -- each row to a padded shared-memory row, so the MMA
+// fragment reads are bank-conflict free -- and of its scales/biases, all
+// completing on one mbarrier. A CTA therefore has its whole tile (37-60 KB)
+// in flight from its first instructions, whatever its register budget.
+// k_down is launched as a programmatic dependent of k_up: its weights are
+// copied while k_up is still running, and only the h reads wait.
 #include "ms_common.cuh"
 #include "frag.cuh"
+#include "tma.cuh"
 #include "kernels.h"
 
 namespace ms {
@@ -25,45 +29,72 @@ namespace ms {
 constexpr int EX_THREADS = 256;
 constexpr int EX_WARPS = EX_THREADS / 32;
 
-__device__ __forceinline__ uint2 ldw(const uint32_t* p) {
-  uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-  return v;
-}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
+// The activations keep MLX's rounding points: gather_qmm returns bf16, and
+// every elementwise op of the SwiGLU rounds its result to bf16
+// (engine_v3.py:592-597, engine_120b.py:136-143), so the block tracks the
+// reference's arithmetic, not a more precise variant of it.
+__device__ __forceinline__ float sigm(float v) { return 1.f / (1.f + expf(-v)); }
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  // activations.swiglu(gate, x) = silu(gate) * x, silu(v) = v * sigmoid(v)
+  return bfr(bfr(g * bfr(sigm(g))) * u);
+}
 
 __device__ __forceinline__ float clamped_swiglu(float g, float u) {
-  // gpt_oss.swiglu(x_linear=u, x_glu=g): alpha 1.702, limit 7 (engine_120b.py:27-29)
+  // gpt_oss.swiglu(x_linear=u, x_glu=g): alpha 1.702 (a bf16 1.703125 once it
+  // meets a bf16 operand), limit 7, (linear + 1) (engine_120b.py:27-29)
   g = fminf(g, 7.f);
   u = fminf(fmaxf(u, -7.f), 7.f);
-  return g / (1.f + expf(-1.702f * g)) * (u + 1.f);
+  const float og = bfr(g * bfr(sigm(bfr(1.703125f * g))));
+  return bfr(og * bfr(u + 1.f));
 }
 
-// Partial dot products of a 16-row tile over quantisation groups [kg0, kg1)
-// for the 8 activation columns of this pass. Returns the lane's C fragment
-// (rows g4, g4+8 x columns 2c, 2c+1) with scales and biases applied.
-__device__ __forceinline__ void tile_dot(float* tot, const uint32_t* W, const uint16_t* S,
-                                         const uint16_t* B, int WPR, int G, int r0, int r1,
-                                         int kg0, int kg1, const __half* frag, long long rb,
-                                         const float* sums, long long rc0, long long rc1,
-                                         int c) {
-  for (int kg = kg0; kg < kg1; ++kg) {
-    const uint2 a0 = ldw(W + (long long)r0 * WPR + kg * 8 + 2 * c);
-    const uint2 a1 = ldw(W + (long long)r1 * WPR + kg * 8 + 2 * c);
-    uint4 b0 = make_uint4(0, 0, 0, 0), b1 = b0;
-    if (rb >= 0) {
-      const uint4* fb = reinterpret_cast<const uint4*>(frag + (rb * G + kg) * 64);
-      b0 = fb[c];
-      b1 = fb[4 + c];
+// Padded shared-memory row stride for a weight row of `row_bytes`: a stride
+// of 8 (mod 32) words puts the 8 rows a warp reads at once on disjoint bank
+// octets, so the 8-byte fragment loads take the minimum two wavefronts.
+__host__ __device__ __forceinline__ int padded_stride(int row_bytes) {
+  int s = row_bytes;
+  while (((s >> 2) & 31) != 8) s += 16;
+  return s;
+}
+
+// Dot products of a 16-row tile held in shared memory (rows at `stride`
+// bytes) over quantisation groups [kg0, kg1), for the 8 activation columns of
+// this pass. B fragments come from global memory (frag layout), hoisted.
+// Scales/biases: sS/sB [16][G] relative to the tile.
+template <int KPW>
+__device__ __forceinline__ void tile_dot_smem(float* tot, const uint8_t* At, int stride, int G,
+                                              int kg0, int kg1, int g4, int c, const uint16_t* sS,
+                                              const uint16_t* sB, const __half* frag_b,
+                                              const float* sum_c0, const float* sum_c1) {
+  uint4 b0[KPW], b1[KPW];
+#pragma unroll
+  for (int q = 0; q < KPW; ++q) {
+    b0[q] = make_uint4(0, 0, 0, 0);
+    b1[q] = b0[q];
+    const int kg = kg0 + q;
+    if (frag_b && kg < kg1) {
+      const uint4* fb = reinterpret_cast<const uint4*>(frag_b + kg * 64);
+      b0[q] = __ldg(fb + c);
+      b1[q] = __ldg(fb + 4 + c);
     }
+  }
+#pragma unroll
+  for (int q = 0; q < KPW; ++q) {
+    const int kg = kg0 + q;
+    if (kg >= kg1) break;
+    const uint2 ra = *reinterpret_cast<const uint2*>(At + g4 * stride + kg * 32 + 8 * c);
+    const uint2 rb = *reinterpret_cast<const uint2*>(At + (g4 + 8) * stride + kg * 32 + 8 * c);
     float cc[4] = {0.f, 0.f, 0.f, 0.f};
-    mma_group(cc, a0, a1, b0, b1);
+    mma_group(cc, ra, rb, b0[q], b1[q]);
     float xs0 = 0.f, xp0 = 0.f, xs1 = 0.f, xp1 = 0.f;
-    if (rc0 >= 0) { xs0 = sums[(rc0 * G + kg) * 2]; xp0 = sums[(rc0 * G + kg) * 2 + 1]; }
-    if (rc1 >= 0) { xs1 = sums[(rc1 * G + kg) * 2]; xp1 = sums[(rc1 * G + kg) * 2 + 1]; }
-    const float s0 = bf2f(S[(long long)r0 * G + kg]), s1 = bf2f(S[(long long)r1 * G + kg]);
-    const float q0 = bf2f(B[(long long)r0 * G + kg]), q1 = bf2f(B[(long long)r1 * G + kg]);
+    if (sum_c0) { const float2 v = *reinterpret_cast<const float2*>(sum_c0 + kg * 2); xs0 = v.x; xp0 = v.y; }
+    if (sum_c1) { const float2 v = *reinterpret_cast<const float2*>(sum_c1 + kg * 2); xs1 = v.x; xp1 = v.y; }
+    const float s0 = bf2f(sS[g4 * G + kg]), s1 = bf2f(sS[(g4 + 8) * G + kg]);
+    const float q0 = bf2f(sB[g4 * G + kg]), q1 = bf2f(sB[(g4 + 8) * G + kg]);
     tot[0] += s0 * (cc[0] - 1024.f * xp0) + q0 * xs0;
     tot[1] += s0 * (cc[1] - 1024.f * xp1) + q0 * xs1;
     tot[2] += s1 * (cc[2] - 1024.f * xp0) + q1 * xs0;
@@ -71,45 +102,76 @@ __device__ __forceinline__ void tile_dot(float* tot, const uint32_t* W, const ui
   }
 }
 
-template <int MODEL>
+struct UpSmem {
+  static __host__ __device__ int stride(int K) { return padded_stride(K / 2); }
+  static __host__ __device__ int a_bytes(int K) { return 16 * stride(K); }
+  static __host__ __device__ int sb_bytes(int G) { return 16 * G * 2; }
+  static __host__ __device__ int total(int K) {
+    const int G = K / 64;
+    return 2 * a_bytes(K) + 4 * sb_bytes(G) + EX_WARPS * 2 * 4 * 32 * 4 + 16;
+  }
+};
+
+template <int MODEL, int KPW>
 __global__ void __launch_bounds__(EX_THREADS) k_up(ExpArgs A) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  pdl_wait();                                   // slots and groups come from the route step
+  pdl_trigger();
   const int g = blockIdx.y;
   if (g >= *A.grp.n_groups) return;
   const int slot = A.grp.grp_slot[g];
   const int m = A.grp.grp_count[g], start = A.grp.grp_start[g];
   const int rt = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g4 = lane >> 2, c = lane & 3;
-  const int K = A.geo.d_model, G = K / 64, WPR = K / 8, F = A.geo.d_ff, GF = F / 64;
+  const int K = A.geo.d_model, G = K / 64, F = A.geo.d_ff, GF = F / 64;
   const int k = A.geo.top_k;
-  const int kg0 = warp * G / EX_WARPS, kg1 = (warp + 1) * G / EX_WARPS;
-  const int r0 = rt * 16 + g4, r1 = r0 + 8;
-  __shared__ float red[EX_WARPS][2][4][32];
+  const int row_bytes = K / 2, stride = UpSmem::stride(K);
+  const int kg0 = min(G, warp * KPW), kg1 = min(G, kg0 + KPW);
+
+  uint8_t* sA[2] = {smem, smem + UpSmem::a_bytes(K)};
+  uint16_t* sSB = reinterpret_cast<uint16_t*>(smem + 2 * UpSmem::a_bytes(K));
+  const int sbn = 16 * G;                       // elements per staged [16][G] block
+  float* red = reinterpret_cast<float*>(smem + 2 * UpSmem::a_bytes(K) + 4 * UpSmem::sb_bytes(G));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(red + EX_WARPS * 2 * 4 * 32);
 
   const uint8_t* blob = A.arena + (long long)(slot < 0 ? 0 : slot) * A.geo.blob;
-  const uint32_t* Wg = reinterpret_cast<const uint32_t*>(blob + A.geo.off[0][0]);
-  const uint16_t* Sg = reinterpret_cast<const uint16_t*>(blob + A.geo.off[0][1]);
-  const uint16_t* Bg = reinterpret_cast<const uint16_t*>(blob + A.geo.off[0][2]);
-  const uint32_t* Wu = reinterpret_cast<const uint32_t*>(blob + A.geo.off[1][0]);
-  const uint16_t* Su = reinterpret_cast<const uint16_t*>(blob + A.geo.off[1][1]);
-  const uint16_t* Bu = reinterpret_cast<const uint16_t*>(blob + A.geo.off[1][2]);
+  if (threadIdx.x == 0 && slot >= 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+    const unsigned bytes = 2u * 16u * row_bytes + 4u * UpSmem::sb_bytes(G);
+    mbar_expect_tx(bar, bytes);
+    for (int p = 0; p < 2; ++p) {
+      const uint8_t* W = blob + A.geo.off[p][0] + (long long)rt * 16 * row_bytes;
+      for (int r = 0; r < 16; ++r) bulk_g2s(sA[p] + r * stride, W + r * row_bytes, row_bytes, bar);
+      bulk_g2s(sSB + (2 * p) * sbn, blob + A.geo.off[p][1] + (long long)rt * 16 * G * 2,
+               UpSmem::sb_bytes(G), bar);
+      bulk_g2s(sSB + (2 * p + 1) * sbn, blob + A.geo.off[p][2] + (long long)rt * 16 * G * 2,
+               UpSmem::sb_bytes(G), bar);
+    }
+  }
+  __syncthreads();
+  bool ok = true;
+  if (slot >= 0) ok = mbar_wait(bar, 0, A.status);
 
   for (int n0 = 0; n0 < m; n0 += 8) {
     const int* pairs = A.grp.grp_pairs + start + n0;
     const int nn = min(8, m - n0);
-    const long long pb = (g4 < nn) ? pairs[g4] : -1;
-    const long long pc0 = (2 * c < nn) ? pairs[2 * c] : -1;
-    const long long pc1 = (2 * c + 1 < nn) ? pairs[2 * c + 1] : -1;
-    const long long tb = pb >= 0 ? pb / k : -1;
-    const long long tc0 = pc0 >= 0 ? pc0 / k : -1, tc1 = pc1 >= 0 ? pc1 / k : -1;
+    const int pb = (g4 < nn) ? pairs[g4] : -1;
+    const int pc0 = (2 * c < nn) ? pairs[2 * c] : -1;
+    const int pc1 = (2 * c + 1 < nn) ? pairs[2 * c + 1] : -1;
+    const __half* fb = pb >= 0 ? A.xfrag + (long long)(pb / k) * G * 64 : nullptr;
+    const float* s0 = pc0 >= 0 ? A.xsum + (long long)(pc0 / k) * G * 2 : nullptr;
+    const float* s1 = pc1 >= 0 ? A.xsum + (long long)(pc1 / k) * G * 2 : nullptr;
     float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f};
-    if (slot >= 0) {
-      tile_dot(tg, Wg, Sg, Bg, WPR, G, r0, r1, kg0, kg1, A.xfrag, tb, A.xsum, tc0, tc1, c);
-      tile_dot(tu, Wu, Su, Bu, WPR, G, r0, r1, kg0, kg1, A.xfrag, tb, A.xsum, tc0, tc1, c);
+    if (slot >= 0 && ok && kg0 < kg1) {
+      tile_dot_smem<KPW>(tg, sA[0], stride, G, kg0, kg1, g4, c, sSB, sSB + sbn, fb, s0, s1);
+      tile_dot_smem<KPW>(tu, sA[1], stride, G, kg0, kg1, g4, c, sSB + 2 * sbn, sSB + 3 * sbn, fb,
+                         s0, s1);
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      red[warp][0][i][lane] = tg[i];
-      red[warp][1][i][lane] = tu[i];
+      red[((warp * 2 + 0) * 4 + i) * 32 + lane] = tg[i];
+      red[((warp * 2 + 1) * 4 + i) * 32 + lane] = tu[i];
     }
     __syncthreads();
     if (warp == 0) {
@@ -117,16 +179,22 @@ __global__ void __launch_bounds__(EX_THREADS) k_up(ExpArgs A) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         float gv = 0.f, uv = 0.f;
-        for (int w = 0; w < EX_WARPS; ++w) { gv += red[w][0][i][lane]; uv += red[w][1][i][lane]; }
-        const int row = (i < 2) ? r0 : r1;
+#pragma unroll
+        for (int w = 0; w < EX_WARPS; ++w) {
+          gv += red[((w * 2 + 0) * 4 + i) * 32 + lane];
+          uv += red[((w * 2 + 1) * 4 + i) * 32 + lane];
+        }
+        const int row = rt * 16 + g4 + ((i < 2) ? 0 : 8);
         const int col = 2 * c + (i & 1);
-        const long long pc = (i & 1) ? pc1 : pc0;
-        if (col < nn && slot >= 0) {
+        const int pc = (i & 1) ? pc1 : pc0;
+        if (col < nn && slot >= 0 && ok) {
           float h;
+          gv = bfr(gv);                          // gather_qmm outputs are bf16
+          uv = bfr(uv);
           if (MODEL == 1) {
             const uint16_t* bgp = reinterpret_cast<const uint16_t*>(blob + A.geo.off[0][3]);
             const uint16_t* bup = reinterpret_cast<const uint16_t*>(blob + A.geo.off[1][3]);
-            h = clamped_swiglu(gv + bf2f(bgp[row]), uv + bf2f(bup[row]));
+            h = clamped_swiglu(bfr(gv + bf2f(bgp[row])), bfr(uv + bf2f(bup[row])));
           } else {
             h = silu_mul(gv, uv);
           }
@@ -150,139 +218,193 @@ __global__ void __launch_bounds__(EX_THREADS) k_up(ExpArgs A) {
       }
       if (g4 == 0) {
         const int nt = F / 16;
-        if (2 * c < nn) {
-          A.hpart[(pc0 * nt + rt) * 2] = hs[0];
-          A.hpart[(pc0 * nt + rt) * 2 + 1] = hp[0];
-        }
-        if (2 * c + 1 < nn) {
-          A.hpart[(pc1 * nt + rt) * 2] = hs[1];
-          A.hpart[(pc1 * nt + rt) * 2 + 1] = hp[1];
-        }
+        if (2 * c < nn)
+          *reinterpret_cast<float2*>(A.hpart + ((long long)pc0 * nt + rt) * 2) = make_float2(hs[0], hp[0]);
+        if (2 * c + 1 < nn)
+          *reinterpret_cast<float2*>(A.hpart + ((long long)pc1 * nt + rt) * 2) = make_float2(hs[1], hp[1]);
       }
     }
     __syncthreads();
   }
 }
 
-template <int MODEL>
+struct DownSmem {
+  static __host__ __device__ int stride(int F) { return padded_stride(F / 2); }
+  static __host__ __device__ int a_bytes(int F, int RT) { return RT * 16 * stride(F); }
+  static __host__ __device__ int sb_bytes(int GF, int RT) { return RT * 16 * GF * 2; }
+  static __host__ __device__ int total(int F, int RT) {
+    const int GF = F / 64;
+    return a_bytes(F, RT) + 2 * sb_bytes(GF, RT) + EX_WARPS * 4 * 32 * 4 + 8 * GF * 2 * 4 + 16;
+  }
+};
+
+template <int MODEL, int KPW, int RT>
 __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  // the route step finished before k_up started, so the groups and the
+  // filled slots can be read now; only h (k_up's output) needs pdl_wait
   const int g = blockIdx.y;
   const int n_groups = *A.grp.n_groups;
-  if (g >= n_groups) return;
+  if (g >= n_groups) {
+    pdl_wait();
+    return;
+  }
   const int slot = A.grp.grp_slot[g];
   const int m = A.grp.grp_count[g], start = A.grp.grp_start[g];
-  const int rt = blockIdx.x;
+  constexpr int WPT = EX_WARPS / RT;            // warps per row tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g4 = lane >> 2, c = lane & 3;
-  const int K = A.geo.d_ff, G = K / 64, WPR = K / 8, D = A.geo.d_model;
+  const int sub = warp / WPT, wk = warp % WPT;
+  const int rt = blockIdx.x * RT + sub;
+  const int K = A.geo.d_ff, G = K / 64, D = A.geo.d_model;
   const int k = A.geo.top_k;
-  const int kg0 = warp * G / EX_WARPS, kg1 = (warp + 1) * G / EX_WARPS;
-  const int r0 = rt * 16 + g4, r1 = r0 + 8;
+  const int row_bytes = K / 2, stride = DownSmem::stride(K);
+  const int kg0 = min(G, wk * KPW), kg1 = min(G, kg0 + KPW);
   const int nt_ff = K / 16;
-  __shared__ float red[EX_WARPS][4][32];
-  __shared__ float s_sums[8][64][2];     // per column: X_g, X'_g for every group of d_ff
-  __shared__ int s_last;
+
+  uint8_t* sA = smem;
+  uint16_t* sS = reinterpret_cast<uint16_t*>(smem + DownSmem::a_bytes(K, RT));
+  uint16_t* sB = sS + RT * 16 * G;
+  float* red = reinterpret_cast<float*>(smem + DownSmem::a_bytes(K, RT) + 2 * DownSmem::sb_bytes(G, RT));
+  float* s_sums = red + EX_WARPS * 4 * 32;      // [8][G][2]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(s_sums + 8 * G * 2);
+  __shared__ int s_last[RT];
 
   const uint8_t* blob = A.arena + (long long)(slot < 0 ? 0 : slot) * A.geo.blob;
-  const uint32_t* Wd = reinterpret_cast<const uint32_t*>(blob + A.geo.off[2][0]);
-  const uint16_t* Sd = reinterpret_cast<const uint16_t*>(blob + A.geo.off[2][1]);
-  const uint16_t* Bd = reinterpret_cast<const uint16_t*>(blob + A.geo.off[2][2]);
+  if (threadIdx.x == 0 && slot >= 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+    mbar_expect_tx(bar, (unsigned)(RT * 16 * row_bytes + 2 * DownSmem::sb_bytes(G, RT)));
+    const uint8_t* W = blob + A.geo.off[2][0] + (long long)blockIdx.x * RT * 16 * row_bytes;
+    for (int r = 0; r < RT * 16; ++r) bulk_g2s(sA + r * stride, W + r * row_bytes, row_bytes, bar);
+    bulk_g2s(sS, blob + A.geo.off[2][1] + (long long)blockIdx.x * RT * 16 * G * 2,
+             DownSmem::sb_bytes(G, RT), bar);
+    bulk_g2s(sB, blob + A.geo.off[2][2] + (long long)blockIdx.x * RT * 16 * G * 2,
+             DownSmem::sb_bytes(G, RT), bar);
+  }
+  pdl_wait();                                   // h and its sums come from k_up
+  __syncthreads();
+  bool ok = true;
+  if (slot >= 0) ok = mbar_wait(bar, 0, A.status);
 
   for (int n0 = 0; n0 < m; n0 += 8) {
     const int* pairs = A.grp.grp_pairs + start + n0;
     const int nn = min(8, m - n0);
-    // per-group sums of h for the columns of this pass (4 row tiles each)
+    // per-group sums of h for this pass's columns: 4 row-tile partials each
     for (int i = threadIdx.x; i < nn * G; i += EX_THREADS) {
       const int col = i / G, kg = i % G;
-      const long long p = pairs[col];
-      float xs = 0.f, xp = 0.f;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        xs += A.hpart[(p * nt_ff + kg * 4 + q) * 2];
-        xp += A.hpart[(p * nt_ff + kg * 4 + q) * 2 + 1];
-      }
-      s_sums[col][kg][0] = xs;
-      s_sums[col][kg][1] = xp;
+      const float4* hp4 = reinterpret_cast<const float4*>(
+          A.hpart + ((long long)pairs[col] * nt_ff + kg * 4) * 2);
+      const float4 a = hp4[0], b = hp4[1];
+      s_sums[(col * G + kg) * 2] = (a.x + a.z) + (b.x + b.z);
+      s_sums[(col * G + kg) * 2 + 1] = (a.y + a.w) + (b.y + b.w);
     }
     __syncthreads();
-    const long long pb = (g4 < nn) ? pairs[g4] : -1;
+    const int pb = (g4 < nn) ? pairs[g4] : -1;
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
-    if (slot >= 0) {
-      for (int kg = kg0; kg < kg1; ++kg) {
-        const uint2 a0 = ldw(Wd + (long long)r0 * WPR + kg * 8 + 2 * c);
-        const uint2 a1 = ldw(Wd + (long long)r1 * WPR + kg * 8 + 2 * c);
-        uint4 b0 = make_uint4(0, 0, 0, 0), b1 = b0;
-        if (pb >= 0) {
-          const uint4* fb = reinterpret_cast<const uint4*>(A.hfrag + (pb * G + kg) * 64);
-          b0 = fb[c];
-          b1 = fb[4 + c];
-        }
-        float cc[4] = {0.f, 0.f, 0.f, 0.f};
-        mma_group(cc, a0, a1, b0, b1);
-        float xs0 = 0.f, xp0 = 0.f, xs1 = 0.f, xp1 = 0.f;
-        if (2 * c < nn) { xs0 = s_sums[2 * c][kg][0]; xp0 = s_sums[2 * c][kg][1]; }
-        if (2 * c + 1 < nn) { xs1 = s_sums[2 * c + 1][kg][0]; xp1 = s_sums[2 * c + 1][kg][1]; }
-        const float s0 = bf2f(Sd[(long long)r0 * G + kg]), s1 = bf2f(Sd[(long long)r1 * G + kg]);
-        const float q0 = bf2f(Bd[(long long)r0 * G + kg]), q1 = bf2f(Bd[(long long)r1 * G + kg]);
-        tot[0] += s0 * (cc[0] - 1024.f * xp0) + q0 * xs0;
-        tot[1] += s0 * (cc[1] - 1024.f * xp1) + q0 * xs1;
-        tot[2] += s1 * (cc[2] - 1024.f * xp0) + q1 * xs0;
-        tot[3] += s1 * (cc[3] - 1024.f * xp1) + q1 * xs1;
-      }
+    if (slot >= 0 && ok && kg0 < kg1) {
+      tile_dot_smem<KPW>(tot, sA + sub * 16 * stride, stride, G, kg0, kg1, g4, c,
+                         sS + sub * 16 * G, sB + sub * 16 * G,
+                         pb >= 0 ? A.hfrag + (long long)pb * G * 64 : nullptr,
+                         (2 * c < nn) ? s_sums + (2 * c) * G * 2 : nullptr,
+                         (2 * c + 1 < nn) ? s_sums + (2 * c + 1) * G * 2 : nullptr);
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) red[warp][i][lane] = tot[i];
+    for (int i = 0; i < 4; ++i) red[(warp * 4 + i) * 32 + lane] = tot[i];
     __syncthreads();
-    if (warp == 0) {
+    if (wk == 0) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         float v = 0.f;
-        for (int w = 0; w < EX_WARPS; ++w) v += red[w][i][lane];
-        const int row = (i < 2) ? r0 : r1;
+#pragma unroll
+        for (int w = 0; w < WPT; ++w) v += red[((sub * WPT + w) * 4 + i) * 32 + lane];
+        const int row = rt * 16 + g4 + ((i < 2) ? 0 : 8);
         const int col = 2 * c + (i & 1);
         if (col < nn) {
+          v = bfr(v);                            // gather_qmm output
           if (MODEL == 1 && slot >= 0) {
             const uint16_t* bdp = reinterpret_cast<const uint16_t*>(blob + A.geo.off[2][3]);
-            v += bf2f(bdp[row]);
+            v = bfr(v + bf2f(bdp[row]));
           }
-          A.ypart[(long long)pairs[col] * D + row] = (slot >= 0) ? v : 0.f;
+          A.ypart[(long long)pairs[col] * D + row] = (slot >= 0 && ok) ? v : 0.f;
         }
       }
     }
     __syncthreads();
   }
 
-  // ---- arrival: the last CTA of this row tile combines all tokens' k parts
+  // ---- arrival: the last CTA of a row tile combines all tokens' k parts
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&A.cnt[rt], 1u);
-    s_last = (prev == (unsigned)n_groups - 1u);
+  if (threadIdx.x < RT) {
+    const unsigned prev = atomicAdd(&A.cnt[blockIdx.x * RT + threadIdx.x], 1u);
+    s_last[threadIdx.x] = (prev == (unsigned)n_groups - 1u);
   }
   __syncthreads();
-  if (!s_last) return;
+  bool any = false;
+  for (int r = 0; r < RT; ++r) any |= s_last[r] != 0;
+  if (!any) return;
   __threadfence();
-  for (int i = threadIdx.x; i < A.T * 16; i += EX_THREADS) {
-    const int t = i >> 4, row = rt * 16 + (i & 15);
-    float acc = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const long long p = (long long)t * k + j;
-      acc += A.scores[p] * __ldcg(A.ypart + p * D + row);
+  for (int r = 0; r < RT; ++r) {
+    if (!s_last[r]) continue;
+    const int rtile = blockIdx.x * RT + r;
+    for (int i = threadIdx.x; i < A.T * 16; i += EX_THREADS) {
+      const int t = i >> 4, row = rtile * 16 + (i & 15);
+      float acc = 0.f;
+      for (int j = 0; j < k; ++j) {
+        const long long p = (long long)t * k + j;
+        // (y * scores) is a bf16 product before the sum (engine_v3.py:600)
+        acc += bfr(A.scores[p] * __ldcg(A.ypart + p * D + row));
+      }
+      A.y[(long long)t * D + row] = f2bf(acc);
     }
-    A.y[(long long)t * D + row] = f2bf(acc);
+    if (threadIdx.x == 0) A.cnt[rtile] = 0u;
   }
-  if (threadIdx.x == 0) A.cnt[rt] = 0u;
+}
+
+template <typename Kern>
+static cudaError_t launch_pdl(Kern kern, dim3 grid, int smem, cudaStream_t s, const ExpArgs& a,
+                              bool pdl) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(EX_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 cudaError_t launch_expert(const ExpArgs& a, int max_groups, cudaStream_t s) {
   if (max_groups <= 0) return cudaSuccess;
-  dim3 gu(a.geo.d_ff / 16, max_groups), gd(a.geo.d_model / 16, max_groups);
+  const int K = a.geo.d_model, F = a.geo.d_ff, G = K / 64, GF = F / 64;
+  dim3 gu(F / 16, max_groups);
+  cudaError_t e;
+  const int su = UpSmem::total(K);
   if (a.geo.model == 1) {
-    k_up<1><<<gu, EX_THREADS, 0, s>>>(a);
-    k_down<1><<<gd, EX_THREADS, 0, s>>>(a);
+    // gpt-oss 2880/2880: 45 groups both ways, 6 per warp
+    if (G > 48 || GF > 48) return cudaErrorInvalidValue;
+    e = launch_pdl(k_up<1, 6>, gu, su, s, a, true);
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(k_down<1, 6, 1>, dim3(K / 16, max_groups), DownSmem::total(F, 1), s, a, true);
+  } else if (G <= 32 && GF <= 12 && (K / 16) % 2 == 0) {
+    // Qwen3 2048/768: up 32 groups, 4 per warp; down 12 groups, 2 row tiles
+    // per CTA with 4 warps x 3 groups each
+    e = launch_pdl(k_up<0, 4>, gu, su, s, a, true);
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(k_down<0, 3, 2>, dim3(K / 32, max_groups), DownSmem::total(F, 2), s, a, true);
   } else {
-    k_up<0><<<gu, EX_THREADS, 0, s>>>(a);
-    k_down<0><<<gd, EX_THREADS, 0, s>>>(a);
+    // other shapes: up to 64 groups, 8 per warp
+    if (G > 64 || GF > 64) return cudaErrorInvalidValue;
+    e = launch_pdl(k_up<0, 8>, gu, su, s, a, true);
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(k_down<0, 8, 1>, dim3(K / 16, max_groups), DownSmem::total(F, 1), s, a, true);
   }
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

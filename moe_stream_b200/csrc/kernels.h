@@ -79,6 +79,7 @@ struct ExpArgs {
   const float* scores;        // [P]
   unsigned* cnt;              // [d_model/16]
   uint16_t* y;                // bf16 [T, d_model]
+  int* status;                // sticky pool status (bounded waits report here)
 };
 
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s);

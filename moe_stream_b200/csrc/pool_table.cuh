@@ -1,9 +1,12 @@
 // Device-resident slot table: ExpertPool's bookkeeping (engine_v3.py:303-454)
 // executed by ONE warp. Every decision is sequential, as in the reference,
-// because each victim choice depends on the previous one; the only parallel
-// part is the victim scan, where 32 lanes score 32 consecutive candidates of
-// the stride-7919 walk at once and a warp prefix scan recovers exactly the
-// candidate the sequential loop would have stopped at.
+// because each victim choice depends on the previous one. Two things are
+// parallel: the victim scan, where 32 lanes score 32 consecutive candidates
+// of the stride-7919 walk at once and a warp prefix scan recovers exactly the
+// candidate the sequential loop would have stopped at; and the loading of the
+// request's per-key state into shared memory ("key cache") before lane 0
+// walks the request, so the walk itself never waits on a global load. Every
+// update goes to the shared copy and straight through to global memory.
 //
 // Timing rule (shared with the CPU oracle and the golden fixtures): a
 // prefetched key stays pending until an acquire waits on it or until the end
@@ -19,6 +22,7 @@ struct OpCtx {
   long long clock, use_clock;
   int n_free, n_pend, n_pin, n_fill;
   int status;
+  int victim_key;           // key evicted by the last warp_alloc, -1 if none
   long long st[ST_N];
 };
 
@@ -27,7 +31,7 @@ __device__ __forceinline__ void op_load(const DevTable& T, OpCtx* c, int lane) {
     const TableCtr* g = T.ctr;
     c->clock = g->clock; c->use_clock = g->use_clock;
     c->n_free = g->n_free; c->n_pend = g->n_pend; c->n_pin = g->n_pin;
-    c->n_fill = 0; c->status = 0;
+    c->n_fill = 0; c->status = 0; c->victim_key = -1;
     for (int i = 0; i < ST_N; ++i) c->st[i] = g->st[i];
   }
   __syncwarp();
@@ -48,10 +52,11 @@ __device__ __forceinline__ void op_store(const DevTable& T, OpCtx* c, int lane) 
 
 // _alloc (engine_v3.py:313-374). All 32 lanes call it; returns the slot or
 // -1 when every slot is empty/pinned/pending ("pool exhausted"). The clock
-// advances even on failure, as in the reference (:323).
+// advances even on failure, as in the reference (:323). The evicted key, if
+// any, is left in c->victim_key.
 __device__ int warp_alloc(const DevTable& T, OpCtx* c, int key, int lane) {
   __syncwarp();
-  if (lane == 0) c->clock += 1;
+  if (lane == 0) { c->clock += 1; c->victim_key = -1; }
   __syncwarp();
   const long long clock = c->clock;
   const int n_free = c->n_free;
@@ -110,6 +115,7 @@ __device__ int warp_alloc(const DevTable& T, OpCtx* c, int key, int lane) {
     slot = (int)((start + (long long)j * STRIDE) % n);
     if (lane == 0) {                         // evict (:357-362)
       const int vk = T.key_of[slot];
+      c->victim_key = vk;
       T.kflags[vk] &= (uint8_t)~KF_FROMPF;
       T.born[vk] = 0;
       T.last_use[vk] = 0;
@@ -126,18 +132,120 @@ __device__ int warp_alloc(const DevTable& T, OpCtx* c, int key, int lane) {
   return slot;
 }
 
-// _touch (engine_v3.py:376-380). Lane 0 only.
-__device__ __forceinline__ void touch0(const DevTable& T, OpCtx* c, int key) {
-  c->use_clock += 1;
-  T.last_use[key] = c->use_clock;
-  T.freq[key] += 1;
+// ---------------------------------------------------------------- key cache
+constexpr int KC_MAX = 640;   // >= n_experts * (1 + prefetch depths), checked at create
+
+struct KeyCache {
+  int n;
+  int key[KC_MAX];
+  int slot[KC_MAX];
+  int freq[KC_MAX];
+  uint8_t flags[KC_MAX];
+  uint8_t pin[KC_MAX];      // pinned[slot[i]] when slot[i] >= 0
+};
+
+// A request: items i = 0..n-1 map to cache entries ci[i] (distinct keys get
+// distinct entries; a repeated expert reuses its entry).
+struct Req {
+  int n;
+  int base;                 // first cache entry of this request
+  int n_uniq;               // entries [base, base + n_uniq)
+  int* ci;                  // [n] shared scratch
+};
+
+// Load keys layer*E + experts[i] into the cache (all lanes). With
+// may_repeat == false the caller guarantees distinct experts.
+__device__ void kc_add(const DevTable& T, KeyCache* kc, Req& r, int layer, const int* experts,
+                       int n, bool may_repeat, int lane) {
+  __syncwarp();
+  r.n = n;
+  r.base = kc->n;
+  if (!may_repeat) {
+    for (int i = lane; i < n; i += 32) r.ci[i] = r.base + i;
+    r.n_uniq = n;
+  } else {
+    // first occurrence of each expert (n is small on this path)
+    for (int i = lane; i < n; i += 32) {
+      int first = i;
+      for (int j = 0; j < i; ++j)
+        if (experts[j] == experts[i]) { first = j; break; }
+      r.ci[i] = -1 - first;                  // provisional: index of first occurrence
+    }
+    __syncwarp();
+    if (lane == 0) {
+      int m = 0;
+      for (int i = 0; i < n; ++i) {
+        const int f = -1 - r.ci[i];
+        r.ci[i] = (f == i) ? r.base + m++ : r.ci[f];
+      }
+      r.n_uniq = m;
+    }
+    __syncwarp();
+    r.n_uniq = __shfl_sync(MS_FULL, r.n_uniq, 0);
+  }
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) {
+    const int c = r.ci[i];
+    const int key = layer * T.n_experts + experts[i];
+    kc->key[c] = key;                        // repeated items write the same values
+    kc->slot[c] = T.slot_of[key];
+    kc->flags[c] = T.kflags[key];
+    kc->freq[c] = T.freq[key];
+  }
+  __syncwarp();
+  for (int c = r.base + lane; c < r.base + r.n_uniq; c += 32) {
+    const int sl = kc->slot[c];
+    kc->pin[c] = sl >= 0 ? T.pinned[sl] : 0;
+  }
+  __syncwarp();
+  if (lane == 0) kc->n = r.base + r.n_uniq;
+  __syncwarp();
 }
 
-__device__ __forceinline__ void pin0(const DevTable& T, OpCtx* c, int slot) {
-  if (!T.pinned[slot]) {
+// _alloc for cache entry ci, keeping the copies coherent (all lanes).
+__device__ int kc_alloc(const DevTable& T, OpCtx* c, KeyCache* kc, int ci, int lane) {
+  const int slot = warp_alloc(T, c, kc->key[ci], lane);
+  if (slot < 0) return -1;
+  const int vk = c->victim_key;
+  if (vk >= 0) {
+    for (int i = lane; i < kc->n; i += 32)
+      if (kc->key[i] == vk) {
+        kc->slot[i] = -1;
+        kc->flags[i] &= (uint8_t)~KF_FROMPF;
+        kc->freq[i] = 0;
+        kc->pin[i] = 0;
+      }
+  }
+  __syncwarp();
+  if (lane == 0) {
+    kc->slot[ci] = slot;
+    kc->pin[ci] = 0;                         // a victim or free slot is never pinned
+  }
+  __syncwarp();
+  return slot;
+}
+
+// _touch (engine_v3.py:376-380). Lane 0 only.
+__device__ __forceinline__ void touch0(const DevTable& T, OpCtx* c, KeyCache* kc, int ci) {
+  const int key = kc->key[ci];
+  c->use_clock += 1;
+  T.last_use[key] = c->use_clock;
+  kc->freq[ci] += 1;
+  T.freq[key] = kc->freq[ci];
+}
+
+__device__ __forceinline__ void pin0(const DevTable& T, OpCtx* c, KeyCache* kc, int ci) {
+  if (!kc->pin[ci]) {
+    const int slot = kc->slot[ci];
+    kc->pin[ci] = 1;
     T.pinned[slot] = 1;
     T.pin_list[c->n_pin++] = slot;
   }
+}
+
+__device__ __forceinline__ void setflags0(const DevTable& T, KeyCache* kc, int ci, uint8_t f) {
+  kc->flags[ci] = f;
+  T.kflags[kc->key[ci]] = f;
 }
 
 __device__ __forceinline__ void add_fill0(const DevTable& T, OpCtx* c, int slot, int key) {
@@ -145,17 +253,17 @@ __device__ __forceinline__ void add_fill0(const DevTable& T, OpCtx* c, int slot,
   c->n_fill++;
 }
 
-// prefetch (engine_v3.py:383-396): experts in caller order; stops at the
+// prefetch (engine_v3.py:383-396) of request r in caller order; stops at the
 // first exhaustion and counts one bail.
-__device__ void warp_prefetch(const DevTable& T, OpCtx* c, int layer, const int* experts,
-                              int n, int lane) {
-  for (int i = 0; i < n; ++i) {
-    const int key = layer * T.n_experts + experts[i];
+__device__ void warp_prefetch(const DevTable& T, OpCtx* c, KeyCache* kc, const Req& r,
+                              int lane) {
+  for (int i = 0; i < r.n; ++i) {
+    const int ci = r.ci[i];
     __syncwarp();
-    const bool skip = T.slot_of[key] >= 0 || (T.kflags[key] & KF_PENDING);
+    const bool skip = kc->slot[ci] >= 0 || (kc->flags[ci] & KF_PENDING);
     __syncwarp();
     if (skip) continue;
-    const int slot = warp_alloc(T, c, key, lane);
+    const int slot = kc_alloc(T, c, kc, ci, lane);
     if (slot < 0) {
       if (lane == 0) c->st[ST_BAIL] += 1;
       __syncwarp();
@@ -163,63 +271,74 @@ __device__ void warp_prefetch(const DevTable& T, OpCtx* c, int layer, const int*
     }
     if (lane == 0) {
       c->st[ST_ISSUED] += 1;
-      T.kflags[key] |= KF_PENDING;
-      T.pend_list[c->n_pend++] = key;
-      add_fill0(T, c, slot, key);
+      setflags0(T, kc, ci, (uint8_t)(kc->flags[ci] | KF_PENDING));
+      T.pend_list[c->n_pend++] = kc->key[ci];
+      add_fill0(T, c, slot, kc->key[ci]);
     }
     __syncwarp();
   }
 }
 
-// Completion of every read still pending (end of an acquire call).
-__device__ void warp_drain(const DevTable& T, OpCtx* c, int lane) {
+// Completion of every read still pending (end of an acquire call). Pending
+// keys are distinct, so the lanes take them in parallel.
+__device__ void warp_drain(const DevTable& T, OpCtx* c, KeyCache* kc, int lane) {
   __syncwarp();
-  if (lane == 0) {
-    for (int i = 0; i < c->n_pend; ++i) {
-      const int key = T.pend_list[i];
-      if (T.kflags[key] & KF_PENDING) {
-        T.kflags[key] = (uint8_t)((T.kflags[key] & ~KF_PENDING) | KF_FROMPF);
-        c->st[ST_READS] += 1;
-      }
+  const int n = c->n_pend;
+  int done = 0;
+  for (int i = lane; i < n; i += 32) {
+    const int key = T.pend_list[i];
+    const uint8_t f = T.kflags[key];
+    if (f & KF_PENDING) {
+      T.kflags[key] = (uint8_t)((f & ~KF_PENDING) | KF_FROMPF);
+      ++done;
     }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) done += __shfl_xor_sync(MS_FULL, done, o);
+  __syncwarp();
+  for (int i = lane; i < kc->n; i += 32)
+    if (kc->flags[i] & KF_PENDING) kc->flags[i] = (uint8_t)((kc->flags[i] & ~KF_PENDING) | KF_FROMPF);
+  if (lane == 0) {
+    c->st[ST_READS] += done;
     c->n_pend = 0;
   }
   __syncwarp();
 }
 
-// acquire (engine_v3.py:398-454). slots_out[i] receives the slot of
-// experts[i] (-1 if exhausted before it was placed). waits: scratch of n
-// ints (shared or global). Returns 0 or MS_E_EXHAUSTED (-3).
-__device__ int warp_acquire(const DevTable& T, OpCtx* c, int layer, const int* experts,
-                            int n, int* slots_out, int* waits, int lane) {
+// acquire (engine_v3.py:398-454) of request r. slots_out[i] receives the
+// slot of item i (-1 if exhausted before it was placed). waits: scratch of
+// r.n ints. Returns 0 or MS_E_EXHAUSTED (-3).
+__device__ int warp_acquire(const DevTable& T, OpCtx* c, KeyCache* kc, const Req& r,
+                            int* slots_out, int* waits, int lane) {
+  const int n = r.n;
   int n_wait = 0, n_issue = 0, status = 0;
+  for (int i = lane; i < n; i += 32) slots_out[i] = -1;
   for (int i = 0; i < n; ++i) {
-    const int key = layer * T.n_experts + experts[i];
+    const int ci = r.ci[i];
     __syncwarp();
-    const bool pend = (T.kflags[key] & KF_PENDING) != 0;
-    int slot = T.slot_of[key];
+    const bool pend = (kc->flags[ci] & KF_PENDING) != 0;
+    int slot = kc->slot[ci];
     __syncwarp();
     bool issued_now = false;
     if (!pend && slot < 0) {
-      slot = warp_alloc(T, c, key, lane);
+      slot = kc_alloc(T, c, kc, ci, lane);
       if (slot < 0) { status = -3; break; }
       if (lane == 0) {
-        pin0(T, c, slot);
-        touch0(T, c, key);
-        add_fill0(T, c, slot, key);
+        pin0(T, c, kc, ci);
+        touch0(T, c, kc, ci);
+        add_fill0(T, c, slot, kc->key[ci]);
       }
       ++n_issue;
       issued_now = true;
     } else if (slot >= 0) {
-      if (lane == 0) { pin0(T, c, slot); touch0(T, c, key); }
+      if (lane == 0) { pin0(T, c, kc, ci); touch0(T, c, kc, ci); }
     }
     if (lane == 0) {
       if (pend) {
         waits[n_wait] = i;
-        slots_out[i] = -1;
       } else if (slot >= 0 && !issued_now) {
-        const bool early = (T.kflags[key] & KF_FROMPF) != 0;
-        T.kflags[key] &= (uint8_t)~KF_FROMPF;
+        const bool early = (kc->flags[ci] & KF_FROMPF) != 0;
+        if (early) setflags0(T, kc, ci, (uint8_t)(kc->flags[ci] & ~KF_FROMPF));
         c->st[early ? ST_PREFETCH : ST_CACHE] += 1;
         slots_out[i] = slot;
       }
@@ -234,29 +353,37 @@ __device__ int warp_acquire(const DevTable& T, OpCtx* c, int layer, const int* e
       c->st[ST_READS] += n_issue;
       for (int w = 0; w < n_wait; ++w) {            // (:438-446)
         const int i = waits[w];
-        const int key = layer * T.n_experts + experts[i];
-        if (T.kflags[key] & KF_PENDING) c->st[ST_READS] += 1;
-        T.kflags[key] &= (uint8_t)~(KF_PENDING | KF_FROMPF);
-        const int slot = T.slot_of[key];
-        slots_out[i] = slot;
-        pin0(T, c, slot);
-        touch0(T, c, key);
+        const int ci = r.ci[i];
+        if (kc->flags[ci] & KF_PENDING) c->st[ST_READS] += 1;
+        setflags0(T, kc, ci, (uint8_t)(kc->flags[ci] & ~(KF_PENDING | KF_FROMPF)));
+        slots_out[i] = kc->slot[ci];
+        pin0(T, c, kc, ci);
+        touch0(T, c, kc, ci);
         c->st[ST_PREFETCH] += 1;
       }
       c->st[ST_MISS] += n_issue;
-      // pinned = set(slots) (:452-453)
-      for (int i = 0; i < c->n_pin; ++i) T.pinned[T.pin_list[i]] = 0;
-      c->n_pin = 0;
-      for (int i = 0; i < n; ++i) {
-        const int s = slots_out[i];
-        if (s >= 0) pin0(T, c, s);
-      }
     }
+    __syncwarp();
+    // pinned = set(slots) (:452-453): unpin every slot on the list, then pin
+    // the slots of this request's distinct keys
+    const int np = c->n_pin;
+    for (int i = lane; i < np; i += 32) T.pinned[T.pin_list[i]] = 0;
+    for (int i = lane; i < kc->n; i += 32) kc->pin[i] = 0;
+    __syncwarp();
+    for (int e = lane; e < r.n_uniq; e += 32) {
+      const int ci = r.base + e;
+      const int s = kc->slot[ci];
+      T.pin_list[e] = s;
+      T.pinned[s] = 1;
+      kc->pin[ci] = 1;
+    }
+    __syncwarp();
+    if (lane == 0) c->n_pin = r.n_uniq;
   } else if (lane == 0) {
     c->status = status;
   }
   __syncwarp();
-  warp_drain(T, c, lane);
+  warp_drain(T, c, kc, lane);
   return status;
 }
 

@@ -119,6 +119,8 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
   __shared__ int s_cnt[MAX_E], s_run[MAX_E];
   __shared__ int s_n_acq;
   __shared__ OpCtx s_op;
+  __shared__ KeyCache s_kc;
+  __shared__ int s_ci[MS_MAX_DEPTHS + 1][MAX_E];
 
   for (int i = threadIdx.x; i < MAX_E / 32; i += RT_THREADS) {
     s_acq_mask[i] = 0;
@@ -210,15 +212,20 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
     if (A.do_pool) {
       const DevTable& Tb = A.tab;
       op_load(Tb, &s_op, lane);
-      // ExpertPool.prefetch for each target layer, then acquire
-      // (engine_v3.py:522-526, 548); np.unique sorts both lists.
-      for (int dd = 0; dd < A.n_pred; ++dd)
-        if (A.pred_layer[dd] >= 0)
-          warp_prefetch(Tb, &s_op, A.pred_layer[dd], s_pred[dd], s_n_pred[dd], lane);
-      if (lane == 0)
-        for (int i = 0; i < n_acq; ++i) s_slots[i] = -1;
+      if (lane == 0) s_kc.n = 0;
       __syncwarp();
-      warp_acquire(Tb, &s_op, A.layer, s_acq, n_acq, s_slots, s_waits, lane);
+      // one parallel load of every key's state, then ExpertPool.prefetch for
+      // each target layer and acquire of this layer (engine_v3.py:522-526,
+      // 548); np.unique makes both lists sorted and distinct
+      Req rp[MS_MAX_DEPTHS], ra;
+      for (int dd = 0; dd < A.n_pred; ++dd) {
+        rp[dd].ci = s_ci[dd];
+        kc_add(Tb, &s_kc, rp[dd], A.pred_layer[dd], s_pred[dd], s_n_pred[dd], false, lane);
+      }
+      ra.ci = s_ci[MS_MAX_DEPTHS];
+      kc_add(Tb, &s_kc, ra, A.layer, s_acq, n_acq, false, lane);
+      for (int dd = 0; dd < A.n_pred; ++dd) warp_prefetch(Tb, &s_op, &s_kc, rp[dd], lane);
+      warp_acquire(Tb, &s_op, &s_kc, ra, s_slots, s_waits, lane);
       op_store(Tb, &s_op, lane);
     } else if (lane == 0) {
       for (int i = 0; i < n_acq; ++i) s_slots[i] = -1;
@@ -240,22 +247,25 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
 // one warp, the request passed by value.
 __global__ void k_pool_op(DevTable Tb, PoolReq R, int* slots_out, int* op_status) {
   __shared__ OpCtx s_op;
+  __shared__ KeyCache s_kc;
   __shared__ int s_exp[MS_MAX_REQ];
+  __shared__ int s_ci[MS_MAX_REQ];
   __shared__ int s_slots[MS_MAX_REQ];
   __shared__ int s_waits[MS_MAX_REQ];
   const int lane = threadIdx.x & 31;
   if (threadIdx.x >= 32) return;
   for (int i = lane; i < R.n; i += 32) s_exp[i] = R.experts[i];
+  if (lane == 0) s_kc.n = 0;
   __syncwarp();
   op_load(Tb, &s_op, lane);
+  Req r;
+  r.ci = s_ci;
+  kc_add(Tb, &s_kc, r, R.layer, s_exp, R.n, true, lane);   // callers may repeat experts
   int st = 0;
   if (R.op == 0) {
-    warp_prefetch(Tb, &s_op, R.layer, s_exp, R.n, lane);
+    warp_prefetch(Tb, &s_op, &s_kc, r, lane);
   } else {
-    if (lane == 0)
-      for (int i = 0; i < R.n; ++i) s_slots[i] = -1;
-    __syncwarp();
-    st = warp_acquire(Tb, &s_op, R.layer, s_exp, R.n, s_slots, s_waits, lane);
+    st = warp_acquire(Tb, &s_op, &s_kc, r, s_slots, s_waits, lane);
     for (int i = lane; i < R.n; i += 32) slots_out[i] = s_slots[i];
   }
   op_store(Tb, &s_op, lane);

@@ -1,0 +1,60 @@
+// Bulk-copy (TMA, cp.async.bulk) staging with mbarrier completion, and the
+// bounded waits every spin in this library must use.
+#pragma once
+#include "ms_common.cuh"
+
+namespace ms {
+
+// Spin limit of an mbarrier wait: ~2^26 polls (far beyond any legitimate
+// copy); on expiry the waiter records MS_E_TIMEOUT and gives up.
+constexpr unsigned MBAR_SPIN_LIMIT = 1u << 26;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for phase `phase` of `bar`. Returns false (and sets *status
+// to MS_E_TIMEOUT once) if the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, int* status) {
+  for (unsigned i = 0; i < MBAR_SPIN_LIMIT; ++i)
+    if (mbar_try_wait(bar, phase)) return true;
+  if (status) atomicCAS(status, 0, -4);
+  return false;
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+}  // namespace ms
