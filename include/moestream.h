@@ -197,6 +197,32 @@ int ms_block_debug(ms_pool* pool, const int32_t** inds, const void** scores,
 int ms_pool_profile(ms_pool* pool, int enable);
 int ms_pool_timing(ms_pool* pool, int layer, float* out3);
 
+/* ms_expert_mlp without a pool and without any allocation. This entry point
+ * has no counterpart in the reference. It is for callers that may not call
+ * cudaMalloc when they run the block -- a runtime that reserved all device
+ * memory up front and only lends out buffers it planned, an engine whose
+ * enqueue step must not allocate -- and so cannot create a pool, whose
+ * arena and scratch buffers are allocated. The caller passes the geometry,
+ * the expert weights (`arena`: n_slots blobs of geom->blob_bytes, laid out as
+ * in the store, e.g. the arena of an existing pool or a caller-owned buffer),
+ * slots int32 [T,k], scores f32 [T,k], x bf16 [T,d_model] and y bf16
+ * [T,d_model], all device memory on the current device; intermediates live in
+ * a fixed ~2 MB __device__ array inside the library, which every GPU that
+ * loads the library keeps until the process exits.
+ * Limits: T <= MS_STATIC_MAX_TOKENS, T*k <= MS_STATIC_MAX_PAIRS, d_model and
+ * d_ff <= 4096, n_slots <= MS_STATIC_MAX_SLOTS; larger sizes return
+ * MS_E_INVALID. The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture. All calls share the array: calls that may overlap on the GPU
+ * (other streams or host threads) race, so the caller must order them.
+ * Enqueued on `stream`; does not synchronise. */
+#define MS_STATIC_MAX_TOKENS  16
+#define MS_STATIC_MAX_PAIRS   64
+#define MS_STATIC_MAX_SLOTS   65536
+int ms_expert_mlp_static(const ms_geom* geom, const void* arena, int n_slots,
+                         const int32_t* slots, const float* scores, const void* x,
+                         int T, int k, void* y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -73,6 +73,9 @@ EXPORTS = {
                       ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p],
     "ms_pool_profile": [ctypes.c_void_p, ctypes.c_int],
     "ms_pool_timing": [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float)],
+    "ms_expert_mlp_static": [ctypes.POINTER(MsGeom), ctypes.c_void_p, ctypes.c_int,
+                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                             ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p],
     "ms_block_debug": [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p),
                        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)],
 }

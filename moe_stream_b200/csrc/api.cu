@@ -46,6 +46,10 @@ int dalloc(T** p, size_t count) {
 
 }  // namespace
 
+namespace ms {
+void set_error_message(const char* msg) { g_err = msg; }
+}  // namespace ms
+
 struct ms_pool {
   int device = 0;
   ms_geom geom{};

@@ -89,4 +89,7 @@ cudaError_t launch_fill(const FillArgs& f, int grid, cudaStream_t s);
 cudaError_t launch_mlp_prep(const MlpPrepArgs& a, cudaStream_t s);
 cudaError_t launch_expert(const ExpArgs& a, int max_groups, cudaStream_t s);
 
+// Message returned by the next ms_last_error() on this thread.
+void set_error_message(const char* msg);
+
 }  // namespace ms
