@@ -66,34 +66,58 @@ __device__ __forceinline__ long long frag_off(long long r, int G, int k) {
   return ((r * G + kg) * 2 + p) * 32 + cc * 8 + hidx;
 }
 
-// Write activation row group (r, kg) in frag layout from 64 bf16 values.
-// One thread per (r, kg).
-__device__ __forceinline__ void frag_write_group(const uint16_t* src64, __half* frag, float* sums,
-                                                 long long r, int G, int kg) {
-  __half vals[64];
+// Frag layout of activation row r, quantisation group kg, word w (inputs
+// 8w..8w+7 of the group) from 8 bf16 values: the 8 halves are exactly the
+// 16-byte B-operand block of lane w>>1, pass w&1, so one thread writes one
+// uint4. The group's sums (X, X') are reduced over the 8 lanes that handle
+// words 0..7 (aligned octet of the warp, all active) and written by word 0.
+__device__ __forceinline__ void frag_write_word(const uint16_t* src8, __half* frag, float* sums,
+                                                long long r, int G, int kg, int w, bool valid) {
   float xs = 0.f, xp = 0.f;
-  const uint4* s4 = reinterpret_cast<const uint4*>(src64);
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const uint4 v = s4[q];
+  if (valid) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src8);
     const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    __half h[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const uint16_t b = (uint16_t)((w4[e >> 1] >> ((e & 1) * 16)) & 0xffffu);
-      const int k = q * 8 + e;                       // element within the group
-      const __half h = __float2half_rn(bf2f(b));
-      const __half hs = (k & 1) ? __hmul(h, __float2half(0.0625f)) : h;
-      xs += __half2float(h);
-      xp += __half2float(hs);
-      const int w = k >> 3, i = k & 7;
-      vals[((w & 1) * 4 + (w >> 1)) * 8 + (((i & 3) << 1) | (i >> 2))] = hs;
+    for (int i = 0; i < 8; ++i) {
+      const uint16_t b = (uint16_t)((w4[i >> 1] >> ((i & 1) * 16)) & 0xffffu);
+      const __half x = __float2half_rn(bf2f(b));
+      const __half xs_ = (i & 1) ? __hmul(x, __float2half(0.0625f)) : x;
+      xs += __half2float(x);
+      xp += __half2float(xs_);
+      h[((i & 3) << 1) | (i >> 2)] = xs_;
     }
+    uint4 out;
+    out.x = (uint32_t)__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[1]) << 16);
+    out.y = (uint32_t)__half_as_ushort(h[2]) | ((uint32_t)__half_as_ushort(h[3]) << 16);
+    out.z = (uint32_t)__half_as_ushort(h[4]) | ((uint32_t)__half_as_ushort(h[5]) << 16);
+    out.w = (uint32_t)__half_as_ushort(h[6]) | ((uint32_t)__half_as_ushort(h[7]) << 16);
+    *reinterpret_cast<uint4*>(frag + (r * G + kg) * 64 + ((w & 1) * 4 + (w >> 1)) * 8) = out;
   }
-  uint4* dst = reinterpret_cast<uint4*>(frag + (r * G + kg) * 64);
 #pragma unroll
-  for (int q = 0; q < 8; ++q) dst[q] = reinterpret_cast<const uint4*>(vals)[q];
-  sums[(r * G + kg) * 2] = xs;
-  sums[(r * G + kg) * 2 + 1] = xp;
+  for (int o = 1; o < 8; o <<= 1) {
+    xs += __shfl_xor_sync(MS_FULL, xs, o);
+    xp += __shfl_xor_sync(MS_FULL, xp, o);
+  }
+  if (valid && w == 0) {
+    sums[(r * G + kg) * 2] = xs;
+    sums[(r * G + kg) * 2 + 1] = xp;
+  }
+}
+
+// Frag layout of rows [0, T) of x (bf16 [T, d]) by the calling threads:
+// thread index `tid` of `nthreads` (a multiple of 32), grid-stride.
+__device__ __forceinline__ void frag_write_rows(const uint16_t* x, int T, int d, __half* frag,
+                                                float* sums, int tid, int nthreads) {
+  const int G = d / 64;
+  const int tasks = T * G * 8;
+  const int rounded = (tasks + 31) & ~31;
+  for (int i = tid; i < rounded; i += nthreads) {
+    const bool valid = i < tasks;
+    const int grp = valid ? (i >> 3) : 0, w = i & 7;
+    const int t = grp / G, kg = grp % G;
+    frag_write_word(x + (long long)t * d + kg * 64 + w * 8, frag, sums, t, G, kg, w, valid);
+  }
 }
 
 }  // namespace ms

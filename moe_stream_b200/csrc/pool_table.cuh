@@ -23,16 +23,17 @@ struct OpCtx {
   int n_free, n_pend, n_pin, n_fill;
   int status;
   int victim_key;           // key evicted by the last warp_alloc, -1 if none
+  int n_pend0;              // pending keys left by earlier calls (0 on the fused path)
   long long st[ST_N];
 };
 
 __device__ __forceinline__ void op_load(const DevTable& T, OpCtx* c, int lane) {
   if (lane == 0) {
-    const TableCtr* g = T.ctr;
-    c->clock = g->clock; c->use_clock = g->use_clock;
-    c->n_free = g->n_free; c->n_pend = g->n_pend; c->n_pin = g->n_pin;
-    c->n_fill = 0; c->status = 0; c->victim_key = -1;
-    for (int i = 0; i < ST_N; ++i) c->st[i] = g->st[i];
+    const TableCtr g = *T.ctr;                 // all loads issued before any store
+    c->clock = g.clock; c->use_clock = g.use_clock;
+    c->n_free = g.n_free; c->n_pend = g.n_pend; c->n_pin = g.n_pin;
+    c->n_fill = 0; c->status = 0; c->victim_key = -1; c->n_pend0 = g.n_pend;
+    for (int i = 0; i < ST_N; ++i) c->st[i] = g.st[i];
   }
   __syncwarp();
 }
@@ -40,12 +41,15 @@ __device__ __forceinline__ void op_load(const DevTable& T, OpCtx* c, int lane) {
 __device__ __forceinline__ void op_store(const DevTable& T, OpCtx* c, int lane) {
   __syncwarp();
   if (lane == 0) {
-    TableCtr* g = T.ctr;
-    g->clock = c->clock; g->use_clock = c->use_clock;
-    g->n_free = c->n_free; g->n_pend = c->n_pend; g->n_pin = c->n_pin;
-    g->n_fill = c->n_fill;
-    if (c->status && !g->status) g->status = c->status;
-    for (int i = 0; i < ST_N; ++i) g->st[i] = c->st[i];
+    TableCtr g;
+    g.clock = c->clock; g.use_clock = c->use_clock;
+    g.n_free = c->n_free; g.n_pend = c->n_pend; g.n_pin = c->n_pin;
+    g.n_fill = c->n_fill;
+    const int prev = T.ctr->status;            // sticky: the first error stays
+    g.status = prev ? prev : c->status;
+    g.pad = 0;
+    for (int i = 0; i < ST_N; ++i) g.st[i] = c->st[i];
+    *T.ctr = g;
   }
   __syncwarp();
 }
@@ -54,7 +58,7 @@ __device__ __forceinline__ void op_store(const DevTable& T, OpCtx* c, int lane) 
 // -1 when every slot is empty/pinned/pending ("pool exhausted"). The clock
 // advances even on failure, as in the reference (:323). The evicted key, if
 // any, is left in c->victim_key.
-__device__ int warp_alloc(const DevTable& T, OpCtx* c, int key, int lane) {
+__device__ __forceinline__ int warp_alloc(const DevTable& T, OpCtx* c, int key, int lane) {
   __syncwarp();
   if (lane == 0) { c->clock += 1; c->victim_key = -1; }
   __syncwarp();
@@ -142,6 +146,8 @@ struct KeyCache {
   int freq[KC_MAX];
   uint8_t flags[KC_MAX];
   uint8_t pin[KC_MAX];      // pinned[slot[i]] when slot[i] >= 0
+  int n_prev_pin;           // the pin list left by the previous acquire
+  int prev_pin[KC_MAX];     // (valid when n_prev_pin <= KC_MAX)
 };
 
 // A request: items i = 0..n-1 map to cache entries ci[i] (distinct keys get
@@ -153,9 +159,10 @@ struct Req {
   int* ci;                  // [n] shared scratch
 };
 
-// Load keys layer*E + experts[i] into the cache (all lanes). With
-// may_repeat == false the caller guarantees distinct experts.
-__device__ void kc_add(const DevTable& T, KeyCache* kc, Req& r, int layer, const int* experts,
+// Register keys layer*E + experts[i] as cache entries (all lanes); no
+// global memory is read here. With may_repeat == false the caller
+// guarantees distinct experts.
+__device__ __forceinline__ void kc_add(const DevTable& T, KeyCache* kc, Req& r, int layer, const int* experts,
                        int n, bool may_repeat, int lane) {
   __syncwarp();
   r.n = n;
@@ -184,26 +191,53 @@ __device__ void kc_add(const DevTable& T, KeyCache* kc, Req& r, int layer, const
     r.n_uniq = __shfl_sync(MS_FULL, r.n_uniq, 0);
   }
   __syncwarp();
-  for (int i = lane; i < n; i += 32) {
-    const int c = r.ci[i];
-    const int key = layer * T.n_experts + experts[i];
-    kc->key[c] = key;                        // repeated items write the same values
-    kc->slot[c] = T.slot_of[key];
-    kc->flags[c] = T.kflags[key];
-    kc->freq[c] = T.freq[key];
-  }
-  __syncwarp();
-  for (int c = r.base + lane; c < r.base + r.n_uniq; c += 32) {
-    const int sl = kc->slot[c];
-    kc->pin[c] = sl >= 0 ? T.pinned[sl] : 0;
-  }
+  for (int i = lane; i < n; i += 32)
+    kc->key[r.ci[i]] = layer * T.n_experts + experts[i];   // repeats write the same key
   __syncwarp();
   if (lane == 0) kc->n = r.base + r.n_uniq;
   __syncwarp();
 }
 
+// Load the state of every registered entry and the previous pin list in one
+// round of independent loads (all lanes). The pinned-ness of an entry's slot
+// is membership in that pin list (pinned[] and the list are kept equal).
+__device__ __forceinline__ void kc_load(const DevTable& T, const OpCtx* c, KeyCache* kc, int lane) {
+  __syncwarp();
+  const int n = kc->n;
+  const int np = c->n_pin;
+  for (int i = lane; i < n; i += 32) {
+    const int key = kc->key[i];
+    const int sl = T.slot_of[key];             // three independent loads, then the stores
+    const uint8_t fl = T.kflags[key];
+    const int fr = T.freq[key];
+    kc->slot[i] = sl;
+    kc->flags[i] = fl;
+    kc->freq[i] = fr;
+  }
+  if (np <= KC_MAX)
+    for (int i = lane; i < np; i += 32) {
+      const int v = T.pin_list[i];
+      kc->prev_pin[i] = v;
+    }
+  if (lane == 0) kc->n_prev_pin = np;
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) {
+    const int sl = kc->slot[i];
+    uint8_t pin = 0;
+    if (sl >= 0) {
+      if (np <= KC_MAX) {
+        for (int j = 0; j < np; ++j) pin |= (kc->prev_pin[j] == sl);
+      } else {
+        pin = T.pinned[sl];
+      }
+    }
+    kc->pin[i] = pin;
+  }
+  __syncwarp();
+}
+
 // _alloc for cache entry ci, keeping the copies coherent (all lanes).
-__device__ int kc_alloc(const DevTable& T, OpCtx* c, KeyCache* kc, int ci, int lane) {
+__device__ __forceinline__ int kc_alloc(const DevTable& T, OpCtx* c, KeyCache* kc, int ci, int lane) {
   const int slot = warp_alloc(T, c, kc->key[ci], lane);
   if (slot < 0) return -1;
   const int vk = c->victim_key;
@@ -255,14 +289,14 @@ __device__ __forceinline__ void add_fill0(const DevTable& T, OpCtx* c, int slot,
 
 // prefetch (engine_v3.py:383-396) of request r in caller order; stops at the
 // first exhaustion and counts one bail.
-__device__ void warp_prefetch(const DevTable& T, OpCtx* c, KeyCache* kc, const Req& r,
+__device__ __forceinline__ void warp_prefetch(const DevTable& T, OpCtx* c, KeyCache* kc, const Req& r,
                               int lane) {
   for (int i = 0; i < r.n; ++i) {
     const int ci = r.ci[i];
-    __syncwarp();
-    const bool skip = kc->slot[ci] >= 0 || (kc->flags[ci] & KF_PENDING);
-    __syncwarp();
-    if (skip) continue;
+    int skip = 0;
+    if (lane == 0) skip = kc->slot[ci] >= 0 || (kc->flags[ci] & KF_PENDING);
+    if (__shfl_sync(MS_FULL, skip, 0)) continue;
+    __syncwarp();                            // lane 0's writes before the collective scan
     const int slot = kc_alloc(T, c, kc, ci, lane);
     if (slot < 0) {
       if (lane == 0) c->st[ST_BAIL] += 1;
@@ -275,22 +309,33 @@ __device__ void warp_prefetch(const DevTable& T, OpCtx* c, KeyCache* kc, const R
       T.pend_list[c->n_pend++] = kc->key[ci];
       add_fill0(T, c, slot, kc->key[ci]);
     }
-    __syncwarp();
   }
+  __syncwarp();
 }
 
 // Completion of every read still pending (end of an acquire call). Pending
 // keys are distinct, so the lanes take them in parallel.
-__device__ void warp_drain(const DevTable& T, OpCtx* c, KeyCache* kc, int lane) {
+__device__ __forceinline__ void warp_drain(const DevTable& T, OpCtx* c, KeyCache* kc, int lane) {
   __syncwarp();
   const int n = c->n_pend;
   int done = 0;
-  for (int i = lane; i < n; i += 32) {
-    const int key = T.pend_list[i];
-    const uint8_t f = T.kflags[key];
-    if (f & KF_PENDING) {
-      T.kflags[key] = (uint8_t)((f & ~KF_PENDING) | KF_FROMPF);
-      ++done;
+  if (c->n_pend0 == 0) {
+    // every pending key went pending in this call, so it is in the cache
+    for (int i = lane; i < kc->n; i += 32) {
+      const uint8_t f = kc->flags[i];
+      if (f & KF_PENDING) {
+        T.kflags[kc->key[i]] = (uint8_t)((f & ~KF_PENDING) | KF_FROMPF);
+        ++done;
+      }
+    }
+  } else {
+    for (int i = lane; i < n; i += 32) {
+      const int key = T.pend_list[i];
+      const uint8_t f = T.kflags[key];
+      if (f & KF_PENDING) {
+        T.kflags[key] = (uint8_t)((f & ~KF_PENDING) | KF_FROMPF);
+        ++done;
+      }
     }
   }
 #pragma unroll
@@ -308,19 +353,24 @@ __device__ void warp_drain(const DevTable& T, OpCtx* c, KeyCache* kc, int lane) 
 // acquire (engine_v3.py:398-454) of request r. slots_out[i] receives the
 // slot of item i (-1 if exhausted before it was placed). waits: scratch of
 // r.n ints. Returns 0 or MS_E_EXHAUSTED (-3).
-__device__ int warp_acquire(const DevTable& T, OpCtx* c, KeyCache* kc, const Req& r,
+__device__ __forceinline__ int warp_acquire(const DevTable& T, OpCtx* c, KeyCache* kc, const Req& r,
                             int* slots_out, int* waits, int lane) {
   const int n = r.n;
   int n_wait = 0, n_issue = 0, status = 0;
   for (int i = lane; i < n; i += 32) slots_out[i] = -1;
+  __syncwarp();
   for (int i = 0; i < n; ++i) {
     const int ci = r.ci[i];
-    __syncwarp();
-    const bool pend = (kc->flags[ci] & KF_PENDING) != 0;
-    int slot = kc->slot[ci];
-    __syncwarp();
+    int pend = 0, slot = -1;
+    if (lane == 0) {                         // lane 0 decides, the warp follows
+      pend = (kc->flags[ci] & KF_PENDING) != 0;
+      slot = kc->slot[ci];
+    }
+    pend = __shfl_sync(MS_FULL, pend, 0);
+    slot = __shfl_sync(MS_FULL, slot, 0);
     bool issued_now = false;
     if (!pend && slot < 0) {
+      __syncwarp();                          // lane 0's writes before the collective scan
       slot = kc_alloc(T, c, kc, ci, lane);
       if (slot < 0) { status = -3; break; }
       if (lane == 0) {
@@ -366,8 +416,18 @@ __device__ int warp_acquire(const DevTable& T, OpCtx* c, KeyCache* kc, const Req
     __syncwarp();
     // pinned = set(slots) (:452-453): unpin every slot on the list, then pin
     // the slots of this request's distinct keys
+    // the list holds the previous acquire's slots (loaded up front) plus the
+    // slots pinned in this call, which all belong to cache entries
     const int np = c->n_pin;
-    for (int i = lane; i < np; i += 32) T.pinned[T.pin_list[i]] = 0;
+    const int npp = kc->n_prev_pin;
+    if (npp <= KC_MAX) {
+      for (int i = lane; i < npp; i += 32) T.pinned[kc->prev_pin[i]] = 0;
+      for (int i = lane; i < kc->n; i += 32)
+        if (kc->pin[i] && kc->slot[i] >= 0) T.pinned[kc->slot[i]] = 0;
+    } else {
+      for (int i = lane; i < np; i += 32) T.pinned[T.pin_list[i]] = 0;
+    }
+    __syncwarp();
     for (int i = lane; i < kc->n; i += 32) kc->pin[i] = 0;
     __syncwarp();
     for (int e = lane; e < r.n_uniq; e += 32) {

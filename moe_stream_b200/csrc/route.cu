@@ -20,34 +20,39 @@ namespace ms {
 
 constexpr int MAX_E = 256;
 constexpr int RT_THREADS = 256;
+constexpr int SMALL_P = 256;     // pairs grouped inside one warp up to this many
 
 __device__ __forceinline__ uint32_t mono_key(uint16_t b) {
   // order-preserving map of bf16 bits to unsigned
   return (b & 0x8000u) ? (uint32_t)(~b & 0xffffu) : (uint32_t)(b | 0x8000u);
 }
 
-// top-k of vals[0..E) (bf16 bit patterns, one warp): descending, exact
-// ties to the lower index. Writes indices to out[0..k).
-__device__ void warp_topk(const uint16_t* vals, int E, int k, int* out, int lane) {
-  // candidates held by this lane: e = lane + 32*i
-  unsigned taken = 0;
-  for (int r = 0; r < k; ++r) {
-    unsigned long long best = 0;
-    for (int i = 0; lane + 32 * i < E; ++i) {
-      if (taken & (1u << i)) continue;
-      const int e = lane + 32 * i;
-      const unsigned long long key =
-          ((unsigned long long)mono_key(vals[e]) << 16) | (unsigned long long)(0xffff - e);
-      if (key > best) best = key;
-    }
+__device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const unsigned long long v = __shfl_xor_sync(MS_FULL, best, o);
-      if (v > best) best = v;
-    }
-    const int e = 0xffff - (int)(best & 0xffff);
-    if ((e & 31) == lane) taken |= 1u << (e >> 5);
-    if (lane == 0) out[r] = e;
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(MS_FULL, v, o);
+  return v;
+}
+
+// top-k of vals[0..E) (bf16 bit patterns, one warp): descending, exact ties
+// to the lower index. A candidate is the 32-bit key (value << 16 | ~index),
+// so one redux.sync per round finds the winner. Writes out[0..k).
+__device__ void warp_topk(const uint16_t* vals, int E, int k, int* out, int lane) {
+  constexpr int PER = MAX_E / 32;
+  uint32_t key[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    key[i] = (e < E) ? ((mono_key(vals[e]) << 16) | (uint32_t)(0xffff - e)) : 0u;
+  }
+  for (int r = 0; r < k; ++r) {
+    uint32_t best = 0u;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) best = max(best, key[i]);
+    const uint32_t w = __reduce_max_sync(MS_FULL, best);
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (key[i] == w) key[i] = 0u;          // keys are unique (they carry the index)
+    if (lane == 0) out[r] = 0xffff - (int)(w & 0xffffu);
   }
   __syncwarp();
 }
@@ -80,19 +85,13 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
           acc = fmaf(__uint_as_float(wa[q] & 0xffff0000u), __uint_as_float(xa[q] & 0xffff0000u), acc);
         }
       }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(MS_FULL, acc, o);
+      acc = warp_sum(acc);
       if (lane == 0) A.logits[(long long)t * rows + r] = acc + bias;
     }
   }
-  if (A.xfrag) {
-    const int G = d / 64;
-    const int tasks = T * G;
-    for (int i = blockIdx.x * RT_THREADS + threadIdx.x; i < tasks; i += gridDim.x * RT_THREADS) {
-      const int t = i / G, kg = i % G;
-      frag_write_group(A.x + (long long)t * d + kg * 64, A.xfrag, A.xsum, t, G, kg);
-    }
-  }
+  if (A.xfrag)
+    frag_write_rows(A.x, T, d, A.xfrag, A.xsum, blockIdx.x * RT_THREADS + threadIdx.x,
+                    gridDim.x * RT_THREADS);
 
   // ----------------------------------------------------- arrival: last CTA
   __shared__ int s_last;
@@ -117,6 +116,8 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
   __shared__ int s_slots[MAX_E];
   __shared__ int s_waits[MAX_E];
   __shared__ int s_cnt[MAX_E], s_run[MAX_E];
+  __shared__ int s_rank[MAX_E];
+  __shared__ int s_inds[SMALL_P];
   __shared__ int s_n_acq;
   __shared__ OpCtx s_op;
   __shared__ KeyCache s_kc;
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
   __syncthreads();
 
   const int kp = A.kp;
+  const bool small = T * k <= SMALL_P;
   for (int t = warp; t < T; t += RT_THREADS / 32) {
     const float* lg = A.logits + (long long)t * rows;
     uint16_t* vals = s_vals[warp];
@@ -143,45 +145,33 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(MS_FULL, lmax, o));
     __syncwarp();
+    float sc = 0.f;
     if (A.geo.model == 0) {
       // softmax(precise) over all experts, bf16 out (engine_v3.py:468)
-      float s = 0.f;
-      for (int e = lane; e < E; e += 32) s += expf(bf2f(vals[e]) - lmax);
-#pragma unroll
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(MS_FULL, s, o);
-      __syncwarp();
-      for (int e = lane; e < E; e += 32) vals[e] = f2bf(expf(bf2f(vals[e]) - lmax) / s);
+      float sum = 0.f;
+      for (int e = lane; e < E; e += 32) sum += expf(bf2f(vals[e]) - lmax);
+      sum = warp_sum(sum);
+      for (int e = lane; e < E; e += 32) vals[e] = f2bf(expf(bf2f(vals[e]) - lmax) / sum);
       __syncwarp();
       warp_topk(vals, E, k, sel, lane);
-      if (lane == 0) {
-        float p[32];
-        float ssum = 0.f;
-        for (int j = 0; j < k; ++j) { p[j] = bf2f(vals[sel[j]]); ssum += p[j]; }
-        const float den = bfr(ssum);
-        for (int j = 0; j < k; ++j) {
-          const float sc = A.geo.norm_topk ? bfr(p[j] / den) : p[j];
-          A.inds[t * k + j] = sel[j];
-          A.scores[t * k + j] = f2bf(sc);
-          A.scores_f[t * k + j] = sc;
-          atomicOr(&s_acq_mask[sel[j] >> 5], 1u << (sel[j] & 31));
-        }
-      }
+      // scores of the k selected, renormalised (engine_v3.py:469-472)
+      const float p = (lane < k) ? bf2f(vals[sel[lane]]) : 0.f;
+      const float den = bfr(warp_sum(p));
+      sc = A.geo.norm_topk ? bfr(p / den) : p;
     } else {
       // gpt-oss: top-k of the logits, softmax over the k (engine_120b.py:67-70)
       warp_topk(vals, E, k, sel, lane);
-      if (lane == 0) {
-        float m = -INFINITY;
-        for (int j = 0; j < k; ++j) m = fmaxf(m, bf2f(vals[sel[j]]));
-        float ex[32], s = 0.f;
-        for (int j = 0; j < k; ++j) { ex[j] = expf(bf2f(vals[sel[j]]) - m); s += ex[j]; }
-        for (int j = 0; j < k; ++j) {
-          const float sc = bfr(ex[j] / s);
-          A.inds[t * k + j] = sel[j];
-          A.scores[t * k + j] = f2bf(sc);
-          A.scores_f[t * k + j] = sc;
-          atomicOr(&s_acq_mask[sel[j] >> 5], 1u << (sel[j] & 31));
-        }
-      }
+      const float m = bf2f(vals[sel[0]]);     // descending: the first is the max
+      const float ex = (lane < k) ? expf(bf2f(vals[sel[lane]]) - m) : 0.f;
+      sc = bfr(ex / warp_sum(ex));
+    }
+    if (lane < k) {
+      const int e = sel[lane];
+      A.inds[t * k + lane] = e;
+      A.scores[t * k + lane] = f2bf(sc);
+      A.scores_f[t * k + lane] = sc;
+      if (small) s_inds[t * k + lane] = e;
+      atomicOr(&s_acq_mask[e >> 5], 1u << (e & 31));
     }
     __syncwarp();
     // speculation: top-(k*widen) of the target layer's raw logits
@@ -190,11 +180,9 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
       for (int e = lane; e < E; e += 32) vals[e] = f2bf(lg[(dd + 1) * E + e]);
       __syncwarp();
       warp_topk(vals, E, kp, sel, lane);
-      if (lane == 0) {
-        for (int j = 0; j < kp; ++j) {
-          atomicOr(&s_pred_mask[dd][sel[j] >> 5], 1u << (sel[j] & 31));
-          if (dd == 0 && A.pred_out) A.pred_out[t * kp + j] = sel[j];
-        }
+      for (int j = lane; j < kp; j += 32) {
+        atomicOr(&s_pred_mask[dd][sel[j] >> 5], 1u << (sel[j] & 31));
+        if (dd == 0 && A.pred_out) A.pred_out[t * kp + j] = sel[j];
       }
       __syncwarp();
     }
@@ -214,9 +202,10 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
       op_load(Tb, &s_op, lane);
       if (lane == 0) s_kc.n = 0;
       __syncwarp();
-      // one parallel load of every key's state, then ExpertPool.prefetch for
-      // each target layer and acquire of this layer (engine_v3.py:522-526,
-      // 548); np.unique makes both lists sorted and distinct
+      // register every key, load all their state in one round, then
+      // ExpertPool.prefetch for each target layer and acquire of this layer
+      // (engine_v3.py:522-526, 548); np.unique makes both lists sorted and
+      // distinct
       Req rp[MS_MAX_DEPTHS], ra;
       for (int dd = 0; dd < A.n_pred; ++dd) {
         rp[dd].ci = s_ci[dd];
@@ -224,16 +213,68 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
       }
       ra.ci = s_ci[MS_MAX_DEPTHS];
       kc_add(Tb, &s_kc, ra, A.layer, s_acq, n_acq, false, lane);
+      kc_load(Tb, &s_op, &s_kc, lane);
       for (int dd = 0; dd < A.n_pred; ++dd) warp_prefetch(Tb, &s_op, &s_kc, rp[dd], lane);
       warp_acquire(Tb, &s_op, &s_kc, ra, s_slots, s_waits, lane);
       op_store(Tb, &s_op, lane);
-    } else if (lane == 0) {
-      for (int i = 0; i < n_acq; ++i) s_slots[i] = -1;
+    } else {
+      for (int i = lane; i < n_acq; i += 32) s_slots[i] = -1;
+    }
+    __syncwarp();
+    if (A.do_groups && small) {
+      // pairs grouped by expert in one warp: everything is computed in
+      // shared memory first and written out once at the end
+      const int P = T * k;
+      for (int g = lane; g < n_acq; g += 32) {
+        s_rank[s_acq[g]] = g;
+        s_cnt[g] = 0;
+      }
+      __syncwarp();
+      for (int p = lane; p < P; p += 32) atomicAdd(&s_cnt[s_rank[s_inds[p]]], 1);
+      __syncwarp();
+      int run = 0;
+      for (int base = 0; base < n_acq; base += 32) {
+        const int g = base + lane;
+        const int cnt = (g < n_acq) ? s_cnt[g] : 0;
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(MS_FULL, incl, o);
+          if (lane >= o) incl += v;
+        }
+        if (g < n_acq) s_run[g] = run + incl - cnt;
+        run += __shfl_sync(MS_FULL, incl, 31);
+      }
+      __syncwarp();
+      for (int g = lane; g < n_acq; g += 32) s_waits[g] = s_run[g];   // group starts
+      for (int base = 0; base < P; base += 32) {
+        const int p = base + lane;
+        const int g = (p < P) ? s_rank[s_inds[p]] : -1;
+        const unsigned same = __match_any_sync(MS_FULL, g);
+        const int rank = __popc(same & ((1u << lane) - 1u));
+        __syncwarp();
+        if (g >= 0) {
+          s_sel[0][s_run[g] + rank] = p;         // stable: ascending pair order
+          if (rank == 0) s_run[g] += __popc(same);
+        }
+        __syncwarp();
+      }
+      for (int g = lane; g < n_acq; g += 32) {
+        A.grp.grp_start[g] = s_waits[g];
+        A.grp.grp_count[g] = s_cnt[g];
+        A.grp.grp_key[g] = s_acq[g];
+        A.grp.grp_slot[g] = s_slots[g];
+      }
+      for (int i = lane; i < P; i += 32) {
+        A.grp.grp_pairs[i] = s_sel[0][i];
+        if (A.pair_slot) A.pair_slot[i] = s_slots[s_rank[s_inds[i]]];
+      }
+      if (lane == 0) *A.grp.n_groups = n_acq;
     }
   }
   __syncthreads();
 
-  if (A.do_groups) {
+  if (A.do_groups && !small) {
     cta_build_groups(A.inds, T * k, s_acq, s_n_acq, A.grp, s_cnt, s_run,
                      [&](int g) { return s_slots[g]; });
     if (A.pair_slot)
@@ -261,6 +302,7 @@ __global__ void k_pool_op(DevTable Tb, PoolReq R, int* slots_out, int* op_status
   Req r;
   r.ci = s_ci;
   kc_add(Tb, &s_kc, r, R.layer, s_exp, R.n, true, lane);   // callers may repeat experts
+  kc_load(Tb, &s_op, &s_kc, lane);
   int st = 0;
   if (R.op == 0) {
     warp_prefetch(Tb, &s_op, &s_kc, r, lane);
@@ -301,9 +343,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_mlp_prep(MlpPrepArgs A) {
   __shared__ int s_uniq[MS_MLP_MAX_PAIRS];
   __shared__ int s_cnt[MS_MLP_MAX_PAIRS], s_run[MS_MLP_MAX_PAIRS];
   extern __shared__ unsigned s_mask[];
-  const int G = A.d_model / 64;
-  for (int i = threadIdx.x; i < A.T * G; i += RT_THREADS)
-    frag_write_group(A.x + (long long)(i / G) * A.d_model + (i % G) * 64, A.xfrag, A.xsum, i / G, G, i % G);
+  frag_write_rows(A.x, A.T, A.d_model, A.xfrag, A.xsum, threadIdx.x, RT_THREADS);
   // key n_slots collects out-of-range slots: its group reads nothing and
   // yields zeros, and the pool status records MS_E_INVALID
   const int nw = (A.n_slots + 1 + 31) / 32;
