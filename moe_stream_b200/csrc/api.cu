@@ -1,8 +1,10 @@
 // Host side of libmoestream: the C ABI declared in include/moestream.h.
 // Owns the slot arena, the device slot table, the mapped store and every
 // scratch buffer; launches the kernels of route.cu and expert.cu.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -90,6 +92,20 @@ struct ms_pool {
   int* d_opstatus = nullptr;
   int* h_pinned = nullptr;   // [MS_MAX_REQ + 1]
   int* mlp_keys = nullptr;     // sanitised slot keys of ms_expert_mlp
+  // decode / small batches: the scratch above holds narrow_tokens tokens
+  int narrow_tokens = 0;
+  // wide batches (prefill): router tiles, grouped tcgen05 GEMM
+  bool wide = false;            // scratch and tensor maps ready
+  int wide_min_pairs = 0;       // T*k from which ms_moe_block takes this path
+  WideArgs wa{};
+  long long p_pad = 0;          // rows of xperm / hbuf / ybuf
+  uint16_t* xperm = nullptr;
+  float* perm_score = nullptr;
+  int* inv = nullptr;
+  uint16_t* hbuf = nullptr;
+  uint16_t* ybuf = nullptr;
+  int nt0 = 0, nt1 = 0;         // column tiles of the two GEMMs
+  CUtensorMap tm_x{}, tm_h{}, tm_wg{}, tm_wu{}, tm_wd{};
   bool profile = false;
   std::vector<cudaEvent_t> prof_ev;   // [n_layers][4]
 };
@@ -155,6 +171,56 @@ Geo make_geo(const ms_geom& g) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Pair count from which ms_moe_block runs the grouped-GEMM path; calls above
+// MS_MLP_MAX_PAIRS pairs always do. MS_WIDE_MIN_PAIRS overrides it.
+int wide_threshold() {
+  const char* v = getenv("MS_WIDE_MIN_PAIRS");
+  if (v && *v) {
+    const long t = strtol(v, nullptr, 10);
+    if (t > 0) return (int)std::min<long>(t, 1L << 30);
+  }
+  return 1024;
+}
+
+// Scratch and tensor maps of the wide-batch path, when max_tokens reaches it.
+int setup_wide(ms_pool* p) {
+  const int E = p->geom.n_experts, D = p->geom.d_model, F = p->geom.d_ff;
+  p->wide_min_pairs = wide_threshold();
+  const long long P = p->max_pairs;
+  if (P < std::min<long long>(p->wide_min_pairs, MS_MLP_MAX_PAIRS + 1)) return MS_OK;
+  p->nt0 = gemm_col_tile(0, F);
+  p->nt1 = gemm_col_tile(1, D);
+  if (!p->nt0 || !p->nt1) return MS_OK;        // d_model / d_ff % 64 != 0 is rejected earlier
+  p->p_pad = (P + 127) / 128 * 128;
+  int rc;
+  WideArgs& w = p->wa;
+  w.max_tiles = (int)std::min<long long>((P + 127) / 128 + std::min<long long>(E, P) + 1, 65535);
+  if ((rc = palloc(p, &w.cnt_e, 256))) return rc;
+  if ((rc = palloc(p, &w.pmask, MS_MAX_DEPTHS * 8))) return rc;
+  if ((rc = palloc(p, &w.cursor, 256))) return rc;
+  if ((rc = palloc(p, &w.tiles, w.max_tiles))) return rc;
+  if ((rc = palloc(p, &w.n_tiles, 1))) return rc;
+  CK(cudaMemset(w.cnt_e, 0, sizeof(int) * 256));
+  CK(cudaMemset(w.pmask, 0, sizeof(unsigned) * MS_MAX_DEPTHS * 8));
+  CK(cudaMemset(w.cursor, 0, sizeof(int) * 256));
+  CK(cudaMemset(w.n_tiles, 0, sizeof(int)));
+  if ((rc = palloc(p, &p->xperm, p->p_pad * D))) return rc;
+  if ((rc = palloc(p, &p->perm_score, p->p_pad))) return rc;
+  if ((rc = palloc(p, &p->inv, P))) return rc;
+  if ((rc = palloc(p, &p->hbuf, p->p_pad * F))) return rc;
+  if ((rc = palloc(p, &p->ybuf, p->p_pad * D))) return rc;
+  const int64_t* o = &p->geom.comp_offset[0][0];
+  const int ns = p->cfg.n_slots;
+  const long long blob = p->geom.blob_bytes;
+  if (encode_act_map(&p->tm_x, p->xperm, D, p->p_pad) || encode_act_map(&p->tm_h, p->hbuf, F, p->p_pad) ||
+      encode_weight_map(&p->tm_wg, p->arena + o[0 * 4 + 0], D, F, ns, blob, p->nt0) ||
+      encode_weight_map(&p->tm_wu, p->arena + o[1 * 4 + 0], D, F, ns, blob, p->nt0) ||
+      encode_weight_map(&p->tm_wd, p->arena + o[2 * 4 + 0], F, D, ns, blob, p->nt1))
+    return fail(MS_E_CUDA, "cuTensorMapEncodeTiled failed for the grouped-GEMM operands");
+  p->wide = true;
+  return MS_OK;
+}
 
 }  // namespace
 
@@ -248,21 +314,24 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   c0.n_free = t.n_slots;
   CK(cudaMemcpy(t.ctr, &c0, sizeof(c0), cudaMemcpyHostToDevice));
 
-  // scratch for up to max_tokens
-  const long long T = cfg->max_tokens, P = p->max_pairs;
+  // scratch: routing results for up to max_tokens; the decode-path
+  // intermediates for up to narrow_tokens (MS_MLP_MAX_PAIRS pairs)
+  const long long P = p->max_pairs;
   const int E = geom->n_experts, D = geom->d_model, F = geom->d_ff;
-  if ((rc = palloc(p, &p->logits, T * E * (1 + cfg->n_depths)))) return bail(rc);
+  p->narrow_tokens = std::min(cfg->max_tokens, MS_MLP_MAX_PAIRS / geom->top_k);
+  const long long Tn = p->narrow_tokens, Pn = Tn * geom->top_k;
+  if ((rc = palloc(p, &p->logits, Tn * E * (1 + cfg->n_depths)))) return bail(rc);
   if ((rc = palloc(p, &p->ticket, 1))) return bail(rc);
   CK(cudaMemset(p->ticket, 0, sizeof(unsigned)));
   if ((rc = palloc(p, &p->inds, P))) return bail(rc);
   if ((rc = palloc(p, &p->scores, P))) return bail(rc);
   if ((rc = palloc(p, &p->scores_f, P))) return bail(rc);
   if ((rc = palloc(p, &p->pair_slot, P))) return bail(rc);
-  if ((rc = palloc(p, &p->xfrag, T * D))) return bail(rc);
-  if ((rc = palloc(p, &p->xsum, T * (D / 64) * 2))) return bail(rc);
-  if ((rc = palloc(p, &p->hfrag, P * F))) return bail(rc);
-  if ((rc = palloc(p, &p->hpart, P * (F / 16) * 2))) return bail(rc);
-  if ((rc = palloc(p, &p->ypart, P * D))) return bail(rc);
+  if ((rc = palloc(p, &p->xfrag, Tn * D))) return bail(rc);
+  if ((rc = palloc(p, &p->xsum, Tn * (D / 64) * 2))) return bail(rc);
+  if ((rc = palloc(p, &p->hfrag, Pn * F))) return bail(rc);
+  if ((rc = palloc(p, &p->hpart, Pn * (F / 16) * 2))) return bail(rc);
+  if ((rc = palloc(p, &p->ypart, Pn * D))) return bail(rc);
   if ((rc = palloc(p, &p->cnt, D / 16))) return bail(rc);
   CK(cudaMemset(p->cnt, 0, sizeof(unsigned) * (D / 16)));
   const long long key_range = std::max<long long>(E, cfg->n_slots + 1);
@@ -281,6 +350,7 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
       cudaSuccess)
     return bail(fail(MS_E_NOMEM, "cudaMallocHost failed"));
   (void)kp;
+  if ((rc = setup_wide(p))) return bail(rc);
   CK(cudaDeviceSynchronize());
   *out = p;
   return MS_OK;
@@ -463,7 +533,7 @@ int ms_pool_arena(ms_pool* p, void** base, size_t* bytes) {
 }
 
 static int route_common(ms_pool* p, int layer, const void* x, int T, cudaStream_t s, bool block,
-                        int32_t* inds_out, void* scores_out, int32_t* pred_out) {
+                        bool wide, int32_t* inds_out, void* scores_out, int32_t* pred_out) {
   if (layer < 0 || layer >= p->geom.n_layers) return fail(MS_E_INVALID, "layer %d out of range", layer);
   if (T <= 0 || T > p->cfg.max_tokens)
     return fail(MS_E_INVALID, "T=%d outside [1, max_tokens=%d]", T, p->cfg.max_tokens);
@@ -496,7 +566,7 @@ static int route_common(ms_pool* p, int layer, const void* x, int T, cudaStream_
   a.scores = scores_out ? static_cast<uint16_t*>(scores_out) : p->scores;
   a.scores_f = p->scores_f;
   a.pred_out = pred_out;
-  a.xfrag = block ? p->xfrag : nullptr;
+  a.xfrag = (block && !wide) ? p->xfrag : nullptr;
   a.xsum = p->xsum;
   a.do_pool = block ? 1 : 0;
   a.tab = p->tab;
@@ -504,12 +574,16 @@ static int route_common(ms_pool* p, int layer, const void* x, int T, cudaStream_
   a.do_groups = block ? 1 : 0;
   a.grp = p->grp;
   a.pair_slot = block ? p->pair_slot : nullptr;
+  CK(cudaSetDevice(p->device));
+  if (wide) {
+    CK(launch_route_wide(a, p->wa, s));
+    return MS_OK;
+  }
   const int rows = p->geom.n_experts * (1 + a.n_pred);
   int grid = (rows + 7) / 8;
   const int xt = block ? (T * (p->geom.d_model / 64) + 255) / 256 : 0;
   grid = std::max(grid, xt);
   grid = std::min(grid, p->sm_count * 4);
-  CK(cudaSetDevice(p->device));
   CK(launch_route_step(a, grid, s));
   return MS_OK;
 }
@@ -519,7 +593,10 @@ int ms_route(ms_pool* p, int layer, const void* x, int T, int32_t* inds, void* s
   if (!p) return fail(MS_E_INVALID, "NULL pool");
   if (!inds || !scores) return fail(MS_E_INVALID, "inds/scores are NULL");
   if (pred && p->cfg.n_depths == 0) return fail(MS_E_INVALID, "pred requested but no prefetch depth configured");
-  return route_common(p, layer, x, T, static_cast<cudaStream_t>(stream), false, inds, scores, pred);
+  // batches past the decode scratch are routed by the tiled router
+  const bool wide = T > p->narrow_tokens;
+  return route_common(p, layer, x, T, static_cast<cudaStream_t>(stream), false, wide, inds, scores,
+                      pred);
 }
 
 static ExpArgs exp_args(ms_pool* p, const void* x, int T, void* y, const float* scores) {
@@ -541,6 +618,57 @@ static ExpArgs exp_args(ms_pool* p, const void* x, int T, void* y, const float* 
   return e;
 }
 
+// Expert MLPs of a routed wide batch: pairs scattered into expert order,
+// the two grouped GEMMs, the weighted combine.
+static int wide_experts(ms_pool* p, const void* x, int T, void* y, cudaStream_t s) {
+  const int k = p->geom.top_k, P = T * k;
+  ScatterArgs sa{};
+  sa.x = static_cast<const uint16_t*>(x);
+  sa.T = T;
+  sa.k = k;
+  sa.d = p->geom.d_model;
+  sa.inds = p->inds;
+  sa.scores_f = p->scores_f;
+  sa.grp = p->grp;
+  sa.cursor = p->wa.cursor;
+  sa.xperm = p->xperm;
+  sa.perm_score = p->perm_score;
+  sa.inv = p->inv;
+  sa.pair_slot = p->pair_slot;
+  CK(launch_scatter(sa, std::min((P + 7) / 8, p->sm_count * 8), s));
+  GemmArgs g{};
+  g.model = p->geo.model;
+  g.arena = p->arena;
+  g.blob = p->geom.blob_bytes;
+  for (int a = 0; a < 3; ++a)
+    for (int b = 0; b < 4; ++b) g.off[a][b] = p->geom.comp_offset[a][b];
+  g.tiles = p->wa.tiles;
+  g.n_tiles = p->wa.n_tiles;
+  g.grp_slot = p->grp.grp_slot;
+  g.H = p->hbuf;
+  g.Y = p->ybuf;
+  g.perm_score = p->perm_score;
+  g.status = &p->tab.ctr->status;
+  const int tiles = (int)std::min<long long>(p->wa.max_tiles,
+                                             (P + 127) / 128 + std::min(P, p->geom.n_experts) + 1);
+  g.K = p->geom.d_model;
+  g.ld_out = p->geom.d_ff;
+  CK(launch_gemm(0, p->nt0, p->tm_x, p->tm_wg, p->tm_wu, g, p->geom.d_ff / p->nt0, tiles, s));
+  g.K = p->geom.d_ff;
+  g.ld_out = p->geom.d_model;
+  CK(launch_gemm(1, p->nt1, p->tm_h, p->tm_wd, p->tm_wd, g, p->geom.d_model / p->nt1, tiles, s));
+  CombineArgs c{};
+  c.Y = p->ybuf;
+  c.inv = p->inv;
+  c.y = static_cast<uint16_t*>(y);
+  c.T = T;
+  c.k = k;
+  c.d = p->geom.d_model;
+  const long long chunks = (long long)T * (c.d / 8);
+  CK(launch_combine(c, (int)std::min<long long>((chunks + 255) / 256, p->sm_count * 8), s));
+  return MS_OK;
+}
+
 int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* stream) {
   if (!p) return fail(MS_E_INVALID, "NULL pool");
   if (!y || !aligned16(y)) return fail(MS_E_INVALID, "y must be a 16-byte aligned device pointer");
@@ -557,13 +685,21 @@ int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* str
     if (cs == cudaStreamCaptureStatusActive) rec_flags = cudaEventRecordExternal;
     CK(cudaEventRecordWithFlags(ev[0], s, rec_flags));
   }
-  int rc = route_common(p, layer, x, T, s, true, nullptr, nullptr, nullptr);
+  const int k = p->geom.top_k;
+  const bool wide = p->wide && (T * k >= p->wide_min_pairs || T > p->narrow_tokens);
+  if (!wide && T > p->narrow_tokens)
+    return fail(MS_E_INVALID, "T=%d exceeds the %d tokens of the decode scratch", T, p->narrow_tokens);
+  int rc = route_common(p, layer, x, T, s, true, wide, nullptr, nullptr, nullptr);
   if (rc) return rc;
   if (ev) CK(cudaEventRecordWithFlags(ev[1], s, rec_flags));
   CK(launch_fill(fill_args(p), p->sm_count * 2, s));
   if (ev) CK(cudaEventRecordWithFlags(ev[2], s, rec_flags));
-  const int max_groups = std::min(T * p->geom.top_k, p->geom.n_experts);
-  CK(launch_expert(exp_args(p, x, T, y, p->scores_f), max_groups, s));
+  if (wide) {
+    if ((rc = wide_experts(p, x, T, y, s))) return rc;
+  } else {
+    const int max_groups = std::min(T * k, p->geom.n_experts);
+    CK(launch_expert(exp_args(p, x, T, y, p->scores_f), max_groups, s));
+  }
   if (ev) CK(cudaEventRecordWithFlags(ev[3], s, rec_flags));
   return MS_OK;
 }

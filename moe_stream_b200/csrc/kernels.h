@@ -1,6 +1,8 @@
 // Kernel argument structures and launchers (host <-> device boundary inside
 // libmoestream; not part of the public C ABI).
 #pragma once
+#include <cuda.h>   // CUtensorMap
+
 #include "ms_common.cuh"
 
 #ifndef MS_MAX_DEPTHS
@@ -82,7 +84,71 @@ struct ExpArgs {
   int* status;                // sticky pool status (bounded waits report here)
 };
 
+// ------------------------------------------------ wide batches (prefill)
+// A 128-row tile of the grouped GEMM: rows [row0, row0 + rows) of the
+// expert-ordered pair list, all routed to group g.
+struct GemmTile {
+  int g, row0, rows, pad;
+};
+
+struct WideArgs {
+  int* cnt_e;                 // [256] pairs per expert; zero between calls
+  unsigned* pmask;            // [MS_MAX_DEPTHS][8] predicted experts; zero between calls
+  int* cursor;                // [256] per-group scatter cursors (zeroed by the router)
+  GemmTile* tiles;            // [max_tiles]
+  int* n_tiles;
+  int max_tiles;
+};
+
+struct ScatterArgs {
+  const uint16_t* x;          // bf16 [T, d]
+  int T, k, d;
+  const int* inds;            // [T, k] experts
+  const float* scores_f;      // [T, k]
+  Groups grp;
+  int* cursor;
+  uint16_t* xperm;            // bf16 [P_pad, d], expert order, k-permuted columns
+  float* perm_score;          // [P_pad]
+  int* inv;                   // [T, k] pair -> row of xperm
+  int* pair_slot;             // [T, k] or null
+};
+
+struct GemmArgs {
+  int model;
+  const uint8_t* arena;
+  long long blob;
+  long long off[3][4];
+  int K;                      // reduction length: d_model (phase 0) or d_ff (phase 1)
+  const GemmTile* tiles;
+  const int* n_tiles;
+  const int* grp_slot;
+  uint16_t* H;                // phase 0 output, bf16 [P_pad, d_ff], k-permuted columns
+  uint16_t* Y;                // phase 1 output, bf16 [P_pad, d_model], score-weighted
+  int ld_out;
+  const float* perm_score;
+  int* status;
+};
+
+struct CombineArgs {
+  const uint16_t* Y;          // [P_pad, d]
+  const int* inv;             // [T, k]
+  uint16_t* y;                // bf16 [T, d]
+  int T, k, d;
+};
+
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s);
+cudaError_t launch_route_wide(const RouteArgs& a, const WideArgs& w, cudaStream_t s);
+cudaError_t launch_scatter(const ScatterArgs& a, int grid, cudaStream_t s);
+cudaError_t launch_gemm(int phase, int nt, const CUtensorMap& tA, const CUtensorMap& tW0,
+                        const CUtensorMap& tW1, const GemmArgs& a, int n_col_tiles, int max_tiles,
+                        cudaStream_t s);
+cudaError_t launch_combine(const CombineArgs& a, int grid, cudaStream_t s);
+// Tensor maps of the grouped GEMM. 0 on success.
+int encode_act_map(CUtensorMap* m, const void* base, int K, long long rows);
+int encode_weight_map(CUtensorMap* m, const void* base, int K, int rows_out, int n_slots,
+                      long long blob, int box_rows);
+// Widest column tile (a multiple of 16 up to 256 / 128) dividing n.
+int gemm_col_tile(int phase, int n);
 cudaError_t launch_pool_op(const DevTable& t, const PoolReq& r, int* slots_out, int* st,
                            cudaStream_t s);
 cudaError_t launch_fill(const FillArgs& f, int grid, cudaStream_t s);

@@ -57,6 +57,79 @@ __device__ void warp_topk(const uint16_t* vals, int E, int k, int* out, int lane
   __syncwarp();
 }
 
+// Routes one token from its fp32 logits lg[0..E) (one warp; vals/sel are the
+// warp's scratch). Leaves the selected experts in sel[0..k) and returns lane
+// j's score for j < k (0 elsewhere).
+__device__ __forceinline__ float route_token(const float* lg, const Geo& geo, uint16_t* vals, int* sel,
+                                             int lane) {
+  const int E = geo.n_experts, k = geo.top_k;
+  // logits rounded to bf16 as the Linear's output (engine_v3.py:468)
+  float lmax = -INFINITY;
+  for (int e = lane; e < E; e += 32) {
+    const uint16_t b = f2bf(lg[e]);
+    vals[e] = b;
+    lmax = fmaxf(lmax, bf2f(b));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(MS_FULL, lmax, o));
+  __syncwarp();
+  float sc = 0.f;
+  if (geo.model == 0) {
+    // softmax(precise) over all experts, bf16 out (engine_v3.py:468)
+    float sum = 0.f;
+    for (int e = lane; e < E; e += 32) sum += expf(bf2f(vals[e]) - lmax);
+    sum = warp_sum(sum);
+    for (int e = lane; e < E; e += 32) vals[e] = f2bf(expf(bf2f(vals[e]) - lmax) / sum);
+    __syncwarp();
+    warp_topk(vals, E, k, sel, lane);
+    // scores of the k selected, renormalised (engine_v3.py:469-472)
+    const float p = (lane < k) ? bf2f(vals[sel[lane]]) : 0.f;
+    const float den = bfr(warp_sum(p));
+    sc = geo.norm_topk ? bfr(p / den) : p;
+  } else {
+    // gpt-oss: top-k of the logits, softmax over the k (engine_120b.py:67-70)
+    warp_topk(vals, E, k, sel, lane);
+    const float m = bf2f(vals[sel[0]]);     // descending: the first is the max
+    const float ex = (lane < k) ? expf(bf2f(vals[sel[lane]]) - m) : 0.f;
+    sc = bfr(ex / warp_sum(ex));
+  }
+  return sc;
+}
+
+// Speculation for one token: top-(k*widen) of a target layer's raw logits
+// lg[0..E) into sel[0..kp) (engine_v3.py:476-483, 509-514).
+__device__ __forceinline__ void predict_token(const float* lg, int E, int kp, uint16_t* vals, int* sel,
+                                              int lane) {
+  for (int e = lane; e < E; e += 32) vals[e] = f2bf(lg[e]);
+  __syncwarp();
+  warp_topk(vals, E, kp, sel, lane);
+}
+
+// The slot-table step of one block call, by one warp: register every key,
+// load all their state in one round, then ExpertPool.prefetch for each
+// target layer and acquire of this layer (engine_v3.py:522-526, 548).
+// np.unique makes both lists sorted and distinct; so are s_pred / s_acq.
+__device__ __forceinline__ void warp_pool_step(const RouteArgs& A, int (*s_pred)[MAX_E],
+                                               const int* s_n_pred, const int* s_acq, int n_acq,
+                                               int* s_slots, int* s_waits, OpCtx* s_op, KeyCache* s_kc,
+                                               int (*s_ci)[MAX_E], int lane) {
+  const DevTable& Tb = A.tab;
+  op_load(Tb, s_op, lane);
+  if (lane == 0) s_kc->n = 0;
+  __syncwarp();
+  Req rp[MS_MAX_DEPTHS], ra;
+  for (int dd = 0; dd < A.n_pred; ++dd) {
+    rp[dd].ci = s_ci[dd];
+    kc_add(Tb, s_kc, rp[dd], A.pred_layer[dd], s_pred[dd], s_n_pred[dd], false, lane);
+  }
+  ra.ci = s_ci[MS_MAX_DEPTHS];
+  kc_add(Tb, s_kc, ra, A.layer, s_acq, n_acq, false, lane);
+  kc_load(Tb, s_op, s_kc, lane);
+  for (int dd = 0; dd < A.n_pred; ++dd) warp_prefetch(Tb, s_op, s_kc, rp[dd], lane);
+  warp_acquire(Tb, s_op, s_kc, ra, s_slots, s_waits, lane);
+  op_store(Tb, s_op, lane);
+}
+
 __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
   const int E = A.geo.n_experts, d = A.geo.d_model, T = A.T, k = A.geo.top_k;
   const int rows = E * (1 + A.n_pred);
@@ -135,36 +208,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
     const float* lg = A.logits + (long long)t * rows;
     uint16_t* vals = s_vals[warp];
     int* sel = s_sel[warp];
-    // logits rounded to bf16 as the Linear's output (engine_v3.py:468)
-    float lmax = -INFINITY;
-    for (int e = lane; e < E; e += 32) {
-      const uint16_t b = f2bf(lg[e]);
-      vals[e] = b;
-      lmax = fmaxf(lmax, bf2f(b));
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(MS_FULL, lmax, o));
-    __syncwarp();
-    float sc = 0.f;
-    if (A.geo.model == 0) {
-      // softmax(precise) over all experts, bf16 out (engine_v3.py:468)
-      float sum = 0.f;
-      for (int e = lane; e < E; e += 32) sum += expf(bf2f(vals[e]) - lmax);
-      sum = warp_sum(sum);
-      for (int e = lane; e < E; e += 32) vals[e] = f2bf(expf(bf2f(vals[e]) - lmax) / sum);
-      __syncwarp();
-      warp_topk(vals, E, k, sel, lane);
-      // scores of the k selected, renormalised (engine_v3.py:469-472)
-      const float p = (lane < k) ? bf2f(vals[sel[lane]]) : 0.f;
-      const float den = bfr(warp_sum(p));
-      sc = A.geo.norm_topk ? bfr(p / den) : p;
-    } else {
-      // gpt-oss: top-k of the logits, softmax over the k (engine_120b.py:67-70)
-      warp_topk(vals, E, k, sel, lane);
-      const float m = bf2f(vals[sel[0]]);     // descending: the first is the max
-      const float ex = (lane < k) ? expf(bf2f(vals[sel[lane]]) - m) : 0.f;
-      sc = bfr(ex / warp_sum(ex));
-    }
+    const float sc = route_token(lg, A.geo, vals, sel, lane);
     if (lane < k) {
       const int e = sel[lane];
       A.inds[t * k + lane] = e;
@@ -177,9 +221,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
     // speculation: top-(k*widen) of the target layer's raw logits
     // (engine_v3.py:476-483, 509-514)
     for (int dd = 0; dd < A.n_pred; ++dd) {
-      for (int e = lane; e < E; e += 32) vals[e] = f2bf(lg[(dd + 1) * E + e]);
-      __syncwarp();
-      warp_topk(vals, E, kp, sel, lane);
+      predict_token(lg + (dd + 1) * E, E, kp, vals, sel, lane);
       for (int j = lane; j < kp; j += 32) {
         atomicOr(&s_pred_mask[dd][sel[j] >> 5], 1u << (sel[j] & 31));
         if (dd == 0 && A.pred_out) A.pred_out[t * kp + j] = sel[j];
@@ -198,25 +240,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
     }
     __syncwarp();
     if (A.do_pool) {
-      const DevTable& Tb = A.tab;
-      op_load(Tb, &s_op, lane);
-      if (lane == 0) s_kc.n = 0;
-      __syncwarp();
-      // register every key, load all their state in one round, then
-      // ExpertPool.prefetch for each target layer and acquire of this layer
-      // (engine_v3.py:522-526, 548); np.unique makes both lists sorted and
-      // distinct
-      Req rp[MS_MAX_DEPTHS], ra;
-      for (int dd = 0; dd < A.n_pred; ++dd) {
-        rp[dd].ci = s_ci[dd];
-        kc_add(Tb, &s_kc, rp[dd], A.pred_layer[dd], s_pred[dd], s_n_pred[dd], false, lane);
-      }
-      ra.ci = s_ci[MS_MAX_DEPTHS];
-      kc_add(Tb, &s_kc, ra, A.layer, s_acq, n_acq, false, lane);
-      kc_load(Tb, &s_op, &s_kc, lane);
-      for (int dd = 0; dd < A.n_pred; ++dd) warp_prefetch(Tb, &s_op, &s_kc, rp[dd], lane);
-      warp_acquire(Tb, &s_op, &s_kc, ra, s_slots, s_waits, lane);
-      op_store(Tb, &s_op, lane);
+      warp_pool_step(A, s_pred, s_n_pred, s_acq, n_acq, s_slots, s_waits, &s_op, &s_kc, s_ci, lane);
     } else {
       for (int i = lane; i < n_acq; i += 32) s_slots[i] = -1;
     }
@@ -280,6 +304,219 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
     if (A.pair_slot)
       for (int p = threadIdx.x; p < T * k; p += RT_THREADS)
         A.pair_slot[p] = s_slots[A.grp.map[A.inds[p]]];
+  }
+  if (threadIdx.x == 0) *A.ticket = 0u;
+}
+
+// ------------------------------------------------------------ wide batches
+// K1 for prefill and large batches. Each CTA owns RW_TOK tokens and computes
+// every router row for them (this layer's and each prefetch target's) on the
+// tensor cores, so the per-token softmax / top-k follows in the same CTA from
+// shared memory; per-expert pair counts and predicted-expert masks are then
+// merged in global memory. The last CTA to arrive runs the slot-table step,
+// lays the groups out (ascending expert id, each a contiguous run of rows)
+// and cuts them into the 128-row tiles of the grouped GEMM.
+constexpr int RW_TOK = 32;
+
+__device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, const uint32_t* b) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__global__ void __launch_bounds__(RT_THREADS) k_route_wide(RouteArgs A, WideArgs W) {
+  extern __shared__ float s_lg[];   // [RW_TOK][rows] logits (+ bias)
+  const int E = A.geo.n_experts, d = A.geo.d_model, T = A.T, k = A.geo.top_k;
+  const int rows = E * (1 + A.n_pred);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * RW_TOK;
+  const int ntok = min(RW_TOK, T - t0);
+  const int g8 = lane >> 2, c4 = lane & 3;
+
+  __shared__ int s_hist[MAX_E];
+  __shared__ unsigned s_pm[MS_MAX_DEPTHS][MAX_E / 32];
+  __shared__ uint16_t s_vals[RT_THREADS / 32][MAX_E];
+  __shared__ int s_sel[RT_THREADS / 32][MAX_E];
+  for (int i = threadIdx.x; i < MAX_E; i += RT_THREADS) s_hist[i] = 0;
+  for (int i = threadIdx.x; i < MS_MAX_DEPTHS * (MAX_E / 32); i += RT_THREADS) (&s_pm[0][0])[i] = 0;
+
+  // ---- logits: mma.sync m16n8k16 over 16-row chunks of the router rows;
+  // fragment rows are read straight from global memory (L1/L2 resident).
+  const uint32_t* xr[2][2];
+#pragma unroll
+  for (int m = 0; m < 2; ++m)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int t = min(t0 + m * 16 + h * 8 + g8, T - 1);   // rows past T: computed, never used
+      xr[m][h] = reinterpret_cast<const uint32_t*>(A.x + (long long)t * d) + c4;
+    }
+  for (int rc = warp; rc * 16 < rows; rc += RT_THREADS / 32) {
+    const uint32_t* wr[2];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      const int r = min(rc * 16 + n * 8 + g8, rows - 1);
+      const int which = r / E, e = r % E;
+      wr[n] = reinterpret_cast<const uint32_t*>((which == 0 ? A.w_r : A.w_p[which - 1]) +
+                                                (long long)e * d) + c4;
+    }
+    float acc[2][2][4];
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[m][n][q] = 0.f;
+#pragma unroll 4
+    for (int kw = 0; kw < d / 2; kw += 8) {    // 16 bf16 = 8 words per step
+      uint32_t a[2][4], b[2][2];
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        a[m][0] = __ldg(xr[m][0] + kw);
+        a[m][1] = __ldg(xr[m][1] + kw);
+        a[m][2] = __ldg(xr[m][0] + kw + 4);
+        a[m][3] = __ldg(xr[m][1] + kw + 4);
+      }
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        b[n][0] = __ldg(wr[n] + kw);
+        b[n][1] = __ldg(wr[n] + kw + 4);
+      }
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int n = 0; n < 2; ++n) mma_bf16_16816(acc[m][n], a[m], b[n]);
+    }
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int r = rc * 16 + n * 8 + 2 * c4 + q;
+        if (r >= rows) continue;
+        const int which = r / E, e = r % E;
+        const uint16_t* b = which == 0 ? A.b_r : A.b_p[which - 1];
+        const float bias = b ? bf2f(b[e]) : 0.f;
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) s_lg[(m * 16 + h * 8 + g8) * rows + r] = acc[m][n][h * 2 + q] + bias;
+      }
+  }
+  __syncthreads();
+
+  // ---- per token: route, predictions
+  const int kp = A.kp;
+  for (int tt = warp; tt < ntok; tt += RT_THREADS / 32) {
+    const int t = t0 + tt;
+    const float* lg = s_lg + tt * rows;
+    const float sc = route_token(lg, A.geo, s_vals[warp], s_sel[warp], lane);
+    if (lane < k) {
+      const int e = s_sel[warp][lane];
+      A.inds[t * k + lane] = e;
+      A.scores[t * k + lane] = f2bf(sc);
+      A.scores_f[t * k + lane] = sc;
+      atomicAdd(&s_hist[e], 1);
+    }
+    __syncwarp();
+    for (int dd = 0; dd < A.n_pred; ++dd) {
+      predict_token(lg + (dd + 1) * E, E, kp, s_vals[warp], s_sel[warp], lane);
+      for (int j = lane; j < kp; j += 32) {
+        const int e = s_sel[warp][j];
+        atomicOr(&s_pm[dd][e >> 5], 1u << (e & 31));
+        if (dd == 0 && A.pred_out) A.pred_out[t * kp + j] = e;
+      }
+      __syncwarp();
+    }
+  }
+  if (!A.do_pool) return;                      // routing only (ms_route)
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += RT_THREADS)
+    if (s_hist[e]) atomicAdd(&W.cnt_e[e], s_hist[e]);
+  for (int i = threadIdx.x; i < A.n_pred * (MAX_E / 32); i += RT_THREADS)
+    if ((&s_pm[0][0])[i]) atomicOr(&W.pmask[i], (&s_pm[0][0])[i]);
+
+  // ---- arrival: the last CTA goes on
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(A.ticket, 1u) == gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  __shared__ int s_cnt[MAX_E], s_acq[MAX_E], s_slots[MAX_E], s_waits[MAX_E];
+  __shared__ int s_pred[MS_MAX_DEPTHS][MAX_E];
+  __shared__ int s_n_pred[MS_MAX_DEPTHS];
+  __shared__ unsigned s_am[MAX_E / 32];
+  __shared__ OpCtx s_op;
+  __shared__ KeyCache s_kc;
+  __shared__ int s_ci[MS_MAX_DEPTHS + 1][MAX_E];
+  for (int e = threadIdx.x; e < MAX_E; e += RT_THREADS) {
+    s_cnt[e] = e < E ? __ldcg(&W.cnt_e[e]) : 0;
+    if (e < E) W.cnt_e[e] = 0;
+  }
+  for (int i = threadIdx.x; i < MS_MAX_DEPTHS * (MAX_E / 32); i += RT_THREADS) {
+    (&s_pm[0][0])[i] = __ldcg(&W.pmask[i]);
+    W.pmask[i] = 0u;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    for (int base = 0; base < MAX_E; base += 32) {
+      const unsigned bits = __ballot_sync(MS_FULL, s_cnt[base + lane] > 0);
+      if (lane == 0) s_am[base >> 5] = bits;
+    }
+    __syncwarp();
+    const int nw = (E + 31) / 32;
+    const int n_acq = warp_mask_to_list(s_am, nw, s_acq, lane);
+    for (int dd = 0; dd < A.n_pred; ++dd) {
+      const int n = warp_mask_to_list(s_pm[dd], nw, s_pred[dd], lane);
+      if (lane == 0) s_n_pred[dd] = n;
+    }
+    __syncwarp();
+    warp_pool_step(A, s_pred, s_n_pred, s_acq, n_acq, s_slots, s_waits, &s_op, &s_kc, s_ci, lane);
+    __syncwarp();
+    // groups in ascending expert order, and their 128-row tiles
+    int run = 0, trun = 0;
+    for (int base = 0; base < n_acq; base += 32) {
+      const int gi = base + lane;
+      const int e = gi < n_acq ? s_acq[gi] : 0;
+      const int cnt = gi < n_acq ? s_cnt[e] : 0;
+      const int nt = (cnt + 127) >> 7;
+      int ic = cnt, itl = nt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(MS_FULL, ic, o);
+        const int u = __shfl_up_sync(MS_FULL, itl, o);
+        if (lane >= o) {
+          ic += v;
+          itl += u;
+        }
+      }
+      if (gi < n_acq) {
+        const int start = run + ic - cnt;
+        A.grp.grp_start[gi] = start;
+        A.grp.grp_count[gi] = cnt;
+        A.grp.grp_key[gi] = e;
+        A.grp.grp_slot[gi] = s_slots[gi];
+        A.grp.map[e] = gi;
+        W.cursor[gi] = 0;
+        const int first = trun + itl - nt;
+        for (int j = 0; j < nt && first + j < W.max_tiles; ++j) {
+          GemmTile tl;
+          tl.g = gi;
+          tl.row0 = start + j * 128;
+          tl.rows = min(128, cnt - j * 128);
+          tl.pad = 0;
+          W.tiles[first + j] = tl;
+        }
+      }
+      run += __shfl_sync(MS_FULL, ic, 31);
+      trun += __shfl_sync(MS_FULL, itl, 31);
+    }
+    if (lane == 0) {
+      *A.grp.n_groups = n_acq;
+      *W.n_tiles = min(trun, W.max_tiles);
+    }
   }
   if (threadIdx.x == 0) *A.ticket = 0u;
 }
@@ -373,6 +610,15 @@ __global__ void __launch_bounds__(RT_THREADS) k_mlp_prep(MlpPrepArgs A) {
 // ----------------------------------------------------------------- launchers
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s) {
   k_route_step<<<grid, RT_THREADS, 0, s>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_route_wide(const RouteArgs& a, const WideArgs& w, cudaStream_t s) {
+  const int rows = a.geo.n_experts * (1 + a.n_pred);
+  const size_t smem = (size_t)RW_TOK * rows * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(k_route_wide, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  k_route_wide<<<(a.T + RW_TOK - 1) / RW_TOK, RT_THREADS, smem, s>>>(a, w);
   return cudaGetLastError();
 }
 cudaError_t launch_pool_op(const DevTable& t, const PoolReq& r, int* slots_out, int* st,

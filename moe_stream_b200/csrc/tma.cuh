@@ -44,13 +44,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned phase) {
   return ok != 0;
 }
 
-// Bounded wait for phase `phase` of `bar`. Returns false (and sets *status
-// to MS_E_TIMEOUT once) if the limit ran out.
+// Wall-clock limit of one mbarrier wait (ns), checked on %globaltimer.
+constexpr unsigned long long MBAR_WAIT_NS = 1000000000ull;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for phase `phase` of `bar`: at most MBAR_SPIN_LIMIT polls
+// and MBAR_WAIT_NS of wall time. Returns false (and sets *status to
+// MS_E_TIMEOUT once) if either limit ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, int* status) {
-  for (unsigned i = 0; i < MBAR_SPIN_LIMIT; ++i)
+  if (mbar_try_wait(bar, phase)) return true;
+  const unsigned long long t0 = global_ns();
+  for (unsigned i = 0; i < MBAR_SPIN_LIMIT; ++i) {
     if (mbar_try_wait(bar, phase)) return true;
+    if ((i & 255u) == 255u && global_ns() - t0 > MBAR_WAIT_NS) break;
+  }
   if (status) atomicCAS(status, 0, -4);
   return false;
+}
+
+// True once any wait of this call chain has timed out: later CTAs then skip
+// their work instead of waiting out the same limit again.
+__device__ __forceinline__ bool timed_out(const int* status) {
+  return status && *reinterpret_cast<const volatile int*>(status) == -4;
 }
 
 __device__ __forceinline__ void fence_barrier_init() {
