@@ -104,7 +104,6 @@ struct ms_pool {
   int* inv = nullptr;
   uint16_t* hbuf = nullptr;
   uint16_t* ybuf = nullptr;
-  int nt0 = 0, nt1 = 0;         // column tiles of the two GEMMs
   CUtensorMap tm_x{}, tm_h{}, tm_wg{}, tm_wu{}, tm_wd{};
   bool profile = false;
   std::vector<cudaEvent_t> prof_ev;   // [n_layers][4]
@@ -189,13 +188,12 @@ int setup_wide(ms_pool* p) {
   p->wide_min_pairs = wide_threshold();
   const long long P = p->max_pairs;
   if (P < std::min<long long>(p->wide_min_pairs, MS_MLP_MAX_PAIRS + 1)) return MS_OK;
-  p->nt0 = gemm_col_tile(0, F);
-  p->nt1 = gemm_col_tile(1, D);
-  if (!p->nt0 || !p->nt1) return MS_OK;        // d_model / d_ff % 64 != 0 is rejected earlier
-  p->p_pad = (P + 127) / 128 * 128;
+  // rows of the GEMM operands: whole 256-row boxes, so no TMA box is taller
+  // than its tensor
+  p->p_pad = (P + GEMM_TILE_ROWS - 1) / GEMM_TILE_ROWS * GEMM_TILE_ROWS;
   int rc;
   WideArgs& w = p->wa;
-  w.max_tiles = (int)std::min<long long>((P + 127) / 128 + std::min<long long>(E, P) + 1, 65535);
+  w.max_tiles = (int)std::min<long long>(P / GEMM_TILE_ROWS + std::min<long long>(E, P) + 1, 65535);
   if ((rc = palloc(p, &w.cnt_e, 256))) return rc;
   if ((rc = palloc(p, &w.pmask, MS_MAX_DEPTHS * 8))) return rc;
   if ((rc = palloc(p, &w.cursor, 256))) return rc;
@@ -214,9 +212,9 @@ int setup_wide(ms_pool* p) {
   const int ns = p->cfg.n_slots;
   const long long blob = p->geom.blob_bytes;
   if (encode_act_map(&p->tm_x, p->xperm, D, p->p_pad) || encode_act_map(&p->tm_h, p->hbuf, F, p->p_pad) ||
-      encode_weight_map(&p->tm_wg, p->arena + o[0 * 4 + 0], D, F, ns, blob, p->nt0) ||
-      encode_weight_map(&p->tm_wu, p->arena + o[1 * 4 + 0], D, F, ns, blob, p->nt0) ||
-      encode_weight_map(&p->tm_wd, p->arena + o[2 * 4 + 0], F, D, ns, blob, p->nt1))
+      encode_weight_map(&p->tm_wg, p->arena + o[0 * 4 + 0], D, F, ns, blob, 64) ||
+      encode_weight_map(&p->tm_wu, p->arena + o[1 * 4 + 0], D, F, ns, blob, 64) ||
+      encode_weight_map(&p->tm_wd, p->arena + o[2 * 4 + 0], F, D, ns, blob, 128))
     return fail(MS_E_CUDA, "cuTensorMapEncodeTiled failed for the grouped-GEMM operands");
   p->wide = true;
   return MS_OK;
@@ -649,14 +647,16 @@ static int wide_experts(ms_pool* p, const void* x, int T, void* y, cudaStream_t 
   g.Y = p->ybuf;
   g.perm_score = p->perm_score;
   g.status = &p->tab.ctr->status;
-  const int tiles = (int)std::min<long long>(p->wa.max_tiles,
-                                             (P + 127) / 128 + std::min(P, p->geom.n_experts) + 1);
+  const int tiles = (int)std::min<long long>(
+      p->wa.max_tiles, P / GEMM_TILE_ROWS + std::min(P, p->geom.n_experts) + 1);
   g.K = p->geom.d_model;
+  g.n_out = p->geom.d_ff;
   g.ld_out = p->geom.d_ff;
-  CK(launch_gemm(0, p->nt0, p->tm_x, p->tm_wg, p->tm_wu, g, p->geom.d_ff / p->nt0, tiles, s));
+  CK(launch_gemm(0, p->tm_x, p->tm_wg, p->tm_wu, g, p->geom.d_ff / 64, tiles, s));
   g.K = p->geom.d_ff;
+  g.n_out = p->geom.d_model;
   g.ld_out = p->geom.d_model;
-  CK(launch_gemm(1, p->nt1, p->tm_h, p->tm_wd, p->tm_wd, g, p->geom.d_model / p->nt1, tiles, s));
+  CK(launch_gemm(1, p->tm_h, p->tm_wd, p->tm_wd, g, (p->geom.d_model + 127) / 128, tiles, s));
   CombineArgs c{};
   c.Y = p->ybuf;
   c.inv = p->inv;

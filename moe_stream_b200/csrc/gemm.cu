@@ -8,32 +8,38 @@
 // enough to flip bf16 output roundings wherever |y| is large. Here every
 // weight is carried exactly as the sum of two fp16 values, hi = fp16(w) and
 // lo = w - hi (a few bits, exact for any scale above ~1e-5), and each K step
-// runs two MMAs, A*hi and A*lo, into the same fp32 accumulator. The
+// runs two MMAs, hi*X and lo*X, into the same fp32 accumulator. The
 // activations enter as fp16, which holds every bf16 value of magnitude
 // 2^-17 .. 65504 exactly. The products are therefore exact and only the fp32
 // accumulation order differs from the reference.
 //
+// Shape. Weights are the MMA's A operand and live in tensor memory: each
+// dequantising thread owns one weight row = one TMEM lane and writes its hi
+// and lo halves there with tcgen05.st, so the dequantised operand never
+// touches shared memory. Tokens are the B operand: up to 256 rows of X per
+// CTA, TMA-loaded into shared memory (128-byte swizzle). D[weight row, token]
+// accumulates in TMEM. Each dequantised weight thus serves up to 256 tokens.
+//
 //   k_scatter  token rows copied into expert order (X_perm, one fp16 row
 //              per token/expert pair), each 8-column block stored in the
 //              order (0,4,1,5,2,6,3,7) that the nibble unpacking gives the
-//              weights, so A and B agree on k; with the per-row score and
-//              the pair -> row map. The groups and their 128-row tiles come
-//              from the wide router (route.cu).
-//   k_gemm<0>  H = SwiGLU(X_perm W_gate^T, X_perm W_up^T) per (M tile, 128/96
-//              features): B = [gate rows ; up rows] dequantised in shared
-//              memory, tcgen05.mma (M=128, N=256/192, K=16) x {hi, lo} per
-//              16 columns, fp32 accumulator in TMEM, SwiGLU in the epilogue,
-//              h written as fp16 in the same column order.
-//   k_gemm<1>  Y = H W_down^T (+bias), times the routing score, per (M tile,
-//              256/192 features).
+//              weights, so both operands agree on k; with the per-row score
+//              and the pair -> row map. The groups and their 256-row tiles
+//              come from the wide router (route.cu).
+//   k_gemm<0>  per (64 features, token tile): A = [64 gate rows; 64 up rows],
+//              D lanes 0-63 gate, 64-127 up; SwiGLU in the epilogue; h
+//              written as fp16 in the k-permuted column order.
+//   k_gemm<1>  per (128 output features, token tile): A = down rows;
+//              Y = bf16(acc) (+bias), times the routing score.
 //   k_combine  y[t] = sum_j Y[inv(t, j)] in a fixed j order.
 //
 // One CTA = 12 warps: warp 0 issues the TMA loads, warp 1 issues the MMAs,
-// warp 2 owns the TMEM allocation, warps 4-11 dequantise each K tile's
-// weights and then run the epilogue. Three mbarrier rings hand the tiles
-// over: activations + codes (TMA -> dequant/MMA, 4 deep), dequantised
-// operands (dequant -> MMA, 2 deep), and the accumulator (MMA -> epilogue).
-// Every wait is bounded and reports MS_E_TIMEOUT instead of hanging.
+// warp 2 owns the TMEM allocation, warps 4-11 dequantise (two warps per
+// TMEM lane quarter, each taking half of a K tile's columns) and then run
+// the epilogue. mbarrier rings hand the tiles over: tokens + codes (TMA ->
+// dequant/MMA, 4 deep), weights in TMEM (dequant -> MMA, 2 deep), and the
+// accumulator (MMA -> epilogue). Every wait is bounded and reports
+// MS_E_TIMEOUT instead of hanging.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
@@ -45,16 +51,18 @@
 namespace ms {
 
 constexpr int GM_THREADS = 384;
-constexpr int GM_AP_STAGES = 4;               // activation + code tiles
-constexpr int GM_B_STAGES = 2;                // dequantised operand tiles
-constexpr int GM_A_BYTES = 128 * 128;         // 128 rows x 64 fp16
-constexpr int GM_P_BYTES = 256 * 32;          // up to 256 rows x 64 nibbles
-constexpr int GM_B_BYTES = 256 * 128;         // up to 256 rows x 64 fp16 (one of hi / lo)
-constexpr int GM_AP_BYTES = GM_A_BYTES + GM_P_BYTES;                   // 24 KB
-constexpr int GM_OFF_B = GM_AP_STAGES * GM_AP_BYTES;                   // 96 KB
-constexpr int GM_OFF_BAR = GM_OFF_B + GM_B_STAGES * 2 * GM_B_BYTES;    // 224 KB
+constexpr int GM_STAGES = 4;                  // token + code tiles
+constexpr int GM_A_STAGES = 2;                // weight tiles in TMEM
+constexpr int GM_TOK = GEMM_TILE_ROWS;        // tokens per CTA (MMA N, at most)
+constexpr int GM_X_BYTES = GM_TOK * 128;      // 256 tokens x 64 fp16
+constexpr int GM_P_BYTES = 128 * 32;          // 128 weight rows x 64 nibbles
+constexpr int GM_OFF_P = GM_STAGES * GM_X_BYTES;                   // 128 KB
+constexpr int GM_OFF_BAR = GM_OFF_P + GM_STAGES * GM_P_BYTES;      // 144 KB
 constexpr int GM_SMEM = GM_OFF_BAR + 256 + 1024;
-static_assert(GM_AP_BYTES % 1024 == 0 && GM_B_BYTES % 1024 == 0, "1 KB aligned tiles");
+// TMEM columns: accumulator [0, 256), weight stage s at 256 + 64 s (hi, then lo)
+constexpr uint32_t TM_ACC = 0, TM_A = 256, TM_COLS = 512;
+static_assert(GM_X_BYTES % 1024 == 0 && GM_P_BYTES % 1024 == 0, "1 KB aligned tiles");
+static_assert(64 * GM_TOK * 4 <= GM_OFF_P, "the up-projection staging fits in the token ring");
 
 // ------------------------------------------------------------- PTX helpers
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y,
@@ -110,19 +118,37 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* p) {
 }
 
 // kind::f16 instruction descriptor: fp16 A and B (both K-major), f32 D,
-// M=128, N.
+// M=128, N (a multiple of 16, at most 256).
 __host__ __device__ constexpr uint32_t idesc_f16(int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((128u >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t idesc, uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem]^T (A: M=128 rows x K=16, one row per lane).
+__device__ __forceinline__ void mma_ts_f16(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
   const uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3));
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3));
 }
+
+// 16 consecutive columns of this thread's lane <- v[0..16)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// barrier 1 among the 256 epilogue threads (warps 4-11)
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
@@ -200,57 +226,57 @@ __global__ void __launch_bounds__(256) k_scatter(ScatterArgs a) {
 }
 
 // ------------------------------------------------------------------ K4
-// PHASE 0: N = 2*NT (gate rows then up rows); PHASE 1: N = NT (down rows).
-template <int PHASE, int NT>
+// PHASE 0: blockIdx.x = 64-feature tile of d_ff (A rows: gate f0..f0+63,
+// then up f0..f0+63). PHASE 1: 128-feature tile of d_model (down rows).
+template <int PHASE>
 __global__ void __launch_bounds__(GM_THREADS, 1)
-    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW0,
+    k_gemm(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW0,
            const __grid_constant__ CUtensorMap tmW1, GemmArgs a) {
-  constexpr int N = PHASE == 0 ? 2 * NT : NT;
-  static_assert(N % 16 == 0 && N <= 256, "MMA N");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.y, nt = blockIdx.x;
+  const int tile = blockIdx.y;
   if (tile >= *a.n_tiles || timed_out(a.status)) return;   // uniform: before any barrier
   const GemmTile t = a.tiles[tile];
   const int slot = a.grp_slot[t.g];
   const int KT = a.K / 64, G = a.K / 64;
+  const int n_out = a.n_out;                   // rows of this projection's output
+  const int f0 = blockIdx.x * (PHASE == 0 ? 64 : 128);
+  const int ntok = (t.rows + 15) & ~15;        // MMA N: the tile's rows, rounded up to 16
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + GM_OFF_BAR);
-  uint64_t* full = bars;                                   // [AP]  TMA landed
-  uint64_t* empty_ap = bars + GM_AP_STAGES;                // [AP]  MMA done with A (and P)
-  uint64_t* deq = bars + 2 * GM_AP_STAGES;                 // [B]   operands written
-  uint64_t* empty_b = deq + GM_B_STAGES;                   // [B]   MMA done with them
-  uint64_t* accf = empty_b + GM_B_STAGES;                  // accumulator complete
+  uint64_t* full = bars;                                   // [S]  TMA landed
+  uint64_t* empty_x = bars + GM_STAGES;                    // [S]  MMA done with X (and P)
+  uint64_t* deq = bars + 2 * GM_STAGES;                    // [A]  weights in TMEM
+  uint64_t* empty_a = deq + GM_A_STAGES;                   // [A]  MMA done with them
+  uint64_t* accf = empty_a + GM_A_STAGES;                  // accumulator complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
-  auto sA = [&](int s) { return smem + s * GM_AP_BYTES; };
-  auto sP = [&](int s) { return smem + s * GM_AP_BYTES + GM_A_BYTES; };
-  auto sBh = [&](int s) { return smem + GM_OFF_B + s * 2 * GM_B_BYTES; };
-  auto sBl = [&](int s) { return smem + GM_OFF_B + s * 2 * GM_B_BYTES + GM_B_BYTES; };
+  auto sX = [&](int s) { return smem + s * GM_X_BYTES; };
+  auto sP = [&](int s) { return smem + GM_OFF_P + s * GM_P_BYTES; };
 
   if (slot < 0) {                              // exhausted pool: this tile contributes zeros
-    const int cols = PHASE == 0 ? NT : N;
+    const int cols = PHASE == 0 ? 64 : min(128, n_out - f0);
+    uint16_t* out = PHASE == 0 ? a.H : a.Y;
     for (int i = threadIdx.x; i < t.rows * cols; i += GM_THREADS) {
       const int m = i / cols, c = i % cols;
-      if (PHASE == 0) a.H[(long long)(t.row0 + m) * a.ld_out + nt * NT + c] = 0;
-      else a.Y[(long long)(t.row0 + m) * a.ld_out + nt * NT + c] = 0;
+      out[(long long)(t.row0 + m) * a.ld_out + f0 + c] = 0;
     }
     return;
   }
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GM_AP_STAGES; ++s) {
+    for (int s = 0; s < GM_STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty_ap[s], 1);
+      mbar_init(&empty_x[s], 1);
     }
-    for (int s = 0; s < GM_B_STAGES; ++s) {
+    for (int s = 0; s < GM_A_STAGES; ++s) {
       mbar_init(&deq[s], 8);
-      mbar_init(&empty_b[s], 1);
+      mbar_init(&empty_a[s], 1);
     }
     mbar_init(accf, 1);
     fence_barrier_init();
   }
-  if (warp == 2) tmem_alloc(tmem_slot, 256);
+  if (warp == 2) tmem_alloc(tmem_slot, TM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -260,75 +286,86 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {                           // ---- TMA producer
       for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % GM_AP_STAGES;
-        if (kt >= GM_AP_STAGES &&
-            !mbar_wait(&empty_ap[s], ((kt / GM_AP_STAGES) - 1) & 1, a.status)) {
+        const int s = kt % GM_STAGES;
+        if (kt >= GM_STAGES && !mbar_wait(&empty_x[s], ((kt / GM_STAGES) - 1) & 1, a.status)) {
           ok = false;
           break;
         }
-        mbar_expect_tx(&full[s], GM_A_BYTES + N * 32);
-        tma_load_2d(sA(s), &tmA, kt * 64, t.row0, &full[s]);
-        tma_load_3d(sP(s), &tmW0, kt * 32, nt * NT, slot, &full[s]);
-        if (PHASE == 0) tma_load_3d(sP(s) + NT * 32, &tmW1, kt * 32, nt * NT, slot, &full[s]);
+        mbar_expect_tx(&full[s], GM_X_BYTES + GM_P_BYTES);
+        tma_load_2d(sX(s), &tmX, kt * 64, t.row0, &full[s]);
+        if (PHASE == 0) {
+          tma_load_3d(sP(s), &tmW0, kt * 32, f0, slot, &full[s]);
+          tma_load_3d(sP(s) + 64 * 32, &tmW1, kt * 32, f0, slot, &full[s]);
+        } else {
+          tma_load_3d(sP(s), &tmW0, kt * 32, f0, slot, &full[s]);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {                           // ---- MMA issuer
-      constexpr uint32_t idesc = idesc_f16(N);
+      const uint32_t idesc = idesc_f16(ntok);
       for (int kt = 0; kt < KT; ++kt) {
-        const int sa = kt % GM_AP_STAGES, sb = kt % GM_B_STAGES;
-        if (!mbar_wait(&deq[sb], (kt / GM_B_STAGES) & 1, a.status)) {
+        const int sx = kt % GM_STAGES, sa = kt % GM_A_STAGES;
+        if (!mbar_wait(&deq[sa], (kt / GM_A_STAGES) & 1, a.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t ad = sw128_desc(sA(sa)), bh = sw128_desc(sBh(sb)), bl = sw128_desc(sBl(sb));
+        const uint64_t bd = sw128_desc(sX(sx));
+        const uint32_t ahi = tmem + TM_A + sa * 64, alo = ahi + 32;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {          // K = 16 per MMA: +32 bytes in the atom
-          mma_f16(tmem, ad + 2 * j, bh + 2 * j, idesc, (kt | j) != 0);
-          mma_f16(tmem, ad + 2 * j, bl + 2 * j, idesc, 1u);
+        for (int j = 0; j < 4; ++j) {          // K = 16 per MMA: 8 TMEM columns, 32 smem bytes
+          mma_ts_f16(tmem + TM_ACC, ahi + 8 * j, bd + 2 * j, idesc, (kt | j) != 0);
+          mma_ts_f16(tmem + TM_ACC, alo + 8 * j, bd + 2 * j, idesc, 1u);
         }
-        mma_commit(&empty_b[sb]);
-        mma_commit(&empty_ap[sa]);
+        mma_commit(&empty_a[sa]);
+        mma_commit(&empty_x[sx]);
       }
       mma_commit(accf);
     }
   } else if (warp >= 4) {
-    // ---- dequantise: one weight row per thread, into hi and lo
-    const int r = threadIdx.x - 128;
-    const int proj = PHASE == 0 ? (r < NT ? 0 : 1) : 2;
-    const int orow = nt * NT + (PHASE == 0 ? (r % NT) : r);
+    // ---- dequantise: TMEM lane r = weight row r; this warp takes columns
+    // [16*half, 16*half + 16) of each K tile (32 codes)
+    const int quarter = warp & 3, half = (warp - 4) >> 2;
+    const int r = quarter * 32 + lane;
+    int proj, orow;
+    if (PHASE == 0) {
+      proj = r < 64 ? 0 : 1;
+      orow = f0 + (r & 63);
+    } else {
+      proj = 2;
+      orow = f0 + r;
+    }
+    const bool active = orow < n_out;
     const uint8_t* blob = a.arena + (long long)slot * a.blob;
     const uint16_t* Sc = reinterpret_cast<const uint16_t*>(blob + a.off[proj][1]) + (long long)orow * G;
     const uint16_t* Bi = reinterpret_cast<const uint16_t*>(blob + a.off[proj][2]) + (long long)orow * G;
-    const bool active = r < N;
     uint16_t s_next = active ? Sc[0] : 0, b_next = active ? Bi[0] : 0;
     const __half2 h1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     for (int kt = 0; kt < KT; ++kt) {
-      const int sa = kt % GM_AP_STAGES, sb = kt % GM_B_STAGES;
+      const int sx = kt % GM_STAGES, sa = kt % GM_A_STAGES;
       const float sc = bf2f(s_next), bi = bf2f(b_next);
       if (active && kt + 1 < KT) {
         s_next = Sc[kt + 1];
         b_next = Bi[kt + 1];
       }
       // every lane waits; the warp goes on only if all of them saw the stage
-      bool got = mbar_wait(&full[sa], (kt / GM_AP_STAGES) & 1, a.status);
-      if (got && kt >= GM_B_STAGES)
-        got = mbar_wait(&empty_b[sb], ((kt / GM_B_STAGES) - 1) & 1, a.status);
+      bool got = mbar_wait(&full[sx], (kt / GM_STAGES) & 1, a.status);
+      if (got && kt >= GM_A_STAGES)
+        got = mbar_wait(&empty_a[sa], ((kt / GM_A_STAGES) - 1) & 1, a.status);
       if (!__all_sync(MS_FULL, got)) {
         ok = false;
         break;
       }
+      tc_fence_after();
+      uint32_t wh[16], wl[16];
       if (active) {
-        const uint4* pk = reinterpret_cast<const uint4*>(sP(sa) + r * 32);
-        const uint4 p0 = pk[0], p1 = pk[1];
-        const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-        uint8_t* rh = sBh(sb) + r * 128;
-        uint8_t* rl = sBl(sb) + r * 128;
+        const uint4 pw = *reinterpret_cast<const uint4*>(sP(sx) + r * 32 + half * 16);
+        const uint32_t words[4] = {pw.x, pw.y, pw.z, pw.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
           const uint32_t u = words[i];
-          uint32_t wh[4], wl[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             // {q_j, q_j+4} exactly, as fp16 1024+q minus 1024
@@ -337,78 +374,83 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             const float w0 = fmaf(sc, q.x, bi), w1 = fmaf(sc, q.y, bi);   // exact in fp32
             const __half2 hi = __floats2half2_rn(w0, w1);
             const float2 hf = __half22float2(hi);
-            wh[j] = *reinterpret_cast<const uint32_t*>(&hi);
-            wl[j] = h2_bits(w0 - hf.x, w1 - hf.y);
+            wh[i * 4 + j] = *reinterpret_cast<const uint32_t*>(&hi);
+            wl[i * 4 + j] = h2_bits(w0 - hf.x, w1 - hf.y);
           }
-          const int c = (i ^ (r & 7)) << 4;
-          *reinterpret_cast<uint4*>(rh + c) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-          *reinterpret_cast<uint4*>(rl + c) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
         }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) wh[i] = wl[i] = 0u;
       }
-      fence_proxy_async();                     // generic writes -> async (MMA) reads
+      const uint32_t col = TM_A + sa * 64 + half * 16;
+      tmem_st16(lane_base + col, wh);
+      tmem_st16(lane_base + col + 32, wl);
+      tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&deq[sb]);
+      if (lane == 0) mbar_arrive(&deq[sa]);
     }
-    // ---- epilogue
-    const int ew = warp - 4, quarter = ew & 3, half = ew >> 2;
-    const int m = quarter * 32 + lane;
-    const bool row_ok = m < t.rows;
-    const long long orow_g = t.row0 + m;
+    // ---- epilogue: this warp reads lanes [32*quarter, +32) and token
+    // columns [128*half, +128)
     if (ok) ok = __all_sync(MS_FULL, mbar_wait(accf, 0, a.status));
     tc_fence_after();
-    const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int c_lo = half * 128, c_hi = min(ntok, c_lo + 128);
     if (PHASE == 0) {
-      constexpr int HALF = NT / 2;
+      // up lanes (64-127) stage bf16(up + bias) as fp32 U[token][feature] in
+      // the (now idle) token ring; gate lanes then form h
+      float* U = reinterpret_cast<float*>(smem);
+      const int f = r & 63;
+      const int fg = f0 + f;                   // feature index in d_ff
       const uint16_t* gbias = reinterpret_cast<const uint16_t*>(blob + a.off[0][3]);
       const uint16_t* ubias = reinterpret_cast<const uint16_t*>(blob + a.off[1][3]);
-      for (int c0 = half * HALF; c0 < (half + 1) * HALF; c0 += 16) {
-        uint32_t gv[16], uv[16];
-        tmem_ld16(tbase + c0, gv);
-        tmem_ld16(tbase + NT + c0, uv);
-        // h (gpt-oss: projection biases first), fp16, in (0,4,1,5,2,6,3,7)
-        // order per 8 columns: the next GEMM's A operand
-        float hv[16];
+      if (r >= 64) {
+        const float ub = a.model == 1 ? bf2f(ubias[fg]) : 0.f;
+        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(lane_base + TM_ACC + c0, v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float g = bfr(__uint_as_float(gv[j])), u = bfr(__uint_as_float(uv[j]));
-          if (a.model == 1) {
-            const int f = nt * NT + c0 + j;
-            g = bfr(g + bf2f(gbias[f]));
-            u = bfr(u + bf2f(ubias[f]));
+          for (int j = 0; j < 16; ++j) {
+            float u = bfr(__uint_as_float(v[j]));
+            if (a.model == 1) u = bfr(u + ub);
+            U[(c0 + j) * 64 + f] = u;
           }
-          hv[(j & 8) | kperm_pos(j & 7)] = g_swiglu(a.model, g, u);
         }
-        uint32_t out[8];
+      }
+      epi_sync();
+      if (r < 64) {
+        const float gb = a.model == 1 ? bf2f(gbias[fg]) : 0.f;
+        const int pos = (fg & ~7) | kperm_pos(fg & 7);   // h column, k-permuted
+        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(lane_base + TM_ACC + c0, v);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) out[j] = h2_bits(hv[2 * j], hv[2 * j + 1]);
-        if (row_ok && ok) {
-          uint4* dst = reinterpret_cast<uint4*>(a.H + orow_g * a.ld_out + nt * NT + c0);
-          dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
-          dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+          for (int j = 0; j < 16; ++j) {
+            const int m = c0 + j;
+            float g = bfr(__uint_as_float(v[j]));
+            if (a.model == 1) g = bfr(g + gb);
+            const float h = g_swiglu(a.model, g, U[m * 64 + f]);
+            if (m < t.rows && ok)
+              a.H[(long long)(t.row0 + m) * a.ld_out + pos] = __half_as_ushort(__float2half_rn(h));
+          }
         }
       }
     } else {
-      constexpr int HALF = N / 2;
-      const float score = row_ok ? a.perm_score[orow_g] : 0.f;
+      const int fo = f0 + r;                   // output feature
+      const bool f_ok = fo < n_out && ok;
       const uint16_t* dbias = reinterpret_cast<const uint16_t*>(blob + a.off[2][3]);
-      for (int c0 = half * HALF; c0 < (half + 1) * HALF; c0 += 16) {
-        uint32_t acc[16];
-        tmem_ld16(tbase + c0, acc);
-        uint32_t out[8];
+      const float db = (a.model == 1 && fo < n_out) ? bf2f(dbias[fo]) : 0.f;
+      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(lane_base + TM_ACC + c0, v);
 #pragma unroll
-        for (int j = 0; j < 16; j += 2) {
-          float v0 = bfr(__uint_as_float(acc[j])), v1 = bfr(__uint_as_float(acc[j + 1]));
-          if (a.model == 1) {
-            v0 = bfr(v0 + bf2f(dbias[nt * NT + c0 + j]));
-            v1 = bfr(v1 + bf2f(dbias[nt * NT + c0 + j + 1]));
+        for (int j = 0; j < 16; ++j) {
+          const int m = c0 + j;
+          if (m < t.rows && f_ok) {
+            float y = bfr(__uint_as_float(v[j]));
+            if (a.model == 1) y = bfr(y + db);
+            // (y * scores) is a bf16 product (engine_v3.py:600)
+            a.Y[(long long)(t.row0 + m) * a.ld_out + fo] = f2bf(a.perm_score[t.row0 + m] * y);
           }
-          // (y * scores) is a bf16 product (engine_v3.py:600)
-          out[j / 2] = (uint32_t)f2bf(score * v0) | ((uint32_t)f2bf(score * v1) << 16);
-        }
-        if (row_ok && ok) {
-          uint4* dst = reinterpret_cast<uint4*>(a.Y + orow_g * a.ld_out + nt * NT + c0);
-          dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
-          dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
         }
       }
     }
@@ -417,7 +459,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, TM_COLS);
   }
 }
 
@@ -460,14 +502,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// fp16 activations [rows, K]: 64 x 128 boxes, 128-byte swizzle (the
+// fp16 activations [rows, K]: 64 x 256 boxes, 128-byte swizzle (the
 // canonical K-major layout the MMA descriptors describe).
 int encode_act_map(CUtensorMap* m, const void* base, int K, long long rows) {
   auto fn = encode_fn();
   if (!fn) return -1;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t box[2] = {64, (cuuint32_t)GM_TOK};
   const cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -490,19 +532,6 @@ int encode_weight_map(CUtensorMap* m, const void* base, int K, int rows_out, int
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS ? 0 : -2;
 }
 
-int gemm_col_tile(int phase, int n) {
-  static const int p0[] = {128, 96, 64};
-  static const int p1[] = {256, 192, 128, 64};
-  if (phase == 0) {
-    for (int c : p0)
-      if (n % c == 0) return c;
-  } else {
-    for (int c : p1)
-      if (n % c == 0) return c;
-  }
-  return 0;
-}
-
 // ---------------------------------------------------------------- launchers
 cudaError_t launch_scatter(const ScatterArgs& a, int grid, cudaStream_t s) {
   k_scatter<<<grid, 256, 0, s>>>(a);
@@ -514,28 +543,22 @@ cudaError_t launch_combine(const CombineArgs& a, int grid, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-template <int PHASE, int NT>
-static cudaError_t launch_gemm_t(const CUtensorMap& tA, const CUtensorMap& tW0,
+template <int PHASE>
+static cudaError_t launch_gemm_t(const CUtensorMap& tX, const CUtensorMap& tW0,
                                  const CUtensorMap& tW1, const GemmArgs& a, int n_col_tiles,
                                  int max_tiles, cudaStream_t s) {
-  auto kern = k_gemm<PHASE, NT>;
+  auto kern = k_gemm<PHASE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(n_col_tiles, max_tiles), GM_THREADS, GM_SMEM, s>>>(tA, tW0, tW1, a);
+  kern<<<dim3(n_col_tiles, max_tiles), GM_THREADS, GM_SMEM, s>>>(tX, tW0, tW1, a);
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm(int phase, int nt, const CUtensorMap& tA, const CUtensorMap& tW0,
+cudaError_t launch_gemm(int phase, const CUtensorMap& tX, const CUtensorMap& tW0,
                         const CUtensorMap& tW1, const GemmArgs& a, int n_col_tiles, int max_tiles,
                         cudaStream_t s) {
-  if (phase == 0 && nt == 128) return launch_gemm_t<0, 128>(tA, tW0, tW1, a, n_col_tiles, max_tiles, s);
-  if (phase == 0 && nt == 96) return launch_gemm_t<0, 96>(tA, tW0, tW1, a, n_col_tiles, max_tiles, s);
-  if (phase == 0 && nt == 64) return launch_gemm_t<0, 64>(tA, tW0, tW1, a, n_col_tiles, max_tiles, s);
-  if (phase == 1 && nt == 256) return launch_gemm_t<1, 256>(tA, tW0, tW1, a, n_col_tiles, max_tiles, s);
-  if (phase == 1 && nt == 192) return launch_gemm_t<1, 192>(tA, tW0, tW1, a, n_col_tiles, max_tiles, s);
-  if (phase == 1 && nt == 128) return launch_gemm_t<1, 128>(tA, tW0, tW1, a, n_col_tiles, max_tiles, s);
-  if (phase == 1 && nt == 64) return launch_gemm_t<1, 64>(tA, tW0, tW1, a, n_col_tiles, max_tiles, s);
-  return cudaErrorInvalidValue;
+  if (phase == 0) return launch_gemm_t<0>(tX, tW0, tW1, a, n_col_tiles, max_tiles, s);
+  return launch_gemm_t<1>(tX, tW0, tW1, a, n_col_tiles, max_tiles, s);
 }
 
 }  // namespace ms

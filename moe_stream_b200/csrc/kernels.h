@@ -85,8 +85,8 @@ struct ExpArgs {
 };
 
 // ------------------------------------------------ wide batches (prefill)
-// A 128-row tile of the grouped GEMM: rows [row0, row0 + rows) of the
-// expert-ordered pair list, all routed to group g.
+// A token tile of the grouped GEMM (at most 256 rows): rows [row0, row0 +
+// rows) of the expert-ordered pair list, all routed to group g.
 struct GemmTile {
   int g, row0, rows, pad;
 };
@@ -119,10 +119,11 @@ struct GemmArgs {
   long long blob;
   long long off[3][4];
   int K;                      // reduction length: d_model (phase 0) or d_ff (phase 1)
+  int n_out;                  // output rows of the projection: d_ff (phase 0) or d_model
   const GemmTile* tiles;
   const int* n_tiles;
   const int* grp_slot;
-  uint16_t* H;                // phase 0 output, bf16 [P_pad, d_ff], k-permuted columns
+  uint16_t* H;                // phase 0 output, fp16 [P_pad, d_ff], k-permuted columns
   uint16_t* Y;                // phase 1 output, bf16 [P_pad, d_model], score-weighted
   int ld_out;
   const float* perm_score;
@@ -139,7 +140,7 @@ struct CombineArgs {
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s);
 cudaError_t launch_route_wide(const RouteArgs& a, const WideArgs& w, cudaStream_t s);
 cudaError_t launch_scatter(const ScatterArgs& a, int grid, cudaStream_t s);
-cudaError_t launch_gemm(int phase, int nt, const CUtensorMap& tA, const CUtensorMap& tW0,
+cudaError_t launch_gemm(int phase, const CUtensorMap& tX, const CUtensorMap& tW0,
                         const CUtensorMap& tW1, const GemmArgs& a, int n_col_tiles, int max_tiles,
                         cudaStream_t s);
 cudaError_t launch_combine(const CombineArgs& a, int grid, cudaStream_t s);
@@ -147,8 +148,8 @@ cudaError_t launch_combine(const CombineArgs& a, int grid, cudaStream_t s);
 int encode_act_map(CUtensorMap* m, const void* base, int K, long long rows);
 int encode_weight_map(CUtensorMap* m, const void* base, int K, int rows_out, int n_slots,
                       long long blob, int box_rows);
-// Widest column tile (a multiple of 16 up to 256 / 128) dividing n.
-int gemm_col_tile(int phase, int n);
+// Token rows per GEMM tile.
+constexpr int GEMM_TILE_ROWS = 256;
 cudaError_t launch_pool_op(const DevTable& t, const PoolReq& r, int* slots_out, int* st,
                            cudaStream_t s);
 cudaError_t launch_fill(const FillArgs& f, int grid, cudaStream_t s);

@@ -350,6 +350,85 @@ __device__ __forceinline__ void warp_drain(const DevTable& T, OpCtx* c, KeyCache
   __syncwarp();
 }
 
+// acquire without allocation: when every key of a request of distinct keys
+// is resident or pending, no slot changes hands, so the items are
+// independent and the warp takes them 32 at a time. The one serial part of
+// the reference loop, the use clock, is reproduced by ranking: every item is
+// touched in item order (a pending key already has its slot), then each
+// waited-on pending key is touched again, in item order
+// (engine_v3.py:412-446). Pins are left to the caller's pinned = set(slots)
+// step, which is all they amount to when nothing is allocated. Returns
+// false (and changes nothing) when some key needs a slot.
+__device__ __forceinline__ bool warp_acquire_resident(const DevTable& T, OpCtx* c, KeyCache* kc,
+                                                      const Req& r, int* slots_out, int lane) {
+  const int n = r.n;
+  if (r.n_uniq != n) return false;
+  bool miss = false;
+  for (int base = 0; base < n; base += 32) {
+    const int i = base + lane;
+    bool m = false;
+    if (i < n) {
+      const int ci = r.ci[i];
+      m = !(kc->flags[ci] & KF_PENDING) && kc->slot[ci] < 0;
+    }
+    miss = __any_sync(MS_FULL, m) || miss;
+  }
+  if (miss) return false;
+  const long long uc0 = c->use_clock;
+  const unsigned lt = (1u << lane) - 1u;
+  int waits_before = 0;
+  long long n_pf = 0, n_cache = 0, n_reads = 0;
+  for (int base = 0; base < n; base += 32) {
+    const int i = base + lane;
+    const int ci = i < n ? r.ci[i] : 0;
+    const bool pend = i < n && (kc->flags[ci] & KF_PENDING) != 0;
+    const unsigned pb = __ballot_sync(MS_FULL, pend);
+    if (i < n) {
+      const int key = kc->key[ci];
+      uint8_t f = kc->flags[ci];
+      long long uc = uc0 + i + 1;              // the in-order touch
+      int uses = 1;
+      if (!pend) {
+        if (f & KF_FROMPF) {                   // first use of a prefetched key (:431-435)
+          f = (uint8_t)(f & ~KF_FROMPF);
+          kc->flags[ci] = f;
+          T.kflags[key] = f;
+          ++n_pf;
+        } else {
+          ++n_cache;
+        }
+      } else {                                 // waited on, touched again (:438-446)
+        uc = uc0 + n + waits_before + __popc(pb & lt) + 1;
+        uses = 2;
+        f = (uint8_t)(f & ~(KF_PENDING | KF_FROMPF));
+        kc->flags[ci] = f;
+        T.kflags[key] = f;
+        ++n_reads;
+        ++n_pf;
+      }
+      T.last_use[key] = uc;                    // _touch (:376-380)
+      kc->freq[ci] += uses;
+      T.freq[key] = kc->freq[ci];
+      slots_out[i] = kc->slot[ci];
+    }
+    waits_before += __popc(pb);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    n_pf += __shfl_xor_sync(MS_FULL, n_pf, o);
+    n_cache += __shfl_xor_sync(MS_FULL, n_cache, o);
+    n_reads += __shfl_xor_sync(MS_FULL, n_reads, o);
+  }
+  if (lane == 0) {
+    c->use_clock = uc0 + n + waits_before;
+    c->st[ST_PREFETCH] += n_pf;
+    c->st[ST_CACHE] += n_cache;
+    c->st[ST_READS] += n_reads;
+  }
+  __syncwarp();
+  return true;
+}
+
 // acquire (engine_v3.py:398-454) of request r. slots_out[i] receives the
 // slot of item i (-1 if exhausted before it was placed). waits: scratch of
 // r.n ints. Returns 0 or MS_E_EXHAUSTED (-3).
@@ -359,7 +438,8 @@ __device__ __forceinline__ int warp_acquire(const DevTable& T, OpCtx* c, KeyCach
   int n_wait = 0, n_issue = 0, status = 0;
   for (int i = lane; i < n; i += 32) slots_out[i] = -1;
   __syncwarp();
-  for (int i = 0; i < n; ++i) {
+  const bool resident = warp_acquire_resident(T, c, kc, r, slots_out, lane);
+  for (int i = 0; i < (resident ? 0 : n); ++i) {
     const int ci = r.ci[i];
     int pend = 0, slot = -1;
     if (lane == 0) {                         // lane 0 decides, the warp follows
@@ -398,7 +478,7 @@ __device__ __forceinline__ int warp_acquire(const DevTable& T, OpCtx* c, KeyCach
   }
   __syncwarp();
   if (status == 0) {
-    if (lane == 0) {
+    if (lane == 0 && !resident) {
       c->st[ST_EXPOSED] += n_issue;
       c->st[ST_READS] += n_issue;
       for (int w = 0; w < n_wait; ++w) {            // (:438-446)

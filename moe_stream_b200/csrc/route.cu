@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
 // shared memory; per-expert pair counts and predicted-expert masks are then
 // merged in global memory. The last CTA to arrive runs the slot-table step,
 // lays the groups out (ascending expert id, each a contiguous run of rows)
-// and cuts them into the 128-row tiles of the grouped GEMM.
+// and cuts them into the token tiles of the grouped GEMM.
 constexpr int RW_TOK = 32;
 
 __device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, const uint32_t* b) {
@@ -341,24 +341,27 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_wide(RouteArgs A, WideArgs
   for (int i = threadIdx.x; i < MAX_E; i += RT_THREADS) s_hist[i] = 0;
   for (int i = threadIdx.x; i < MS_MAX_DEPTHS * (MAX_E / 32); i += RT_THREADS) (&s_pm[0][0])[i] = 0;
 
-  // ---- logits: mma.sync m16n8k16 over 16-row chunks of the router rows;
-  // fragment rows are read straight from global memory (L1/L2 resident).
-  const uint32_t* xr[2][2];
+  // ---- logits: mma.sync m16n8k16 over 16-row chunks of the router rows.
+  // Lane (g8, c4) loads 16 contiguous bytes of its rows per 32-column chunk
+  // (columns 8*c4 .. 8*c4+7): the first four feed k slots (2c, 2c+1, 2c+8,
+  // 2c+9) of one MMA, the last four those of a second. A and B use the same
+  // assignment, so the two MMAs sum the chunk's 32 products exactly once.
+  const uint4* xr[2][2];
 #pragma unroll
   for (int m = 0; m < 2; ++m)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int t = min(t0 + m * 16 + h * 8 + g8, T - 1);   // rows past T: computed, never used
-      xr[m][h] = reinterpret_cast<const uint32_t*>(A.x + (long long)t * d) + c4;
+      xr[m][h] = reinterpret_cast<const uint4*>(A.x + (long long)t * d) + c4;
     }
   for (int rc = warp; rc * 16 < rows; rc += RT_THREADS / 32) {
-    const uint32_t* wr[2];
+    const uint4* wr[2];
 #pragma unroll
     for (int n = 0; n < 2; ++n) {
       const int r = min(rc * 16 + n * 8 + g8, rows - 1);
       const int which = r / E, e = r % E;
-      wr[n] = reinterpret_cast<const uint32_t*>((which == 0 ? A.w_r : A.w_p[which - 1]) +
-                                                (long long)e * d) + c4;
+      wr[n] = reinterpret_cast<const uint4*>((which == 0 ? A.w_r : A.w_p[which - 1]) +
+                                             (long long)e * d) + c4;
     }
     float acc[2][2][4];
 #pragma unroll
@@ -368,24 +371,25 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_wide(RouteArgs A, WideArgs
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[m][n][q] = 0.f;
 #pragma unroll 4
-    for (int kw = 0; kw < d / 2; kw += 8) {    // 16 bf16 = 8 words per step
-      uint32_t a[2][4], b[2][2];
-#pragma unroll
-      for (int m = 0; m < 2; ++m) {
-        a[m][0] = __ldg(xr[m][0] + kw);
-        a[m][1] = __ldg(xr[m][1] + kw);
-        a[m][2] = __ldg(xr[m][0] + kw + 4);
-        a[m][3] = __ldg(xr[m][1] + kw + 4);
-      }
-#pragma unroll
-      for (int n = 0; n < 2; ++n) {
-        b[n][0] = __ldg(wr[n] + kw);
-        b[n][1] = __ldg(wr[n] + kw + 4);
-      }
+    for (int kc = 0; kc < d / 8; kc += 4) {     // 32 columns per step
+      uint4 av[2][2], bv[2];
 #pragma unroll
       for (int m = 0; m < 2; ++m)
 #pragma unroll
-        for (int n = 0; n < 2; ++n) mma_bf16_16816(acc[m][n], a[m], b[n]);
+        for (int h = 0; h < 2; ++h) av[m][h] = __ldg(xr[m][h] + kc);
+#pragma unroll
+      for (int n = 0; n < 2; ++n) bv[n] = __ldg(wr[n] + kc);
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+          const uint32_t a0[4] = {av[m][0].x, av[m][1].x, av[m][0].y, av[m][1].y};
+          const uint32_t b0[2] = {bv[n].x, bv[n].y};
+          mma_bf16_16816(acc[m][n], a0, b0);
+          const uint32_t a1[4] = {av[m][0].z, av[m][1].z, av[m][0].w, av[m][1].w};
+          const uint32_t b1[2] = {bv[n].z, bv[n].w};
+          mma_bf16_16816(acc[m][n], a1, b1);
+        }
     }
 #pragma unroll
     for (int n = 0; n < 2; ++n)
@@ -475,13 +479,13 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_wide(RouteArgs A, WideArgs
     __syncwarp();
     warp_pool_step(A, s_pred, s_n_pred, s_acq, n_acq, s_slots, s_waits, &s_op, &s_kc, s_ci, lane);
     __syncwarp();
-    // groups in ascending expert order, and their 128-row tiles
+    // groups in ascending expert order, and their token tiles
     int run = 0, trun = 0;
     for (int base = 0; base < n_acq; base += 32) {
       const int gi = base + lane;
       const int e = gi < n_acq ? s_acq[gi] : 0;
       const int cnt = gi < n_acq ? s_cnt[e] : 0;
-      const int nt = (cnt + 127) >> 7;
+      const int nt = (cnt + GEMM_TILE_ROWS - 1) / GEMM_TILE_ROWS;
       int ic = cnt, itl = nt;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -504,8 +508,8 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_wide(RouteArgs A, WideArgs
         for (int j = 0; j < nt && first + j < W.max_tiles; ++j) {
           GemmTile tl;
           tl.g = gi;
-          tl.row0 = start + j * 128;
-          tl.rows = min(128, cnt - j * 128);
+          tl.row0 = start + j * GEMM_TILE_ROWS;
+          tl.rows = min(GEMM_TILE_ROWS, cnt - j * GEMM_TILE_ROWS);
           tl.pad = 0;
           W.tiles[first + j] = tl;
         }
