@@ -52,7 +52,7 @@ namespace ms {
 
 constexpr int GM_THREADS = 384;
 constexpr int GM_STAGES = 4;                  // token + code tiles
-constexpr int GM_A_STAGES = 2;                // weight tiles in TMEM
+constexpr int GM_A_STAGES = 4;                // weight tiles in TMEM
 constexpr int GM_TOK = GEMM_TILE_ROWS;        // tokens per CTA (MMA N, at most)
 constexpr int GM_X_BYTES = GM_TOK * 128;      // 256 tokens x 64 fp16
 constexpr int GM_P_BYTES = 128 * 32;          // 128 weight rows x 64 nibbles
@@ -61,8 +61,11 @@ constexpr int GM_OFF_BAR = GM_OFF_P + GM_STAGES * GM_P_BYTES;      // 144 KB
 constexpr int GM_SMEM = GM_OFF_BAR + 256 + 1024;
 // TMEM columns: accumulator [0, 256), weight stage s at 256 + 64 s (hi, then lo)
 constexpr uint32_t TM_ACC = 0, TM_A = 256, TM_COLS = 512;
+static_assert(TM_A + GM_A_STAGES * 64 <= TM_COLS, "weight stages fit in TMEM");
 static_assert(GM_X_BYTES % 1024 == 0 && GM_P_BYTES % 1024 == 0, "1 KB aligned tiles");
-static_assert(64 * GM_TOK * 4 <= GM_OFF_P, "the up-projection staging fits in the token ring");
+// epilogue staging, in the (then idle) token ring: 256 tokens x 128 fp32
+static_assert(GM_TOK * 128 * 4 <= GM_OFF_P, "epilogue staging fits in the token ring");
+constexpr int SCALE_AHEAD = 4;                // scale/bias loads issued this many K tiles early
 
 // ------------------------------------------------------------- PTX helpers
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y,
@@ -340,16 +343,20 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     const uint8_t* blob = a.arena + (long long)slot * a.blob;
     const uint16_t* Sc = reinterpret_cast<const uint16_t*>(blob + a.off[proj][1]) + (long long)orow * G;
     const uint16_t* Bi = reinterpret_cast<const uint16_t*>(blob + a.off[proj][2]) + (long long)orow * G;
-    uint16_t s_next = active ? Sc[0] : 0, b_next = active ? Bi[0] : 0;
-    const __half2 h1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+    // (scale | bias << 16) of K tiles kt .. kt + SCALE_AHEAD - 1, a shifting ring
+    uint32_t sb[SCALE_AHEAD];
+#pragma unroll
+    for (int i = 0; i < SCALE_AHEAD; ++i)
+      sb[i] = (active && i < KT) ? ((uint32_t)Sc[i] | ((uint32_t)Bi[i] << 16)) : 0u;
+    const float2 magic_off = make_float2(-8388608.f, -8388608.f);
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     for (int kt = 0; kt < KT; ++kt) {
       const int sx = kt % GM_STAGES, sa = kt % GM_A_STAGES;
-      const float sc = bf2f(s_next), bi = bf2f(b_next);
-      if (active && kt + 1 < KT) {
-        s_next = Sc[kt + 1];
-        b_next = Bi[kt + 1];
-      }
+      const float sc = __uint_as_float(sb[0] << 16), bi = __uint_as_float(sb[0] & 0xffff0000u);
+#pragma unroll
+      for (int i = 0; i + 1 < SCALE_AHEAD; ++i) sb[i] = sb[i + 1];
+      const int kn = kt + SCALE_AHEAD;
+      sb[SCALE_AHEAD - 1] = (active && kn < KT) ? ((uint32_t)Sc[kn] | ((uint32_t)Bi[kn] << 16)) : 0u;
       // every lane waits; the warp goes on only if all of them saw the stage
       bool got = mbar_wait(&full[sx], (kt / GM_STAGES) & 1, a.status);
       if (got && kt >= GM_A_STAGES)
@@ -363,19 +370,23 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       if (active) {
         const uint4 pw = *reinterpret_cast<const uint4*>(sP(sx) + r * 32 + half * 16);
         const uint32_t words[4] = {pw.x, pw.y, pw.z, pw.w};
+        const float2 s2 = make_float2(sc, sc), b2 = make_float2(bi, bi);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const uint32_t u = words[i];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            // {q_j, q_j+4} exactly, as fp16 1024+q minus 1024
-            const uint32_t m = ((u >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
-            const float2 q = __half22float2(__hsub2(*reinterpret_cast<const __half2*>(&m), h1024));
-            const float w0 = fmaf(sc, q.x, bi), w1 = fmaf(sc, q.y, bi);   // exact in fp32
-            const __half2 hi = __floats2half2_rn(w0, w1);
+            // q_j and q_j+4 as exact floats (2^23 + q, minus 2^23)
+            const uint32_t m = (u >> (4 * j)) & 0x000F000Fu;
+            const float2 q = __fadd2_rn(make_float2(__uint_as_float((m & 0xFu) | 0x4B000000u),
+                                                    __uint_as_float((m >> 16) | 0x4B000000u)),
+                                        magic_off);
+            const float2 w = __ffma2_rn(q, s2, b2);             // exact: s*q + b
+            const __half2 hi = __floats2half2_rn(w.x, w.y);
             const float2 hf = __half22float2(hi);
+            const float2 lo = __fadd2_rn(w, make_float2(-hf.x, -hf.y));
             wh[i * 4 + j] = *reinterpret_cast<const uint32_t*>(&hi);
-            wl[i * 4 + j] = h2_bits(w0 - hf.x, w1 - hf.y);
+            wl[i * 4 + j] = h2_bits(lo.x, lo.y);
           }
         }
       } else {
@@ -390,68 +401,78 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&deq[sa]);
     }
-    // ---- epilogue: this warp reads lanes [32*quarter, +32) and token
-    // columns [128*half, +128)
+    // ---- epilogue. Each warp reads lanes [32*quarter, +32) and token
+    // columns [128*half, +128) of the accumulator into the staging area S
+    // (the token ring, idle once the accumulator is complete), as fp32
+    // S[token][lane]; then the 256 threads write whole 16-byte chunks.
     if (ok) ok = __all_sync(MS_FULL, mbar_wait(accf, 0, a.status));
     tc_fence_after();
+    float* S = reinterpret_cast<float*>(smem);
     const int c_lo = half * 128, c_hi = min(ntok, c_lo + 128);
+    const int et = threadIdx.x - 128;          // 0..255
     if (PHASE == 0) {
-      // up lanes (64-127) stage bf16(up + bias) as fp32 U[token][feature] in
-      // the (now idle) token ring; gate lanes then form h
-      float* U = reinterpret_cast<float*>(smem);
-      const int f = r & 63;
-      const int fg = f0 + f;                   // feature index in d_ff
-      const uint16_t* gbias = reinterpret_cast<const uint16_t*>(blob + a.off[0][3]);
-      const uint16_t* ubias = reinterpret_cast<const uint16_t*>(blob + a.off[1][3]);
-      if (r >= 64) {
-        const float ub = a.model == 1 ? bf2f(ubias[fg]) : 0.f;
-        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(lane_base + TM_ACC + c0, v);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float u = bfr(__uint_as_float(v[j]));
-            if (a.model == 1) u = bfr(u + ub);
-            U[(c0 + j) * 64 + f] = u;
-          }
-        }
-      }
-      epi_sync();
-      if (r < 64) {
-        const float gb = a.model == 1 ? bf2f(gbias[fg]) : 0.f;
-        const int pos = (fg & ~7) | kperm_pos(fg & 7);   // h column, k-permuted
-        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(lane_base + TM_ACC + c0, v);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = c0 + j;
-            float g = bfr(__uint_as_float(v[j]));
-            if (a.model == 1) g = bfr(g + gb);
-            const float h = g_swiglu(a.model, g, U[m * 64 + f]);
-            if (m < t.rows && ok)
-              a.H[(long long)(t.row0 + m) * a.ld_out + pos] = __half_as_ushort(__float2half_rn(h));
-          }
-        }
-      }
-    } else {
-      const int fo = f0 + r;                   // output feature
-      const bool f_ok = fo < n_out && ok;
-      const uint16_t* dbias = reinterpret_cast<const uint16_t*>(blob + a.off[2][3]);
-      const float db = (a.model == 1 && fo < n_out) ? bf2f(dbias[fo]) : 0.f;
+      // lanes 0-63: gate + bias, 64-127: up + bias, both bf16-rounded
+      const int fg = f0 + (r & 63);
+      const float bias = a.model == 1 ? bf2f(reinterpret_cast<const uint16_t*>(
+                                                blob + a.off[r < 64 ? 0 : 1][3])[fg])
+                                      : 0.f;
       for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
         uint32_t v[16];
         tmem_ld16(lane_base + TM_ACC + c0, v);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int m = c0 + j;
-          if (m < t.rows && f_ok) {
-            float y = bfr(__uint_as_float(v[j]));
-            if (a.model == 1) y = bfr(y + db);
-            // (y * scores) is a bf16 product (engine_v3.py:600)
-            a.Y[(long long)(t.row0 + m) * a.ld_out + fo] = f2bf(a.perm_score[t.row0 + m] * y);
-          }
+          float g = bfr(__uint_as_float(v[j]));
+          if (a.model == 1) g = bfr(g + bias);
+          S[(c0 + j) * 128 + r] = g;
         }
+      }
+      epi_sync();
+      // h for 8 consecutive features of one token per task, k-permuted, fp16
+      for (int task = et; task < t.rows * 8; task += 256) {
+        const int m = task >> 3, c8 = (task & 7) * 8;
+        const float4* gs = reinterpret_cast<const float4*>(S + m * 128 + c8);
+        const float4 g0 = gs[0], g1 = gs[1], u0 = gs[16], u1 = gs[17];
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        float hv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) hv[kperm_pos(j)] = g_swiglu(a.model, gv[j], uv[j]);
+        if (ok)
+          *reinterpret_cast<uint4*>(a.H + (long long)(t.row0 + m) * a.ld_out + f0 + c8) =
+              make_uint4(h2_bits(hv[0], hv[1]), h2_bits(hv[2], hv[3]), h2_bits(hv[4], hv[5]),
+                         h2_bits(hv[6], hv[7]));
+      }
+    } else {
+      const int fo = f0 + r;                   // output feature
+      const float bias = (a.model == 1 && fo < n_out)
+                             ? bf2f(reinterpret_cast<const uint16_t*>(blob + a.off[2][3])[fo]) : 0.f;
+      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(lane_base + TM_ACC + c0, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float y = bfr(__uint_as_float(v[j]));
+          if (a.model == 1) y = bfr(y + bias);
+          S[(c0 + j) * 128 + r] = y;
+        }
+      }
+      epi_sync();
+      // (y * scores) is a bf16 product (engine_v3.py:600); 8 features per task
+      const int nf = min(128, n_out - f0);     // a multiple of 8 (d_model % 64 == 0)
+      const int chunks = nf >> 3;
+      for (int task = et; task < t.rows * chunks; task += 256) {
+        const int m = task / chunks, c8 = (task % chunks) * 8;
+        const float sc = a.perm_score[t.row0 + m];
+        const float4* y4 = reinterpret_cast<const float4*>(S + m * 128 + c8);
+        const float4 y0 = y4[0], y1 = y4[1];
+        const float ys[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          o[j] = (uint32_t)f2bf(sc * ys[2 * j]) | ((uint32_t)f2bf(sc * ys[2 * j + 1]) << 16);
+        if (ok)
+          *reinterpret_cast<uint4*>(a.Y + (long long)(t.row0 + m) * a.ld_out + f0 + c8) =
+              make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
   }
