@@ -642,7 +642,6 @@ static int wide_experts(ms_pool* p, const void* x, int T, void* y, cudaStream_t 
     for (int b = 0; b < 4; ++b) g.off[a][b] = p->geom.comp_offset[a][b];
   g.tiles = p->wa.tiles;
   g.n_tiles = p->wa.n_tiles;
-  g.grp_slot = p->grp.grp_slot;
   g.H = p->hbuf;
   g.Y = p->ybuf;
   g.perm_score = p->perm_score;
@@ -652,11 +651,12 @@ static int wide_experts(ms_pool* p, const void* x, int T, void* y, cudaStream_t 
   g.K = p->geom.d_model;
   g.n_out = p->geom.d_ff;
   g.ld_out = p->geom.d_ff;
-  CK(launch_gemm(0, p->tm_x, p->tm_wg, p->tm_wu, g, p->geom.d_ff / 64, tiles, s));
+  CK(launch_gemm(0, p->tm_x, p->tm_wg, p->tm_wu, g, tiles * (p->geom.d_ff / 64), p->sm_count, s));
   g.K = p->geom.d_ff;
   g.n_out = p->geom.d_model;
   g.ld_out = p->geom.d_model;
-  CK(launch_gemm(1, p->tm_h, p->tm_wd, p->tm_wd, g, (p->geom.d_model + 127) / 128, tiles, s));
+  CK(launch_gemm(1, p->tm_h, p->tm_wd, p->tm_wd, g, tiles * ((p->geom.d_model + 127) / 128),
+                 p->sm_count, s));
   CombineArgs c{};
   c.Y = p->ybuf;
   c.inv = p->inv;

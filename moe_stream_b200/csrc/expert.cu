@@ -36,7 +36,8 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 // every elementwise op of the SwiGLU rounds its result to bf16
 // (engine_v3.py:592-597, engine_120b.py:136-143), so the block tracks the
 // reference's arithmetic, not a more precise variant of it.
-__device__ __forceinline__ float sigm(float v) { return 1.f / (1.f + expf(-v)); }
+// 1/(1+e^-v); __frcp_rn is the correctly rounded reciprocal, i.e. 1.f / x
+__device__ __forceinline__ float sigm(float v) { return __frcp_rn(1.f + expf(-v)); }
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
   // activations.swiglu(gate, x) = silu(gate) * x, silu(v) = v * sigmoid(v)

@@ -16,30 +16,36 @@
 // Shape. Weights are the MMA's A operand and live in tensor memory: each
 // dequantising thread owns one weight row = one TMEM lane and writes its hi
 // and lo halves there with tcgen05.st, so the dequantised operand never
-// touches shared memory. Tokens are the B operand: up to 256 rows of X per
-// CTA, TMA-loaded into shared memory (128-byte swizzle). D[weight row, token]
-// accumulates in TMEM. Each dequantised weight thus serves up to 256 tokens.
+// touches shared memory. Tokens are the B operand: up to 128 rows of X per
+// work item, TMA-loaded into shared memory (128-byte swizzle). D[weight row,
+// token] accumulates in TMEM.
 //
 //   k_scatter  token rows copied into expert order (X_perm, one fp16 row
 //              per token/expert pair), each 8-column block stored in the
 //              order (0,4,1,5,2,6,3,7) that the nibble unpacking gives the
 //              weights, so both operands agree on k; with the per-row score
-//              and the pair -> row map. The groups and their 256-row tiles
+//              and the pair -> row map. The groups and their 128-row tiles
 //              come from the wide router (route.cu).
-//   k_gemm<0>  per (64 features, token tile): A = [64 gate rows; 64 up rows],
-//              D lanes 0-63 gate, 64-127 up; SwiGLU in the epilogue; h
-//              written as fp16 in the k-permuted column order.
+//   k_gemm<0>  per (64 features, token tile): A = 64 gate and 64 up rows,
+//              arranged so that lane 32q + l holds gate feature 16q + l and
+//              lane 32q + 16 + l the up row of the same feature; SwiGLU in
+//              the epilogue pairs them with one shuffle; h written as fp16
+//              in the k-permuted column order.
 //   k_gemm<1>  per (128 output features, token tile): A = down rows;
 //              Y = bf16(acc) (+bias), times the routing score.
 //   k_combine  y[t] = sum_j Y[inv(t, j)] in a fixed j order.
 //
-// One CTA = 12 warps: warp 0 issues the TMA loads, warp 1 issues the MMAs,
-// warp 2 owns the TMEM allocation, warps 4-11 dequantise (two warps per
-// TMEM lane quarter, each taking half of a K tile's columns) and then run
-// the epilogue. mbarrier rings hand the tiles over: tokens + codes (TMA ->
-// dequant/MMA, 4 deep), weights in TMEM (dequant -> MMA, 2 deep), and the
-// accumulator (MMA -> epilogue). Every wait is bounded and reports
-// MS_E_TIMEOUT instead of hanging.
+// Persistent CTAs, one per SM, each looping over (token tile, feature tile)
+// work items with 24 warps in fixed roles: warp 0 issues the TMA loads,
+// warp 1 the MMAs, warp 2 owns the TMEM allocation, warps 4-19 dequantise
+// (four per TMEM lane quarter, each taking a quarter of a K tile's columns),
+// warps 20-23 drain finished accumulators (one per lane quarter). mbarrier
+// rings hand the work over: tokens + codes (TMA -> dequant/MMA, 6 deep),
+// weights in TMEM (dequant -> MMA, 4 deep) and two accumulators (MMA <->
+// epilogue), so one item's epilogue overlaps the next item's main loop.
+// Every wait is bounded and reports MS_E_TIMEOUT instead of hanging.
+#include <algorithm>
+
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
@@ -50,21 +56,21 @@
 
 namespace ms {
 
-constexpr int GM_THREADS = 384;
-constexpr int GM_STAGES = 4;                  // token + code tiles
+constexpr int GM_THREADS = 768;              // 24 warps, see the role list above
+constexpr int GM_STAGES = 6;                  // token + code tiles
 constexpr int GM_A_STAGES = 4;                // weight tiles in TMEM
-constexpr int GM_TOK = GEMM_TILE_ROWS;        // tokens per CTA (MMA N, at most)
-constexpr int GM_X_BYTES = GM_TOK * 128;      // 256 tokens x 64 fp16
+constexpr int GM_TOK = GEMM_TILE_ROWS;        // tokens per tile (MMA N, at most)
+constexpr int GM_X_BYTES = GM_TOK * 128;      // 128 tokens x 64 fp16
 constexpr int GM_P_BYTES = 128 * 32;          // 128 weight rows x 64 nibbles
-constexpr int GM_OFF_P = GM_STAGES * GM_X_BYTES;                   // 128 KB
-constexpr int GM_OFF_BAR = GM_OFF_P + GM_STAGES * GM_P_BYTES;      // 144 KB
-constexpr int GM_SMEM = GM_OFF_BAR + 256 + 1024;
-// TMEM columns: accumulator [0, 256), weight stage s at 256 + 64 s (hi, then lo)
+constexpr int GM_OFF_P = GM_STAGES * GM_X_BYTES;                   // 96 KB
+constexpr int GM_OFF_BAR = GM_OFF_P + GM_STAGES * GM_P_BYTES;      // 120 KB (> half an SM:
+constexpr int GM_SMEM = GM_OFF_BAR + 256 + 1024;                   //  one CTA per SM)
+// TMEM columns: accumulators [0, 128) and [128, 256); weight stage s at
+// 256 + 64 s (hi, then lo)
 constexpr uint32_t TM_ACC = 0, TM_A = 256, TM_COLS = 512;
-static_assert(TM_A + GM_A_STAGES * 64 <= TM_COLS, "weight stages fit in TMEM");
+static_assert(2 * GM_TOK <= (int)TM_A && TM_A + GM_A_STAGES * 64 <= TM_COLS, "TMEM budget");
 static_assert(GM_X_BYTES % 1024 == 0 && GM_P_BYTES % 1024 == 0, "1 KB aligned tiles");
-// epilogue staging, in the (then idle) token ring: 256 tokens x 128 fp32
-static_assert(GM_TOK * 128 * 4 <= GM_OFF_P, "epilogue staging fits in the token ring");
+static_assert(GM_SMEM > 232448 / 2, "one CTA per SM: the whole of TMEM is allocated");
 constexpr int SCALE_AHEAD = 4;                // scale/bias loads issued this many K tiles early
 
 // ------------------------------------------------------------- PTX helpers
@@ -146,12 +152,16 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
       : "memory");
 }
 
+// 8 consecutive columns of this thread's lane <- v[0..8)
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
-
-// barrier 1 among the 256 epilogue threads (warps 4-11)
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
@@ -173,7 +183,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
 // ---------------------------------------------------------------- numerics
 // Same rounding points as the decode kernels (MLX's): gather_qmm output bf16,
 // each SwiGLU op rounded to bf16.
-__device__ __forceinline__ float g_sigm(float v) { return 1.f / (1.f + expf(-v)); }
+// 1/(1+e^-v); __frcp_rn is the correctly rounded reciprocal, i.e. 1.f / x
+__device__ __forceinline__ float g_sigm(float v) { return __frcp_rn(1.f + expf(-v)); }
 __device__ __forceinline__ float g_swiglu(int model, float g, float u) {
   if (model == 1) {
     g = fminf(g, 7.f);
@@ -229,43 +240,35 @@ __global__ void __launch_bounds__(256) k_scatter(ScatterArgs a) {
 }
 
 // ------------------------------------------------------------------ K4
-// PHASE 0: blockIdx.x = 64-feature tile of d_ff (A rows: gate f0..f0+63,
-// then up f0..f0+63). PHASE 1: 128-feature tile of d_model (down rows).
+// Work item w: token tile w / n_ft, feature tile w % n_ft. PHASE 0 feature
+// tiles are 64 features of d_ff (gate and up rows), PHASE 1 tiles 128
+// features of d_model (down rows). Items whose group has no slot (pool
+// exhausted) run with zero weights and write zeros.
 template <int PHASE>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW0,
            const __grid_constant__ CUtensorMap tmW1, GemmArgs a) {
+  constexpr int FT = PHASE == 0 ? 64 : 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.y;
-  if (tile >= *a.n_tiles || timed_out(a.status)) return;   // uniform: before any barrier
-  const GemmTile t = a.tiles[tile];
-  const int slot = a.grp_slot[t.g];
+  const int n_out = a.n_out;
+  const int n_ft = (n_out + FT - 1) / FT;
+  const int total = *a.n_tiles * n_ft;
+  if (blockIdx.x >= total || timed_out(a.status)) return;   // uniform: before any barrier
   const int KT = a.K / 64, G = a.K / 64;
-  const int n_out = a.n_out;                   // rows of this projection's output
-  const int f0 = blockIdx.x * (PHASE == 0 ? 64 : 128);
-  const int ntok = (t.rows + 15) & ~15;        // MMA N: the tile's rows, rounded up to 16
+  const int step = gridDim.x;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + GM_OFF_BAR);
   uint64_t* full = bars;                                   // [S]  TMA landed
-  uint64_t* empty_x = bars + GM_STAGES;                    // [S]  MMA done with X (and P)
-  uint64_t* deq = bars + 2 * GM_STAGES;                    // [A]  weights in TMEM
+  uint64_t* empty_x = full + GM_STAGES;                    // [S]  MMA done with X (and P)
+  uint64_t* deq = empty_x + GM_STAGES;                     // [A]  weights in TMEM
   uint64_t* empty_a = deq + GM_A_STAGES;                   // [A]  MMA done with them
-  uint64_t* accf = empty_a + GM_A_STAGES;                  // accumulator complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* acc_full = empty_a + GM_A_STAGES;              // [2]  accumulator complete
+  uint64_t* acc_empty = acc_full + 2;                      // [2]  accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   auto sX = [&](int s) { return smem + s * GM_X_BYTES; };
   auto sP = [&](int s) { return smem + GM_OFF_P + s * GM_P_BYTES; };
-
-  if (slot < 0) {                              // exhausted pool: this tile contributes zeros
-    const int cols = PHASE == 0 ? 64 : min(128, n_out - f0);
-    uint16_t* out = PHASE == 0 ? a.H : a.Y;
-    for (int i = threadIdx.x; i < t.rows * cols; i += GM_THREADS) {
-      const int m = i / cols, c = i % cols;
-      out[(long long)(t.row0 + m) * a.ld_out + f0 + c] = 0;
-    }
-    return;
-  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < GM_STAGES; ++s) {
@@ -273,10 +276,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       mbar_init(&empty_x[s], 1);
     }
     for (int s = 0; s < GM_A_STAGES; ++s) {
-      mbar_init(&deq[s], 8);
+      mbar_init(&deq[s], 16);
       mbar_init(&empty_a[s], 1);
     }
-    mbar_init(accf, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
     fence_barrier_init();
   }
   if (warp == 2) tmem_alloc(tmem_slot, TM_COLS);
@@ -284,196 +290,241 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  bool ok = true;
 
   if (warp == 0) {
     if (lane == 0) {                           // ---- TMA producer
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % GM_STAGES;
-        if (kt >= GM_STAGES && !mbar_wait(&empty_x[s], ((kt / GM_STAGES) - 1) & 1, a.status)) {
-          ok = false;
-          break;
-        }
-        mbar_expect_tx(&full[s], GM_X_BYTES + GM_P_BYTES);
-        tma_load_2d(sX(s), &tmX, kt * 64, t.row0, &full[s]);
-        if (PHASE == 0) {
-          tma_load_3d(sP(s), &tmW0, kt * 32, f0, slot, &full[s]);
-          tma_load_3d(sP(s) + 64 * 32, &tmW1, kt * 32, f0, slot, &full[s]);
-        } else {
-          tma_load_3d(sP(s), &tmW0, kt * 32, f0, slot, &full[s]);
+      int it = 0;
+      bool ok = true;
+      GemmTile tn = a.tiles[blockIdx.x / n_ft];          // tile records: one item ahead
+      for (int w = blockIdx.x; w < total && ok; w += step) {
+        const GemmTile t = tn;
+        if (w + step < total) tn = a.tiles[(w + step) / n_ft];
+        const int f0 = (w % n_ft) * FT;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = it % GM_STAGES;
+          if (it >= GM_STAGES && !mbar_wait(&empty_x[s], ((it / GM_STAGES) - 1) & 1, a.status)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], GM_X_BYTES + GM_P_BYTES);
+          tma_load_2d(sX(s), &tmX, kt * 64, t.row0, &full[s]);
+          // a slot of -1 reads outside the tensor: the codes arrive as zeros
+          if (PHASE == 0) {
+            tma_load_3d(sP(s), &tmW0, kt * 32, f0, t.slot, &full[s]);
+            tma_load_3d(sP(s) + 64 * 32, &tmW1, kt * 32, f0, t.slot, &full[s]);
+          } else {
+            tma_load_3d(sP(s), &tmW0, kt * 32, f0, t.slot, &full[s]);
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {                           // ---- MMA issuer
-      const uint32_t idesc = idesc_f16(ntok);
-      for (int kt = 0; kt < KT; ++kt) {
-        const int sx = kt % GM_STAGES, sa = kt % GM_A_STAGES;
-        if (!mbar_wait(&deq[sa], (kt / GM_A_STAGES) & 1, a.status)) {
-          ok = false;
-          break;
-        }
+      int it = 0, ai = 0;
+      bool ok = true;
+      GemmTile tn = a.tiles[blockIdx.x / n_ft];
+      for (int w = blockIdx.x; w < total && ok; w += step, ++ai) {
+        const GemmTile t = tn;
+        if (w + step < total) tn = a.tiles[(w + step) / n_ft];
+        const uint32_t idesc = idesc_f16((t.rows + 15) & ~15);
+        const int b = ai & 1;
+        if (ai >= 2 && !mbar_wait(&acc_empty[b], ((ai >> 1) - 1) & 1, a.status)) break;
         tc_fence_after();
-        const uint64_t bd = sw128_desc(sX(sx));
-        const uint32_t ahi = tmem + TM_A + sa * 64, alo = ahi + 32;
+        const uint32_t d = tmem + TM_ACC + b * GM_TOK;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int sx = it % GM_STAGES, sa = it % GM_A_STAGES;
+          if (!mbar_wait(&deq[sa], (it / GM_A_STAGES) & 1, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bd = sw128_desc(sX(sx));
+          const uint32_t ahi = tmem + TM_A + sa * 64, alo = ahi + 32;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {          // K = 16 per MMA: 8 TMEM columns, 32 smem bytes
-          mma_ts_f16(tmem + TM_ACC, ahi + 8 * j, bd + 2 * j, idesc, (kt | j) != 0);
-          mma_ts_f16(tmem + TM_ACC, alo + 8 * j, bd + 2 * j, idesc, 1u);
+          for (int j = 0; j < 4; ++j) {        // K = 16 per MMA: 8 TMEM columns, 32 smem bytes
+            mma_ts_f16(d, ahi + 8 * j, bd + 2 * j, idesc, (kt | j) != 0);
+            mma_ts_f16(d, alo + 8 * j, bd + 2 * j, idesc, 1u);
+          }
+          mma_commit(&empty_a[sa]);
+          mma_commit(&empty_x[sx]);
         }
-        mma_commit(&empty_a[sa]);
-        mma_commit(&empty_x[sx]);
+        if (ok) mma_commit(&acc_full[b]);
       }
-      mma_commit(accf);
     }
-  } else if (warp >= 4) {
-    // ---- dequantise: TMEM lane r = weight row r; this warp takes columns
-    // [16*half, 16*half + 16) of each K tile (32 codes)
-    const int quarter = warp & 3, half = (warp - 4) >> 2;
-    const int r = quarter * 32 + lane;
-    int proj, orow;
-    if (PHASE == 0) {
-      proj = r < 64 ? 0 : 1;
-      orow = f0 + (r & 63);
-    } else {
-      proj = 2;
-      orow = f0 + r;
-    }
-    const bool active = orow < n_out;
-    const uint8_t* blob = a.arena + (long long)slot * a.blob;
-    const uint16_t* Sc = reinterpret_cast<const uint16_t*>(blob + a.off[proj][1]) + (long long)orow * G;
-    const uint16_t* Bi = reinterpret_cast<const uint16_t*>(blob + a.off[proj][2]) + (long long)orow * G;
-    // (scale | bias << 16) of K tiles kt .. kt + SCALE_AHEAD - 1, a shifting ring
-    uint32_t sb[SCALE_AHEAD];
+  } else if (warp >= 4 && warp < 20) {
+    // ---- dequantise: TMEM lane L = one weight row; this warp takes columns
+    // [8*part, 8*part + 8) of each K tile (16 codes)
+    const int quarter = warp & 3, part = (warp - 4) >> 2;
+    const int L = quarter * 32 + lane;
+    // this lane's row inside the tile of codes (PHASE 0: gate rows 0-63,
+    // then up rows 64-127 of the shared-memory tile)
+    const int prow = PHASE == 0 ? ((lane < 16 ? 0 : 64) + 16 * quarter + (lane & 15)) : L;
+    const int proj = PHASE == 0 ? (lane < 16 ? 0 : 1) : 2;
+    // scale/bias prefetch cursor: item pw, K tile pkt, SCALE_AHEAD K tiles
+    // ahead of the work and running across item boundaries. Every load
+    // address is valid (rows without weights read row 0 of slot 0 and are
+    // masked when consumed), so no load is ever waited on early.
+    int pw = blockIdx.x, pkt = 0;
+    const uint16_t *psc = nullptr, *pbi = nullptr;
+    bool pact = false;
+    GemmTile pnext = a.tiles[pw / n_ft];
+    auto enter = [&](int w) {                  // the cursor enters item w (pnext = its tile)
+      const GemmTile tt = pnext;
+      if (w + step < total) pnext = a.tiles[(w + step) / n_ft];
+      const int orow = (w % n_ft) * FT + (PHASE == 0 ? 16 * quarter + (lane & 15) : L);
+      pact = tt.slot >= 0 && orow < n_out;
+      const uint8_t* blob = a.arena + (long long)(pact ? tt.slot : 0) * a.blob;
+      const long long ro = pact ? (long long)orow * G : 0;
+      psc = reinterpret_cast<const uint16_t*>(blob + a.off[proj][1]) + ro;
+      pbi = reinterpret_cast<const uint16_t*>(blob + a.off[proj][2]) + ro;
+    };
+    auto fetch = [&](uint16_t& sv, uint16_t& bv, bool& av) {
+      av = pact && pw < total;
+      sv = psc[pkt];
+      bv = pbi[pkt];
+      if (++pkt == KT) {
+        pkt = 0;
+        pw += step;
+        if (pw < total) enter(pw);
+      }
+    };
+    enter(pw);
+    uint16_t rs[SCALE_AHEAD], rb[SCALE_AHEAD];
+    bool ra[SCALE_AHEAD];
 #pragma unroll
-    for (int i = 0; i < SCALE_AHEAD; ++i)
-      sb[i] = (active && i < KT) ? ((uint32_t)Sc[i] | ((uint32_t)Bi[i] << 16)) : 0u;
+    for (int i = 0; i < SCALE_AHEAD; ++i) fetch(rs[i], rb[i], ra[i]);
     const float2 magic_off = make_float2(-8388608.f, -8388608.f);
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
-    for (int kt = 0; kt < KT; ++kt) {
-      const int sx = kt % GM_STAGES, sa = kt % GM_A_STAGES;
-      const float sc = __uint_as_float(sb[0] << 16), bi = __uint_as_float(sb[0] & 0xffff0000u);
+    const int n_it = ((total - (int)blockIdx.x + step - 1) / step) * KT;   // K tiles of this CTA
+    bool ok = true;
+    // one flat loop over this CTA's K tiles, unrolled so that every ring
+    // entry is a fixed register
+    for (int it0 = 0; it0 < n_it && ok; it0 += SCALE_AHEAD) {
 #pragma unroll
-      for (int i = 0; i + 1 < SCALE_AHEAD; ++i) sb[i] = sb[i + 1];
-      const int kn = kt + SCALE_AHEAD;
-      sb[SCALE_AHEAD - 1] = (active && kn < KT) ? ((uint32_t)Sc[kn] | ((uint32_t)Bi[kn] << 16)) : 0u;
-      // every lane waits; the warp goes on only if all of them saw the stage
-      bool got = mbar_wait(&full[sx], (kt / GM_STAGES) & 1, a.status);
-      if (got && kt >= GM_A_STAGES)
-        got = mbar_wait(&empty_a[sa], ((kt / GM_A_STAGES) - 1) & 1, a.status);
-      if (!__all_sync(MS_FULL, got)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t wh[16], wl[16];
-      if (active) {
-        const uint4 pw = *reinterpret_cast<const uint4*>(sP(sx) + r * 32 + half * 16);
-        const uint32_t words[4] = {pw.x, pw.y, pw.z, pw.w};
+      for (int j = 0; j < SCALE_AHEAD; ++j) {
+        const int it = it0 + j;
+        if (it >= n_it || !ok) continue;
+        const float sc = ra[j] ? bf2f(rs[j]) : 0.f, bi = ra[j] ? bf2f(rb[j]) : 0.f;
+        fetch(rs[j], rb[j], ra[j]);
+        const int sx = it % GM_STAGES, sa = it % GM_A_STAGES;
+        // every lane waits; the warp goes on only if all of them saw the stage
+        bool got = mbar_wait(&full[sx], (it / GM_STAGES) & 1, a.status);
+        if (got && it >= GM_A_STAGES)
+          got = mbar_wait(&empty_a[sa], ((it / GM_A_STAGES) - 1) & 1, a.status);
+        if (!__all_sync(MS_FULL, got)) {
+          ok = false;
+          continue;
+        }
+        tc_fence_after();
+        uint32_t wh[8], wl[8];
+        const uint2 pw2 = *reinterpret_cast<const uint2*>(sP(sx) + prow * 32 + part * 8);
+        const uint32_t words[2] = {pw2.x, pw2.y};
         const float2 s2 = make_float2(sc, sc), b2 = make_float2(bi, bi);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 2; ++i) {
           const uint32_t u = words[i];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            // q_j and q_j+4 as exact floats (2^23 + q, minus 2^23)
-            const uint32_t m = (u >> (4 * j)) & 0x000F000Fu;
+          for (int q4 = 0; q4 < 4; ++q4) {
+            // q and q+4 of this word as exact floats (2^23 + q, minus 2^23)
+            const uint32_t m = (u >> (4 * q4)) & 0x000F000Fu;
             const float2 q = __fadd2_rn(make_float2(__uint_as_float((m & 0xFu) | 0x4B000000u),
                                                     __uint_as_float((m >> 16) | 0x4B000000u)),
                                         magic_off);
-            const float2 w = __ffma2_rn(q, s2, b2);             // exact: s*q + b
-            const __half2 hi = __floats2half2_rn(w.x, w.y);
+            const float2 wv = __ffma2_rn(q, s2, b2);            // exact: s*q + b
+            const __half2 hi = __floats2half2_rn(wv.x, wv.y);
             const float2 hf = __half22float2(hi);
-            const float2 lo = __fadd2_rn(w, make_float2(-hf.x, -hf.y));
-            wh[i * 4 + j] = *reinterpret_cast<const uint32_t*>(&hi);
-            wl[i * 4 + j] = h2_bits(lo.x, lo.y);
+            const float2 lo = __fadd2_rn(wv, make_float2(-hf.x, -hf.y));
+            wh[i * 4 + q4] = *reinterpret_cast<const uint32_t*>(&hi);
+            wl[i * 4 + q4] = h2_bits(lo.x, lo.y);
+          }
+        }
+        const uint32_t col = TM_A + sa * 64 + part * 8;
+        tmem_st8(lane_base + col, wh);
+        tmem_st8(lane_base + col + 32, wl);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&deq[sa]);
+      }
+    }
+  } else if (warp >= 20) {
+    // ---- epilogue: lanes [32*quarter, +32) of each finished accumulator
+    const int quarter = warp & 3;
+    const int L = quarter * 32 + lane;
+    int ai = 0;
+    GemmTile tn = a.tiles[blockIdx.x / n_ft];
+    for (int w = blockIdx.x; w < total; w += step, ++ai) {
+      const GemmTile t = tn;
+      if (w + step < total) tn = a.tiles[(w + step) / n_ft];
+      const int f0 = (w % n_ft) * FT;
+      const int b = ai & 1;
+      const int ntok = (t.rows + 15) & ~15;
+      // routing scores of the item's tokens, lane l holding tokens l + 32 i
+      float sc4[GM_TOK / 32];
+#pragma unroll
+      for (int i = 0; i < GM_TOK / 32; ++i)
+        sc4[i] = (PHASE == 1 && i * 32 + lane < t.rows) ? a.perm_score[t.row0 + i * 32 + lane] : 0.f;
+      if (!__all_sync(MS_FULL, mbar_wait(&acc_full[b], (ai >> 1) & 1, a.status))) break;
+      tc_fence_after();
+      const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + TM_ACC + b * GM_TOK;
+      const uint8_t* blob = a.arena + (long long)(t.slot >= 0 ? t.slot : 0) * a.blob;
+      if (PHASE == 0) {
+        const bool is_up = lane >= 16;
+        const int fg = f0 + 16 * quarter + (lane & 15);     // feature index in d_ff
+        const int pos = (fg & ~7) | kperm_pos(fg & 7);      // its k-permuted h column
+        const float bias = (a.model == 1 && t.slot >= 0)
+                               ? bf2f(reinterpret_cast<const uint16_t*>(blob + a.off[is_up ? 1 : 0][3])[fg])
+                               : 0.f;
+        uint16_t* hrow = a.H + (long long)t.row0 * a.ld_out + pos;
+        for (int c0 = 0; c0 < ntok; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(lane_base + c0, v);
+          float vf[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float x = bfr(__uint_as_float(v[j]));
+            if (a.model == 1) x = bfr(x + bias);
+            vf[j] = x;
+          }
+          // gate lane l and up lane l + 16 hold the same feature: the gate
+          // lane forms tokens c0..c0+7, the up lane tokens c0+8..c0+15
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float other = __shfl_xor_sync(MS_FULL, is_up ? vf[j] : vf[8 + j], 16);
+            const float g = is_up ? other : vf[j];
+            const float u = is_up ? vf[8 + j] : other;
+            const int m = c0 + (is_up ? 8 : 0) + j;
+            const float h = t.slot >= 0 ? g_swiglu(a.model, g, u) : 0.f;
+            if (m < t.rows) hrow[(long long)m * a.ld_out] = __half_as_ushort(__float2half_rn(h));
           }
         }
       } else {
+        const int fo = f0 + L;                 // output feature
+        const bool f_ok = fo < n_out;
+        const float bias = (a.model == 1 && f_ok && t.slot >= 0)
+                               ? bf2f(reinterpret_cast<const uint16_t*>(blob + a.off[2][3])[fo]) : 0.f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) wh[i] = wl[i] = 0u;
+        for (int c0 = 0; c0 < GM_TOK; c0 += 16) {
+          if (c0 >= ntok) continue;
+          uint32_t v[16];
+          tmem_ld16(lane_base + c0, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = c0 + j;
+            const float score = __shfl_sync(MS_FULL, sc4[m >> 5], m & 31);
+            if (m < t.rows && f_ok) {
+              float y = bfr(__uint_as_float(v[j]));
+              if (a.model == 1) y = bfr(y + bias);
+              // (y * scores) is a bf16 product (engine_v3.py:600)
+              const uint16_t o = t.slot >= 0 ? f2bf(score * y) : (uint16_t)0;
+              a.Y[(long long)(t.row0 + m) * a.ld_out + fo] = o;
+            }
+          }
+        }
       }
-      const uint32_t col = TM_A + sa * 64 + half * 16;
-      tmem_st16(lane_base + col, wh);
-      tmem_st16(lane_base + col + 32, wl);
-      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&deq[sa]);
-    }
-    // ---- epilogue. Each warp reads lanes [32*quarter, +32) and token
-    // columns [128*half, +128) of the accumulator into the staging area S
-    // (the token ring, idle once the accumulator is complete), as fp32
-    // S[token][lane]; then the 256 threads write whole 16-byte chunks.
-    if (ok) ok = __all_sync(MS_FULL, mbar_wait(accf, 0, a.status));
-    tc_fence_after();
-    float* S = reinterpret_cast<float*>(smem);
-    const int c_lo = half * 128, c_hi = min(ntok, c_lo + 128);
-    const int et = threadIdx.x - 128;          // 0..255
-    if (PHASE == 0) {
-      // lanes 0-63: gate + bias, 64-127: up + bias, both bf16-rounded
-      const int fg = f0 + (r & 63);
-      const float bias = a.model == 1 ? bf2f(reinterpret_cast<const uint16_t*>(
-                                                blob + a.off[r < 64 ? 0 : 1][3])[fg])
-                                      : 0.f;
-      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(lane_base + TM_ACC + c0, v);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float g = bfr(__uint_as_float(v[j]));
-          if (a.model == 1) g = bfr(g + bias);
-          S[(c0 + j) * 128 + r] = g;
-        }
-      }
-      epi_sync();
-      // h for 8 consecutive features of one token per task, k-permuted, fp16
-      for (int task = et; task < t.rows * 8; task += 256) {
-        const int m = task >> 3, c8 = (task & 7) * 8;
-        const float4* gs = reinterpret_cast<const float4*>(S + m * 128 + c8);
-        const float4 g0 = gs[0], g1 = gs[1], u0 = gs[16], u1 = gs[17];
-        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-        const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-        float hv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) hv[kperm_pos(j)] = g_swiglu(a.model, gv[j], uv[j]);
-        if (ok)
-          *reinterpret_cast<uint4*>(a.H + (long long)(t.row0 + m) * a.ld_out + f0 + c8) =
-              make_uint4(h2_bits(hv[0], hv[1]), h2_bits(hv[2], hv[3]), h2_bits(hv[4], hv[5]),
-                         h2_bits(hv[6], hv[7]));
-      }
-    } else {
-      const int fo = f0 + r;                   // output feature
-      const float bias = (a.model == 1 && fo < n_out)
-                             ? bf2f(reinterpret_cast<const uint16_t*>(blob + a.off[2][3])[fo]) : 0.f;
-      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(lane_base + TM_ACC + c0, v);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float y = bfr(__uint_as_float(v[j]));
-          if (a.model == 1) y = bfr(y + bias);
-          S[(c0 + j) * 128 + r] = y;
-        }
-      }
-      epi_sync();
-      // (y * scores) is a bf16 product (engine_v3.py:600); 8 features per task
-      const int nf = min(128, n_out - f0);     // a multiple of 8 (d_model % 64 == 0)
-      const int chunks = nf >> 3;
-      for (int task = et; task < t.rows * chunks; task += 256) {
-        const int m = task / chunks, c8 = (task % chunks) * 8;
-        const float sc = a.perm_score[t.row0 + m];
-        const float4* y4 = reinterpret_cast<const float4*>(S + m * 128 + c8);
-        const float4 y0 = y4[0], y1 = y4[1];
-        const float ys[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          o[j] = (uint32_t)f2bf(sc * ys[2 * j]) | ((uint32_t)f2bf(sc * ys[2 * j + 1]) << 16);
-        if (ok)
-          *reinterpret_cast<uint4*>(a.Y + (long long)(t.row0 + m) * a.ld_out + f0 + c8) =
-              make_uint4(o[0], o[1], o[2], o[3]);
-      }
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
   tc_fence_before();
@@ -566,20 +617,21 @@ cudaError_t launch_combine(const CombineArgs& a, int grid, cudaStream_t s) {
 
 template <int PHASE>
 static cudaError_t launch_gemm_t(const CUtensorMap& tX, const CUtensorMap& tW0,
-                                 const CUtensorMap& tW1, const GemmArgs& a, int n_col_tiles,
-                                 int max_tiles, cudaStream_t s) {
+                                 const CUtensorMap& tW1, const GemmArgs& a, int grid,
+                                 cudaStream_t s) {
   auto kern = k_gemm<PHASE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(n_col_tiles, max_tiles), GM_THREADS, GM_SMEM, s>>>(tX, tW0, tW1, a);
+  kern<<<grid, GM_THREADS, GM_SMEM, s>>>(tX, tW0, tW1, a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_gemm(int phase, const CUtensorMap& tX, const CUtensorMap& tW0,
-                        const CUtensorMap& tW1, const GemmArgs& a, int n_col_tiles, int max_tiles,
+                        const CUtensorMap& tW1, const GemmArgs& a, int max_items, int sms,
                         cudaStream_t s) {
-  if (phase == 0) return launch_gemm_t<0>(tX, tW0, tW1, a, n_col_tiles, max_tiles, s);
-  return launch_gemm_t<1>(tX, tW0, tW1, a, n_col_tiles, max_tiles, s);
+  const int grid = std::max(1, std::min(max_items, sms));
+  if (phase == 0) return launch_gemm_t<0>(tX, tW0, tW1, a, grid, s);
+  return launch_gemm_t<1>(tX, tW0, tW1, a, grid, s);
 }
 
 }  // namespace ms

@@ -88,7 +88,8 @@ struct ExpArgs {
 // A token tile of the grouped GEMM (at most 256 rows): rows [row0, row0 +
 // rows) of the expert-ordered pair list, all routed to group g.
 struct GemmTile {
-  int g, row0, rows, pad;
+  int g, row0, rows;
+  int slot;                   // the group's slot, -1 when the pool could not place it
 };
 
 struct WideArgs {
@@ -122,7 +123,6 @@ struct GemmArgs {
   int n_out;                  // output rows of the projection: d_ff (phase 0) or d_model
   const GemmTile* tiles;
   const int* n_tiles;
-  const int* grp_slot;
   uint16_t* H;                // phase 0 output, fp16 [P_pad, d_ff], k-permuted columns
   uint16_t* Y;                // phase 1 output, bf16 [P_pad, d_model], score-weighted
   int ld_out;
@@ -140,8 +140,10 @@ struct CombineArgs {
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s);
 cudaError_t launch_route_wide(const RouteArgs& a, const WideArgs& w, cudaStream_t s);
 cudaError_t launch_scatter(const ScatterArgs& a, int grid, cudaStream_t s);
+// Persistent grouped GEMM over at most max_items (token tile, feature tile)
+// items, one CTA per SM (sms).
 cudaError_t launch_gemm(int phase, const CUtensorMap& tX, const CUtensorMap& tW0,
-                        const CUtensorMap& tW1, const GemmArgs& a, int n_col_tiles, int max_tiles,
+                        const CUtensorMap& tW1, const GemmArgs& a, int max_items, int sms,
                         cudaStream_t s);
 cudaError_t launch_combine(const CombineArgs& a, int grid, cudaStream_t s);
 // Tensor maps of the grouped GEMM. 0 on success.
@@ -149,7 +151,7 @@ int encode_act_map(CUtensorMap* m, const void* base, int K, long long rows);
 int encode_weight_map(CUtensorMap* m, const void* base, int K, int rows_out, int n_slots,
                       long long blob, int box_rows);
 // Token rows per GEMM tile.
-constexpr int GEMM_TILE_ROWS = 256;
+constexpr int GEMM_TILE_ROWS = 128;
 cudaError_t launch_pool_op(const DevTable& t, const PoolReq& r, int* slots_out, int* st,
                            cudaStream_t s);
 cudaError_t launch_fill(const FillArgs& f, int grid, cudaStream_t s);

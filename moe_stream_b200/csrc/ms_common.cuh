@@ -77,12 +77,9 @@ struct Geo {
 __device__ __forceinline__ float bf2f(uint16_t b) {
   return __uint_as_float(((uint32_t)b) << 16);
 }
-// round-to-nearest-even float -> bf16 bits (finite inputs)
+// round-to-nearest-even float -> bf16 bits (the hardware conversion)
 __device__ __forceinline__ uint16_t f2bf(float f) {
-  uint32_t u = __float_as_uint(f);
-  if ((u & 0x7f800000u) == 0x7f800000u) return (uint16_t)((u >> 16) | ((u & 0xffff) ? 0x40 : 0));
-  u += 0x7fffu + ((u >> 16) & 1u);
-  return (uint16_t)(u >> 16);
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 __device__ __forceinline__ float bfr(float f) { return bf2f(f2bf(f)); }
 

@@ -510,7 +510,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_wide(RouteArgs A, WideArgs
           tl.g = gi;
           tl.row0 = start + j * GEMM_TILE_ROWS;
           tl.rows = min(GEMM_TILE_ROWS, cnt - j * GEMM_TILE_ROWS);
-          tl.pad = 0;
+          tl.slot = s_slots[gi];
           W.tiles[first + j] = tl;
         }
       }

@@ -53,15 +53,28 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Bounded wait for phase `phase` of `bar`: at most MBAR_SPIN_LIMIT polls
-// and MBAR_WAIT_NS of wall time. Returns false (and sets *status to
-// MS_E_TIMEOUT once) if either limit ran out.
+// try_wait that may suspend the thread until the phase completes, for at
+// most hint_ns: a waiting warp then leaves its issue slots to the others.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, unsigned phase, unsigned hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for phase `phase` of `bar`: suspending polls, at most
+// MBAR_SPIN_LIMIT of them and MBAR_WAIT_NS of wall time. Returns false (and
+// sets *status to MS_E_TIMEOUT once) if either limit ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, int* status) {
   if (mbar_try_wait(bar, phase)) return true;
   const unsigned long long t0 = global_ns();
   for (unsigned i = 0; i < MBAR_SPIN_LIMIT; ++i) {
-    if (mbar_try_wait(bar, phase)) return true;
-    if ((i & 255u) == 255u && global_ns() - t0 > MBAR_WAIT_NS) break;
+    if (mbar_try_wait_sleep(bar, phase, 100000u)) return true;
+    if (global_ns() - t0 > MBAR_WAIT_NS) break;
   }
   if (status) atomicCAS(status, 0, -4);
   return false;
