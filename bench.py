@@ -42,10 +42,14 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-sample-layers", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=["stack", "layer"], default="stack",
+    ap.add_argument("--case", choices=["stack", "layer", "prefill"], default="stack",
                     help="layer: a 2-layer Qwen3 stack with every expert resident (a small "
-                         "case for ncu section captures); prints per-call timings only")
-    ap.add_argument("--tokens", type=int, default=1)
+                         "case for ncu section captures); prints per-call timings only. "
+                         "prefill: one MoE layer on a large token batch (config 2: qwen3, "
+                         "T=4096; config 3: gptoss, T=512; config 4 on one GPU: gptoss, "
+                         "T=16384), the grouped tcgen05 GEMM path")
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--model", choices=["qwen3", "gptoss"], default="qwen3")
     return ap.parse_args()
 
 
@@ -59,12 +63,12 @@ def layer_case(args):
     from moe_stream_b200.pool import ExpertPool
     torch.cuda.set_device(0)
     geom = geometry.qwen3(2)
-    pool = ExpertPool(geom, geom.n_keys, depths=(1,), max_tokens=max(1, args.tokens))
+    pool = ExpertPool(geom, geom.n_keys, depths=(1,), max_tokens=max(1, args.tokens or 1))
     st = torch.from_numpy(pool.alloc_store()).view(geom.n_keys, geom.blob_bytes)
     for layer in range(2):
         st[layer * 128:(layer + 1) * 128].copy_(S.make_layer_blobs(geom, SEED, layer))
     blocks = [MoEBlock(pool, l, *S.router_weights(geom, SEED, l, zipf_s=1.1)) for l in range(2)]
-    T = args.tokens
+    T = args.tokens or 1
     n = args.warmup + args.steps
     x = S.decode_inputs(n * T, 1, geom.d_model, SEED).cuda().reshape(-1, geom.d_model)
     for i in range(args.warmup):
@@ -80,6 +84,126 @@ def layer_case(args):
     print(json.dumps({"case": "layer", "tokens": T, "calls": args.steps,
                       "us_per_call": e0.elapsed_time(e1) * 1e3 / args.steps}))
     pool.close()
+
+
+def prefill_case(args):
+    """One MoE layer of BASELINE config 2 / 3 / 4 on one GPU: T tokens routed
+    over 128 resident experts (the pool holds the whole layer), grouped
+    tcgen05 GEMMs. A step is one block call on T tokens."""
+    import ctypes
+    import torch
+    from moe_stream_b200 import _lib, geometry, store as S
+    from moe_stream_b200.block import MoEBlock
+    from moe_stream_b200.pool import ExpertPool
+    torch.cuda.set_device(0)
+    model = args.model
+    T = args.tokens or (4096 if model == "qwen3" else 512)
+    geom = geometry.qwen3(1) if model == "qwen3" else geometry.gptoss(1)
+    E = geom.n_experts
+    pool = ExpertPool(geom, E, depths=(), max_tokens=T)
+    st = torch.from_numpy(pool.alloc_store()).view(geom.n_keys, geom.blob_bytes)
+    st.copy_(S.make_layer_blobs(geom, SEED, 0).cpu())
+    zipf = 1.1 if (model == "qwen3" or T >= 16384) else None
+    w, b = S.router_weights(geom, SEED, 0, zipf_s=zipf)
+    blk = MoEBlock(pool, 0, w, b)
+    W, K = max(3, args.warmup), args.steps
+    xs = [S.rms_norm_tokens(T, geom.d_model, seed=SEED + 100 + i, device="cuda") for i in range(2)]
+    y = torch.empty_like(xs[0])
+    for i in range(W):
+        blk(xs[i % 2], out=y)
+    torch.cuda.synchronize()
+    pool.status()
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        blk(xs[i % 2], out=y)
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    pool.status()
+    ms = e0.elapsed_time(e1) / K
+    # expert phase (scatter, two grouped GEMMs, combine) timed by the
+    # library's own events around it
+    _lib.check(pool._lib.ms_pool_profile(pool._h, 1))
+    buf = (ctypes.c_float * 3)()
+    acc = [0.0, 0.0, 0.0]
+    n_prof = max(3, min(K, 10))
+    for i in range(n_prof):
+        blk(xs[i % 2], out=y)
+        torch.cuda.synchronize()
+        _lib.check(pool._lib.ms_pool_timing(pool._h, 0, buf))
+        for j in range(3):
+            acc[j] += buf[j] / n_prof
+    _lib.check(pool._lib.ms_pool_profile(pool._h, 0))
+    flops = 2.0 * T * geom.top_k * 3 * geom.d_model * geom.d_ff
+    peaks, peak_kind = measured_peaks()
+    achieved = flops / (acc[2] * 1e-3) / 1e12
+    # e2e: pinned host tokens in, block, pinned host result out
+    xh = xs[0].cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    xd = torch.empty_like(xs[0])
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(K):
+        xd.copy_(xh, non_blocking=True)
+        blk(xd, out=y)
+        yh.copy_(y, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+    pool.status()
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = prefill_cpu_baseline(geom, st, w, b, xs[0], model, n_tok=16)
+    cfg = {"qwen3": "config2: qwen3 layer, 128 experts resident, top-8",
+           "gptoss": "config3/4 (1 GPU): gpt-oss layer, 128 experts resident, top-4"}[model]
+    line = {
+        "metric": "MoE-block prefill tok/s (one layer, grouped tcgen05 GEMM)",
+        "value": T / (ms * 1e-3), "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u4 weights as exact fp16 hi+lo pairs x fp16 tokens, f32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, MLX affine 4-bit g64; N(0,1) RMS-normed tokens)",
+        "config": {"workload": cfg, "tokens": T, "top_k": geom.top_k, "d_model": geom.d_model,
+                   "d_ff": geom.d_ff, "router_bias": "Zipf(1.1)" if zipf else "none",
+                   "l2": "inputs larger than L2: %.0f MB of expert weights" % (E * geom.payload_bytes / 1e6)},
+        "per_call_us": {"router_table": acc[0] * 1e3, "fill": acc[1] * 1e3, "experts": acc[2] * 1e3},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                     "peak_kind": peak_kind,
+                     "kernel": "expert phase: scatter + k_gemm<0> + k_gemm<1> + combine",
+                     "algorithmic_flops_per_launch": flops,
+                     "note": "algorithmic flops count one MMA pass; the exact hi+lo split runs two"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tok/s",
+                "h2d_bytes_per_step": int(xh.numel() * 2), "d2h_bytes_per_step": int(yh.numel() * 2),
+                "path": "MoEBlock.__call__ (ms_moe_block), pinned host x in / y out"},
+        "gpu_launches": 7 * K,
+        "clocks": clk,
+    }
+    print(json.dumps(line))
+    pool.close()
+
+
+def prefill_cpu_baseline(geom, st, w, b, x, model, n_tok):
+    """The oracle on the first n_tok tokens of the batch (routing + every
+    routed expert of those tokens), scaled to tok/s."""
+    import numpy as np
+    from oracle import moe as OM
+    comps = [dict(c) for c in geom.components]
+    xn = x[:n_tok].float().cpu().numpy()
+    t0 = time.perf_counter()
+    f = lambda t: None if t is None else t.float().numpy()
+    if model == "qwen3":
+        inds, scores, _ = OM.route_qwen3(xn, f(w), geom.top_k, True, f(b))
+    else:
+        inds, scores, _ = OM.route_gptoss(xn, f(w), geom.top_k, f(b))
+    blobs = {int(e): st[int(e)].numpy() for e in np.unique(inds)}
+    OM.expert_block(xn, inds, scores, blobs, comps, model)
+    dt = time.perf_counter() - t0
+    return {"value": n_tok / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n_tok} tokens of the batch ({dt:.1f} s): routing and every routed expert"}
 
 
 # ------------------------------------------------------------------ clocks
@@ -394,6 +518,9 @@ def main():
         return
     if args.case == "layer":
         layer_case(args)
+        return
+    if args.case == "prefill":
+        prefill_case(args)
         return
     gpu_arm(args)
 
