@@ -178,7 +178,10 @@ int ms_pool_status(ms_pool* pool, void* stream);
 
 /* kernels.moe_expert_mlp (kernels.py:231-252), generalised to T tokens:
  * slots int32 [T, k] and scores f32 [T, k] (device), x bf16 [T, d_model],
- * y bf16 [T, d_model]. Reads the arena only; no routing, no table. */
+ * y bf16 [T, d_model]. Reads the arena only; no routing, no table.
+ * k = top_k with T*k <= MS_MLP_MAX_PAIRS runs the decode kernels; larger
+ * batches, and any 1 <= k < top_k, run the grouped tensor-core GEMM (the
+ * pool's max_tokens * top_k bounds T*k there). */
 int ms_expert_mlp(ms_pool* pool, const int32_t* slots, const float* scores,
                   const void* x, int T, int k, void* y, void* stream);
 
@@ -196,6 +199,29 @@ int ms_block_debug(ms_pool* pool, const int32_t** inds, const void** scores,
  * out[0] router+table, out[1] fills, out[2] expert kernels. */
 int ms_pool_profile(ms_pool* pool, int enable);
 int ms_pool_timing(ms_pool* pool, int layer, float* out3);
+
+/* Expert parallelism, no counterpart in the reference,
+ * which runs on one device; the block it distributes is engine_120b.py:78-149.
+ * Rank r of `world` holds experts [r * e_local, (r + 1) * e_local) in its pool,
+ * expert r * e_local + i in slot i. The host moves the buffers between ranks
+ * (an all-to-all over NCCL) and runs the experts with ms_expert_mlp (k = 1).
+ *
+ * ms_ep_pack: the T*top_k token/expert pairs of x (routing from ms_route:
+ * inds int32 [T, top_k], scores bf16 [T, top_k]) packed destination-major:
+ * send_x bf16 [T*top_k, d_model] (the token's row), send_meta int32
+ * [T*top_k][2] (slot on the destination, score as f32 bits), send_counts int32
+ * [world] (pairs per destination, device memory), pair_pos int32 [T*top_k]
+ * (row of each pair in send_x). Rows inside a destination come in no fixed
+ * order. */
+int ms_ep_pack(ms_pool* pool, const void* x, int T, const int32_t* inds, const void* scores,
+               int world, int e_local, void* send_x, int32_t* send_meta, int32_t* send_counts,
+               int32_t* pair_pos, void* stream);
+
+/* ms_ep_combine: y[t] = sum over j of back[pair_pos[t*top_k + j]] (the
+ * score-weighted expert outputs returned to their senders), summed in fp32 in
+ * j order and rounded once to bf16, as the single-device block does. */
+int ms_ep_combine(ms_pool* pool, const void* back, const int32_t* pair_pos, int T, void* y,
+                  void* stream);
 
 /* ms_expert_mlp without a pool and without any allocation. This entry point
  * has no counterpart in the reference. It is for callers that may not call

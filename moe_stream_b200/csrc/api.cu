@@ -105,6 +105,9 @@ struct ms_pool {
   uint16_t* hbuf = nullptr;
   uint16_t* ybuf = nullptr;
   CUtensorMap tm_x{}, tm_h{}, tm_wg{}, tm_wu{}, tm_wd{};
+  int* mlp_cnt = nullptr;       // [n_slots + 1] pairs per slot (wide ms_expert_mlp)
+  int* mlp_wkeys = nullptr;     // [max_pairs] sanitised slot keys (wide ms_expert_mlp)
+  int* ep_scratch = nullptr;    // [128]: counts and cursors of ms_ep_pack
   bool profile = false;
   std::vector<cudaEvent_t> prof_ev;   // [n_layers][4]
 };
@@ -193,10 +196,16 @@ int setup_wide(ms_pool* p) {
   p->p_pad = (P + GEMM_TILE_ROWS - 1) / GEMM_TILE_ROWS * GEMM_TILE_ROWS;
   int rc;
   WideArgs& w = p->wa;
-  w.max_tiles = (int)std::min<long long>(P / GEMM_TILE_ROWS + std::min<long long>(E, P) + 1, 65535);
+  // groups: experts on the routed path, slots (up to n_slots + 1) on the
+  // ms_expert_mlp path
+  const long long n_keys = std::max<long long>(E, (long long)p->cfg.n_slots + 1);
+  w.max_tiles = (int)std::min<long long>(P / GEMM_TILE_ROWS + std::min<long long>(n_keys, P) + 1, 65535);
   if ((rc = palloc(p, &w.cnt_e, 256))) return rc;
   if ((rc = palloc(p, &w.pmask, MS_MAX_DEPTHS * 8))) return rc;
-  if ((rc = palloc(p, &w.cursor, 256))) return rc;
+  if ((rc = palloc(p, &w.cursor, std::max<long long>(256, n_keys)))) return rc;
+  if ((rc = palloc(p, &p->mlp_cnt, p->cfg.n_slots + 1))) return rc;
+  if ((rc = palloc(p, &p->mlp_wkeys, P))) return rc;
+  CK(cudaMemset(p->mlp_cnt, 0, sizeof(int) * (p->cfg.n_slots + 1)));
   if ((rc = palloc(p, &w.tiles, w.max_tiles))) return rc;
   if ((rc = palloc(p, &w.n_tiles, 1))) return rc;
   CK(cudaMemset(w.cnt_e, 0, sizeof(int) * 256));
@@ -342,6 +351,7 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   if ((rc = palloc(p, &p->grp.grp_pairs, P))) return bail(rc);
   if ((rc = palloc(p, &p->grp.map, key_range))) return bail(rc);
   CK(cudaMemset(p->grp.n_groups, 0, sizeof(int)));
+  if ((rc = palloc(p, &p->ep_scratch, 128))) return bail(rc);
   if ((rc = palloc(p, &p->d_slots, MS_MAX_REQ))) return bail(rc);
   if ((rc = palloc(p, &p->d_opstatus, 1))) return bail(rc);
   if (cudaMallocHost(reinterpret_cast<void**>(&p->h_pinned), sizeof(int) * (MS_MAX_REQ + 1)) !=
@@ -591,8 +601,10 @@ int ms_route(ms_pool* p, int layer, const void* x, int T, int32_t* inds, void* s
   if (!p) return fail(MS_E_INVALID, "NULL pool");
   if (!inds || !scores) return fail(MS_E_INVALID, "inds/scores are NULL");
   if (pred && p->cfg.n_depths == 0) return fail(MS_E_INVALID, "pred requested but no prefetch depth configured");
-  // batches past the decode scratch are routed by the tiled router
-  const bool wide = T > p->narrow_tokens;
+  // the router ms_moe_block would use for this batch: the tiled router for
+  // wide batches (and whenever the batch exceeds the decode scratch)
+  const bool wide = T > p->narrow_tokens ||
+                    (p->wide && (long long)T * p->geom.top_k >= p->wide_min_pairs);
   return route_common(p, layer, x, T, static_cast<cudaStream_t>(stream), false, wide, inds, scores,
                       pred);
 }
@@ -618,21 +630,24 @@ static ExpArgs exp_args(ms_pool* p, const void* x, int T, void* y, const float* 
 
 // Expert MLPs of a routed wide batch: pairs scattered into expert order,
 // the two grouped GEMMs, the weighted combine.
-static int wide_experts(ms_pool* p, const void* x, int T, void* y, cudaStream_t s) {
-  const int k = p->geom.top_k, P = T * k;
+// keys: the group key of every pair (expert id after the wide router, slot
+// after launch_mlp_wide_prep); the groups and tiles are already laid out.
+static int wide_experts(ms_pool* p, const void* x, int T, int k, const int* keys,
+                        const float* scores, int* pair_slot, void* y, cudaStream_t s) {
+  const int P = T * k;
   ScatterArgs sa{};
   sa.x = static_cast<const uint16_t*>(x);
   sa.T = T;
   sa.k = k;
   sa.d = p->geom.d_model;
-  sa.inds = p->inds;
-  sa.scores_f = p->scores_f;
+  sa.inds = keys;
+  sa.scores_f = scores;
   sa.grp = p->grp;
   sa.cursor = p->wa.cursor;
   sa.xperm = p->xperm;
   sa.perm_score = p->perm_score;
   sa.inv = p->inv;
-  sa.pair_slot = p->pair_slot;
+  sa.pair_slot = pair_slot;
   CK(launch_scatter(sa, std::min((P + 7) / 8, p->sm_count * 8), s));
   GemmArgs g{};
   g.model = p->geo.model;
@@ -695,7 +710,7 @@ int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* str
   CK(launch_fill(fill_args(p), p->sm_count * 2, s));
   if (ev) CK(cudaEventRecordWithFlags(ev[2], s, rec_flags));
   if (wide) {
-    if ((rc = wide_experts(p, x, T, y, s))) return rc;
+    if ((rc = wide_experts(p, x, T, k, p->inds, p->scores_f, p->pair_slot, y, s))) return rc;
   } else {
     const int max_groups = std::min(T * k, p->geom.n_experts);
     CK(launch_expert(exp_args(p, x, T, y, p->scores_f), max_groups, s));
@@ -722,12 +737,33 @@ int ms_expert_mlp(ms_pool* p, const int32_t* slots, const float* scores, const v
                   int k, void* y, void* stream) {
   if (!p) return fail(MS_E_INVALID, "NULL pool");
   if (!slots || !scores || !x || !y) return fail(MS_E_INVALID, "NULL argument");
-  if (k != p->geom.top_k) return fail(MS_E_INVALID, "k=%d must equal top_k=%d", k, p->geom.top_k);
-  if (T <= 0 || T > p->cfg.max_tokens || T * k > MS_MLP_MAX_PAIRS)
-    return fail(MS_E_INVALID, "T=%d outside [1, min(max_tokens, %d/k)]", T, MS_MLP_MAX_PAIRS);
+  if (k <= 0 || k > p->geom.top_k) return fail(MS_E_INVALID, "k=%d outside [1, top_k=%d]", k, p->geom.top_k);
+  if (T <= 0) return fail(MS_E_INVALID, "T=%d must be positive", T);
   if (!aligned16(x) || !aligned16(y)) return fail(MS_E_INVALID, "x and y must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CK(cudaSetDevice(p->device));
+  // wide batches (and any k other than top_k): slot-keyed grouped GEMM
+  const long long P = (long long)T * k;
+  const bool wide = p->wide && P <= p->max_pairs &&
+                    (k != p->geom.top_k || P >= p->wide_min_pairs || P > MS_MLP_MAX_PAIRS);
+  if (wide) {
+    MlpWideArgs m{};
+    m.slots = slots;
+    m.P = (int)P;
+    m.n_slots = p->cfg.n_slots;
+    m.keys = p->mlp_wkeys;
+    m.cnt = p->mlp_cnt;
+    m.status = &p->tab.ctr->status;
+    m.grp = p->grp;
+    m.w = p->wa;
+    CK(launch_mlp_wide_prep(m, p->sm_count, s));
+    return wide_experts(p, x, T, k, p->mlp_wkeys, scores, nullptr, y, s);
+  }
+  if (k != p->geom.top_k)
+    return fail(MS_E_INVALID, "k=%d != top_k=%d needs the wide path (max_tokens * top_k >= %d pairs)",
+                k, p->geom.top_k, p->wide_min_pairs);
+  if (T > p->cfg.max_tokens || P > MS_MLP_MAX_PAIRS)
+    return fail(MS_E_INVALID, "T=%d outside [1, min(max_tokens, %d/k)]", T, MS_MLP_MAX_PAIRS);
   MlpPrepArgs a{};
   a.x = static_cast<const uint16_t*>(x);
   a.T = T;
@@ -742,6 +778,61 @@ int ms_expert_mlp(ms_pool* p, const int32_t* slots, const float* scores, const v
   a.grp = p->grp;
   CK(launch_mlp_prep(a, s));
   CK(launch_expert(exp_args(p, x, T, y, scores), std::min(T * k, p->cfg.n_slots), s));
+  return MS_OK;
+}
+
+int ms_ep_pack(ms_pool* p, const void* x, int T, const int32_t* inds, const void* scores, int world,
+               int e_local, void* send_x, int32_t* send_meta, int32_t* send_counts,
+               int32_t* pair_pos, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (!x || !inds || !scores || !send_x || !send_meta || !send_counts || !pair_pos)
+    return fail(MS_E_INVALID, "NULL argument");
+  if (T <= 0) return fail(MS_E_INVALID, "T=%d must be positive", T);
+  if (world <= 0 || world > 64) return fail(MS_E_INVALID, "world=%d outside [1, 64]", world);
+  if (e_local <= 0 || (long long)e_local * world != p->geom.n_experts)
+    return fail(MS_E_INVALID, "e_local=%d x world=%d must equal n_experts=%d", e_local, world,
+                p->geom.n_experts);
+  if (!aligned16(x) || !aligned16(send_x)) return fail(MS_E_INVALID, "x and send_x must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaSetDevice(p->device));
+  int* cursor = p->ep_scratch;
+  CK(cudaMemsetAsync(send_counts, 0, sizeof(int) * world, s));
+  CK(cudaMemsetAsync(cursor, 0, sizeof(int) * world, s));
+  EpPackArgs a{};
+  a.x = static_cast<const uint16_t*>(x);
+  a.T = T;
+  a.k = p->geom.top_k;
+  a.d = p->geom.d_model;
+  a.inds = inds;
+  a.scores = static_cast<const uint16_t*>(scores);
+  a.world = world;
+  a.e_local = e_local;
+  a.send_x = static_cast<uint16_t*>(send_x);
+  a.send_meta = send_meta;
+  a.counts = send_counts;
+  a.cursor = cursor;
+  a.pair_pos = pair_pos;
+  CK(launch_ep_pack(a, p->sm_count, s));
+  return MS_OK;
+}
+
+int ms_ep_combine(ms_pool* p, const void* back, const int32_t* pair_pos, int T, void* y,
+                  void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (!back || !pair_pos || !y) return fail(MS_E_INVALID, "NULL argument");
+  if (T <= 0) return fail(MS_E_INVALID, "T=%d must be positive", T);
+  if (!aligned16(back) || !aligned16(y)) return fail(MS_E_INVALID, "back and y must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaSetDevice(p->device));
+  CombineArgs c{};
+  c.Y = static_cast<const uint16_t*>(back);
+  c.inv = pair_pos;
+  c.y = static_cast<uint16_t*>(y);
+  c.T = T;
+  c.k = p->geom.top_k;
+  c.d = p->geom.d_model;
+  const long long chunks = (long long)T * (c.d / 8);
+  CK(launch_combine(c, (int)std::min<long long>((chunks + 255) / 256, p->sm_count * 8), s));
   return MS_OK;
 }
 

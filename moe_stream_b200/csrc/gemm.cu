@@ -561,6 +561,164 @@ __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
   }
 }
 
+// ------------------------------------------------- slot-keyed grouping
+// ms_expert_mlp on a wide batch (kernels.py:231-252 generalised to many
+// tokens): pairs are grouped by the slot they read, groups in ascending slot
+// order, each cut into GEMM tiles. Pass 1 counts pairs per slot; pass 2 (one
+// CTA) lays the groups out: every thread takes a contiguous range of slots,
+// a CTA scan turns the ranges' group/row/tile totals into offsets.
+__global__ void __launch_bounds__(256) k_mlp_count(MlpWideArgs a) {
+  for (int p = blockIdx.x * 256 + threadIdx.x; p < a.P; p += gridDim.x * 256) {
+    int s = a.slots[p];
+    if (s < 0 || s >= a.n_slots) {             // its group reads nothing and yields zeros
+      s = a.n_slots;
+      atomicCAS(a.status, 0, -1);
+    }
+    a.keys[p] = s;
+    atomicAdd(&a.cnt[s], 1);
+  }
+}
+
+__device__ __forceinline__ int cta_exclusive_scan(int v, int* s_tmp, int* total) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(MS_FULL, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) s_tmp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < 8 ? s_tmp[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const int u = __shfl_up_sync(MS_FULL, wi, o);
+      if (lane >= o) wi += u;
+    }
+    if (lane < 8) s_tmp[8 + lane] = wi - w;
+    if (lane == 7) s_tmp[16] = wi;
+  }
+  __syncthreads();
+  const int ex = s_tmp[8 + warp] + incl - v;
+  *total = s_tmp[16];
+  __syncthreads();
+  return ex;
+}
+
+__global__ void __launch_bounds__(256) k_mlp_groups(MlpWideArgs a) {
+  __shared__ int s_tmp[32];
+  const int nk = a.n_slots + 1;
+  const int chunk = (nk + 255) / 256;
+  const int k0 = threadIdx.x * chunk, k1 = min(nk, k0 + chunk);
+  int ng = 0, nr = 0, nt = 0;
+  for (int key = k0; key < k1; ++key) {
+    const int c = a.cnt[key];
+    if (c) {
+      ++ng;
+      nr += c;
+      nt += (c + GEMM_TILE_ROWS - 1) / GEMM_TILE_ROWS;
+    }
+  }
+  int tot_g, tot_r, tot_t;
+  int g = cta_exclusive_scan(ng, s_tmp, &tot_g);
+  int row = cta_exclusive_scan(nr, s_tmp, &tot_r);
+  int tl = cta_exclusive_scan(nt, s_tmp, &tot_t);
+  for (int key = k0; key < k1; ++key) {
+    const int c = a.cnt[key];
+    if (!c) continue;
+    a.cnt[key] = 0;
+    a.grp.grp_key[g] = key;
+    a.grp.grp_slot[g] = key < a.n_slots ? key : -1;
+    a.grp.grp_start[g] = row;
+    a.grp.grp_count[g] = c;
+    a.grp.map[key] = g;
+    a.w.cursor[g] = 0;
+    for (int j = 0; j * GEMM_TILE_ROWS < c; ++j, ++tl) {
+      if (tl >= a.w.max_tiles) continue;
+      GemmTile t;
+      t.g = g;
+      t.row0 = row + j * GEMM_TILE_ROWS;
+      t.rows = min(GEMM_TILE_ROWS, c - j * GEMM_TILE_ROWS);
+      t.slot = key < a.n_slots ? key : -1;
+      a.w.tiles[tl] = t;
+    }
+    row += c;
+    ++g;
+  }
+  if (threadIdx.x == 0) {
+    *a.grp.n_groups = tot_g;
+    *a.w.n_tiles = min(tot_t, a.w.max_tiles);
+  }
+}
+
+cudaError_t launch_mlp_wide_prep(const MlpWideArgs& a, int sms, cudaStream_t s) {
+  k_mlp_count<<<std::max(1, std::min((a.P + 255) / 256, sms * 4)), 256, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  k_mlp_groups<<<1, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------ expert-parallel dispatch
+// Pairs are packed destination-major (rank = expert / e_local); inside a
+// destination in arrival order, which changes nothing in the result (every
+// row is computed on its own and returns to pair_pos).
+__global__ void __launch_bounds__(256) k_ep_count(EpPackArgs a) {
+  const int P = a.T * a.k;
+  for (int p = blockIdx.x * 256 + threadIdx.x; p < P; p += gridDim.x * 256)
+    atomicAdd(&a.counts[a.inds[p] / a.e_local], 1);
+}
+
+__global__ void __launch_bounds__(256) k_ep_pack(EpPackArgs a) {
+  __shared__ int s_start[64];
+  if (threadIdx.x < 32) {
+    int run = 0;
+    for (int base = 0; base < a.world; base += 32) {
+      const int r = base + threadIdx.x;
+      const int c = r < a.world ? a.counts[r] : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(MS_FULL, incl, o);
+        if ((int)threadIdx.x >= o) incl += u;
+      }
+      if (r < a.world) s_start[r] = run + incl - c;
+      run += __shfl_sync(MS_FULL, incl, 31);
+    }
+  }
+  __syncthreads();
+  const int P = a.T * a.k;
+  const int warps = gridDim.x * 8;
+  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int chunks = a.d / 8;
+  for (int p = gw; p < P; p += warps) {
+    int pos = 0;
+    if (lane == 0) {
+      const int e = a.inds[p];
+      const int dest = e / a.e_local;
+      pos = s_start[dest] + atomicAdd(&a.cursor[dest], 1);
+      a.send_meta[2 * pos] = e - dest * a.e_local;
+      a.send_meta[2 * pos + 1] = __float_as_int(bf2f(a.scores[p]));
+      a.pair_pos[p] = pos;
+    }
+    pos = __shfl_sync(MS_FULL, pos, 0);
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)(p / a.k) * a.d);
+    uint4* dst = reinterpret_cast<uint4*>(a.send_x + (long long)pos * a.d);
+    for (int c = lane; c < chunks; c += 32) dst[c] = __ldg(src + c);
+  }
+}
+
+cudaError_t launch_ep_pack(const EpPackArgs& a, int sms, cudaStream_t s) {
+  const int P = a.T * a.k;
+  k_ep_count<<<std::max(1, std::min((P + 255) / 256, sms * 4)), 256, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  k_ep_pack<<<std::max(1, std::min((P + 7) / 8, sms * 8)), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------- tensor maps
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;

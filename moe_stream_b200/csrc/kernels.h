@@ -137,6 +137,33 @@ struct CombineArgs {
   int T, k, d;
 };
 
+// ms_expert_mlp on a wide batch: pairs grouped by the slot they read.
+struct MlpWideArgs {
+  const int* slots;           // [P] caller's slot per pair
+  int P, n_slots;
+  int* keys;                  // [P] scratch: the slot, or n_slots when it is invalid
+  int* cnt;                   // [n_slots + 1] pairs per key; zero between calls
+  int* status;                // sticky pool status (MS_E_INVALID for a bad slot)
+  Groups grp;
+  WideArgs w;
+};
+
+// Expert-parallel dispatch: token/expert pairs packed by destination rank.
+struct EpPackArgs {
+  const uint16_t* x;          // bf16 [T, d]
+  int T, k, d;
+  const int* inds;            // [T, k] global expert ids
+  const uint16_t* scores;     // bf16 [T, k]
+  int world, e_local;         // rank r owns experts [r * e_local, (r + 1) * e_local)
+  uint16_t* send_x;           // bf16 [T * k, d], destination-major
+  int* send_meta;             // [T * k][2]: slot on the destination, score (f32 bits)
+  int* counts;                // [world] pairs per destination (zeroed before)
+  int* cursor;                // [world] (zeroed before)
+  int* pair_pos;              // [T * k] row of each pair in send_x
+};
+
+cudaError_t launch_mlp_wide_prep(const MlpWideArgs& a, int sms, cudaStream_t s);
+cudaError_t launch_ep_pack(const EpPackArgs& a, int sms, cudaStream_t s);
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s);
 cudaError_t launch_route_wide(const RouteArgs& a, const WideArgs& w, cudaStream_t s);
 cudaError_t launch_scatter(const ScatterArgs& a, int grid, cudaStream_t s);

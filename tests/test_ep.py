@@ -1,0 +1,142 @@
+"""The expert-parallel exchange protocol (moe_stream_b200.ep.ep_forward) on
+CPU ranks over gloo, world 2 and 4.
+
+The device operations are replaced by CPU stand-ins with the same contracts
+(routing, destination-major packing, k = 1 expert rows, combine), computed
+by the oracle. The protocol -- count exchange, split sizes, row and metadata
+all-to-alls, the return trip and the combine through pair_pos -- must then
+reproduce the single-process oracle block exactly: every row is computed on
+its own, so sharding the experts changes no bit of the output.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from moe_stream_b200 import geometry, store as S
+from oracle import bf16 as OB
+from oracle import moe as OM
+
+SEED = 7
+
+
+def _geom():
+    # gpt-oss arithmetic (top-4 then softmax, biases, clamped SwiGLU) at a
+    # size the oracle handles in seconds
+    return geometry.make("gptoss", 256, 256, 8, 1, 4, False)
+
+
+def _inputs(geom, T):
+    w, b = S.router_weights(geom, SEED, 0, bias_std=0.5)
+    x = S.rms_norm_tokens(T, geom.d_model, seed=SEED + 1)
+    blobs = {e: S.make_blob(geom, SEED, 0, e).numpy() for e in range(geom.n_experts)}
+    return w, b, x, blobs
+
+
+class OracleOps:
+    """CPU stand-ins for the four device operations of ep_forward."""
+
+    def __init__(self, geom, rank, world, w, b, blobs):
+        self.geom, self.rank, self.world = geom, rank, world
+        self.e_local = geom.n_experts // world
+        self.w = w.float().numpy()
+        self.b = None if b is None else b.float().numpy()
+        self.comps = [dict(c) for c in geom.components]
+        # slot i of this rank holds expert rank * e_local + i
+        self.local = {i: blobs[rank * self.e_local + i] for i in range(self.e_local)}
+
+    def route(self, x):
+        inds, scores, _ = OM.route_gptoss(x.float().numpy(), self.w, self.geom.top_k, self.b)
+        return torch.from_numpy(inds.astype(np.int32)), torch.from_numpy(scores.astype(np.float32))
+
+    def pack(self, x, inds, scores):
+        T, k = inds.shape
+        flat = inds.reshape(-1).numpy()
+        dest = flat // self.e_local
+        order = np.argsort(dest, kind="stable")          # pair index for each send row
+        pair_pos = np.empty(T * k, np.int32)
+        pair_pos[order] = np.arange(T * k, dtype=np.int32)
+        send_x = x[torch.from_numpy(order // k)]
+        meta = np.empty((T * k, 2), np.int32)
+        meta[:, 0] = (flat % self.e_local)[order]
+        meta[:, 1] = scores.reshape(-1).numpy()[order].view(np.int32)
+        counts = np.bincount(dest, minlength=self.world).astype(np.int32)
+        return send_x, torch.from_numpy(meta), torch.from_numpy(counts), torch.from_numpy(pair_pos)
+
+    def experts(self, recv_x, recv_meta):
+        n = recv_x.shape[0]
+        if n == 0:
+            return recv_x.new_empty(recv_x.shape)
+        meta = recv_meta.numpy()
+        slots = meta[:, 0:1].astype(np.int64)
+        scores = meta[:, 1:2].copy().view(np.float32)
+        y = OM.expert_block(recv_x.float().numpy(), slots, scores, self.local, self.comps, "gptoss")
+        return torch.from_numpy(np.asarray(y, np.float32)).to(torch.bfloat16)
+
+    def combine(self, back, pair_pos, T):
+        k = self.geom.top_k
+        rows = back.float()[pair_pos.long()].reshape(T, k, -1)
+        return torch.from_numpy(OB.r(rows.numpy().sum(axis=1, dtype=np.float32))).to(torch.bfloat16)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank_main(rank, world, port, T, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from moe_stream_b200.ep import ep_forward
+        geom = _geom()
+        w, b, x, blobs = _inputs(geom, T)
+        shard = T // world
+        ops = OracleOps(geom, rank, world, w, b, blobs)
+        y = ep_forward(x[rank * shard:(rank + 1) * shard], ops, world)
+        torch.save(y, os.path.join(out_dir, f"y{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_protocol_matches_single_process_oracle(world, tmp_path):
+    T = 24
+    mp.start_processes(_rank_main, args=(world, _free_port(), T, str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    y = torch.cat([torch.load(tmp_path / f"y{r}.pt") for r in range(world)]).float().numpy()
+    geom = _geom()
+    w, b, x, blobs = _inputs(geom, T)
+    inds, scores, _ = OM.route_gptoss(x.float().numpy(), w.float().numpy(), geom.top_k,
+                                      b.float().numpy())
+    ref = OM.expert_block(x.float().numpy(), inds, scores, blobs,
+                          [dict(c) for c in geom.components], "gptoss")
+    assert np.array_equal(y, np.asarray(ref, np.float32))
+
+
+def test_ep_pack_contract():
+    """The stand-in's packing obeys the contract the device pack follows:
+    rows destination-major, counts per destination, pair_pos the row of each
+    pair, metadata (slot on the destination, score bits)."""
+    geom = _geom()
+    w, b, x, blobs = _inputs(geom, 10)
+    ops = OracleOps(geom, 0, 4, w, b, blobs)
+    inds, scores = ops.route(x)
+    send_x, meta, counts, pair_pos = ops.pack(x, inds, scores)
+    flat = inds.reshape(-1).numpy()
+    starts = np.concatenate([[0], np.cumsum(counts.numpy())[:-1]])
+    for p in range(flat.size):
+        pos = int(pair_pos[p])
+        dest = flat[p] // ops.e_local
+        assert starts[dest] <= pos < starts[dest] + counts[dest]
+        assert int(meta[pos, 0]) == flat[p] % ops.e_local
+        assert np.int32(meta[pos, 1]).view(np.float32) == scores.reshape(-1)[p].item()
+        assert torch.equal(send_x[pos], x[p // geom.top_k])
