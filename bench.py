@@ -42,12 +42,14 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-sample-layers", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=["stack", "layer", "prefill"], default="stack",
+    ap.add_argument("--case", choices=["stack", "layer", "prefill", "ep"], default="stack",
                     help="layer: a 2-layer Qwen3 stack with every expert resident (a small "
                          "case for ncu section captures); prints per-call timings only. "
                          "prefill: one MoE layer on a large token batch (config 2: qwen3, "
                          "T=4096; config 3: gptoss, T=512; config 4 on one GPU: gptoss, "
-                         "T=16384), the grouped tcgen05 GEMM path")
+                         "T=16384), the grouped tcgen05 GEMM path. ep: config 4, the "
+                         "gpt-oss layer on T=16384 tokens with its 128 experts sharded over "
+                         "the ranks (run under torchrun), NCCL all-to-all dispatch/combine")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--model", choices=["qwen3", "gptoss"], default="qwen3")
     return ap.parse_args()
@@ -184,6 +186,117 @@ def prefill_case(args):
     }
     print(json.dumps(line))
     pool.close()
+
+
+def ep_case(args):
+    """one gpt-oss layer on T tokens (default 16384), the
+    tokens split evenly over the ranks and the 128 experts sharded 128/G per
+    GPU; a step is one expert-parallel block (route, pack, all-to-all out,
+    local grouped GEMMs, all-to-all back, combine) on every rank. Timed on the
+    device, max over ranks."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from moe_stream_b200 import geometry, store as S
+    from moe_stream_b200.block import MoEBlock
+    from moe_stream_b200.ep import DeviceOps, ep_forward, load_local_experts
+    from moe_stream_b200.pool import ExpertPool
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29541")
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=300), device_id=dev)
+    geom = geometry.gptoss(1)
+    T = args.tokens or 16384
+    if T % world or geom.n_experts % world:
+        raise SystemExit(f"T={T} and {geom.n_experts} experts must split over {world} ranks")
+    Tr = T // world
+    pool = ExpertPool(geom, geom.n_experts // world, depths=(), max_tokens=T)
+    st = torch.from_numpy(pool.alloc_store()).view(geom.n_keys, geom.blob_bytes)
+    st.copy_(S.make_layer_blobs(geom, SEED, 0, device=dev).cpu())
+    load_local_experts(pool, 0, rank, world)
+    w, b = S.router_weights(geom, SEED, 0, zipf_s=1.1)
+    block = MoEBlock(pool, 0, w, b)
+    ops = DeviceOps(block, world)
+    xs = [S.rms_norm_tokens(T, geom.d_model, seed=SEED + 200 + i)[rank * Tr:(rank + 1) * Tr]
+          .to(dev) for i in range(2)]
+    W, K = max(3, args.warmup), args.steps
+    for i in range(W):
+        ep_forward(xs[i % 2], ops, world)
+    torch.cuda.synchronize()
+    pool.status()
+    clocks = ClockSampler(local)
+    clocks.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        ep_forward(xs[i % 2], ops, world)
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    pool.status()
+    ms = torch.tensor([e0.elapsed_time(e1) / K], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    # e2e: pinned host tokens in, pinned host result out, every step
+    xh = xs[0].cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    xd = torch.empty_like(xs[0])
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(K):
+        xd.copy_(xh, non_blocking=True)
+        y = ep_forward(xd, ops, world)
+        yh.copy_(y, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ems = torch.tensor([e0.elapsed_time(e1) / K], device=dev)
+    dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+    ems = float(ems.item())
+    pool.status()
+    flops = 2.0 * T * geom.top_k * 3 * geom.d_model * geom.d_ff
+    peaks, peak_kind = measured_peaks()
+    achieved = flops / (ms * 1e-3) / 1e12
+    a2a_bytes = 2 * T * geom.top_k * geom.d_model * 2          # rows out and back, whole job
+    if rank == 0:
+        line = {
+            "metric": "MoE-block expert-parallel prefill tok/s (gpt-oss layer, T=%d)" % T,
+            "value": T / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "u4 weights as exact fp16 hi+lo pairs x fp16 tokens, f32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights, MLX affine 4-bit g64; N(0,1) RMS-normed tokens)",
+            "config": {"workload": "config4: gpt-oss layer, experts sharded %d per GPU, NCCL "
+                                   "all-to-all dispatch/combine" % (geom.n_experts // world),
+                       "tokens": T, "tokens_per_rank": Tr, "top_k": geom.top_k,
+                       "router_bias": "Zipf(1.1)", "parallelism": f"ep{world}",
+                       "l2": "inputs larger than L2: %.1f GB of expert weights per GPU"
+                             % (geom.n_experts // world * geom.payload_bytes / 1e9)},
+            "roofline": {"bound": "tensor", "achieved": achieved,
+                         "peak": peaks["bf16_tflops"] * world, "unit": "TFLOP/s",
+                         "frac": achieved / (peaks["bf16_tflops"] * world), "traffic": None,
+                         "peak_kind": peak_kind, "kernel": "whole expert-parallel step",
+                         "algorithmic_flops_per_step": flops,
+                         "a2a_bytes_per_step": a2a_bytes},
+            "cpu_baseline": None,
+            "e2e": {"value": T / (ems * 1e-3), "unit": "tok/s",
+                    "h2d_bytes_per_step": int(xh.numel() * 2 * world),
+                    "d2h_bytes_per_step": int(yh.numel() * 2 * world),
+                    "path": "ep.ep_forward on every rank, pinned host tokens in / result out"},
+            "gpu_launches": 12 * K,
+            "clocks": clk,
+        }
+        print(json.dumps(line))
+    pool.close()
+    dist.destroy_process_group()
 
 
 def prefill_cpu_baseline(geom, st, w, b, x, model, n_tok):
@@ -521,6 +634,9 @@ def main():
         return
     if args.case == "prefill":
         prefill_case(args)
+        return
+    if args.case == "ep":
+        ep_case(args)
         return
     gpu_arm(args)
 
