@@ -52,6 +52,8 @@ def parse():
                          "the ranks (run under torchrun), NCCL all-to-all dispatch/combine")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--model", choices=["qwen3", "gptoss"], default="qwen3")
+    ap.add_argument("--no-replicas", action="store_true",
+                    help="ep: plain sharding, no replicas of hot experts")
     return ap.parse_args()
 
 
@@ -199,7 +201,8 @@ def ep_case(args):
     import torch.distributed as dist
     from moe_stream_b200 import geometry, store as S
     from moe_stream_b200.block import MoEBlock
-    from moe_stream_b200.ep import DeviceOps, ep_forward, load_local_experts
+    from moe_stream_b200.ep import (DeviceOps, ep_forward, load_local_experts, plan_placement,
+                                    routed_counts)
     from moe_stream_b200.pool import ExpertPool
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -215,15 +218,23 @@ def ep_case(args):
     if T % world or geom.n_experts % world:
         raise SystemExit(f"T={T} and {geom.n_experts} experts must split over {world} ranks")
     Tr = T // world
-    pool = ExpertPool(geom, geom.n_experts // world, depths=(), max_tokens=T)
+    base = geom.n_experts // world
+    spare = 0 if (world == 1 or args.no_replicas) else base // 2
+    pool = ExpertPool(geom, base + spare, depths=(), max_tokens=T)
     st = torch.from_numpy(pool.alloc_store()).view(geom.n_keys, geom.blob_bytes)
     st.copy_(S.make_layer_blobs(geom, SEED, 0, device=dev).cpu())
-    load_local_experts(pool, 0, rank, world)
     w, b = S.router_weights(geom, SEED, 0, zipf_s=1.1)
     block = MoEBlock(pool, 0, w, b)
-    ops = DeviceOps(block, world)
     xs = [S.rms_norm_tokens(T, geom.d_model, seed=SEED + 200 + i)[rank * Tr:(rank + 1) * Tr]
-          .to(dev) for i in range(2)]
+          .to(dev) for i in range(3)]
+    # placement from a calibration batch (not a timed one): hot experts
+    # replicated into the spare slots, replicas balanced over the ranks
+    counts = routed_counts(DeviceOps(block, world), xs[2])
+    table, slots = plan_placement(counts, world, base + spare)
+    load_local_experts(pool, 0, rank, world, slots[rank])
+    ops = DeviceOps(block, world, placement=table)
+    rank_load = [float(sum(counts[e] / table[e, 0] for e in r)) for r in slots]
+    xs = xs[:2]
     W, K = max(3, args.warmup), args.steps
     for i in range(W):
         ep_forward(xs[i % 2], ops, world)
@@ -267,6 +278,23 @@ def ep_case(args):
     peaks, peak_kind = measured_peaks()
     achieved = flops / (ms * 1e-3) / 1e12
     a2a_bytes = 2 * T * geom.top_k * geom.d_model * 2          # rows out and back, whole job
+    # phase breakdown of one more step (device events at the phase marks)
+    evs = []
+
+    def mark(name):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        evs.append((name, e))
+
+    dist.barrier()
+    torch.cuda.synchronize()
+    mark("start")
+    ep_forward(xs[0], ops, world, mark=mark)
+    torch.cuda.synchronize()
+    phases = {evs[i][0]: evs[i - 1][1].elapsed_time(evs[i][1]) for i in range(1, len(evs))}
+    ph = torch.tensor([phases[n] for n in phases], device=dev)
+    dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+    phases = dict(zip(phases, [round(float(v), 3) for v in ph.tolist()]))
     if rank == 0:
         line = {
             "metric": "MoE-block expert-parallel prefill tok/s (gpt-oss layer, T=%d)" % T,
@@ -276,6 +304,8 @@ def ep_case(args):
             "data": "synthetic (seeded N(0,0.02) weights, MLX affine 4-bit g64; N(0,1) RMS-normed tokens)",
             "config": {"workload": "config4: gpt-oss layer, experts sharded %d per GPU, NCCL "
                                    "all-to-all dispatch/combine" % (geom.n_experts // world),
+                       "placement": {"slots_per_gpu": base + spare, "replicas": int(table[:, 0].sum() - geom.n_experts),
+                                     "max_rank_share": max(rank_load) / max(1.0, sum(rank_load))},
                        "tokens": T, "tokens_per_rank": Tr, "top_k": geom.top_k,
                        "router_bias": "Zipf(1.1)", "parallelism": f"ep{world}",
                        "l2": "inputs larger than L2: %.1f GB of expert weights per GPU"
@@ -293,6 +323,7 @@ def ep_case(args):
                     "path": "ep.ep_forward on every rank, pinned host tokens in / result out"},
             "gpu_launches": 12 * K,
             "clocks": clk,
+            "phase_ms_max_over_ranks": phases,
         }
         print(json.dumps(line))
     pool.close()

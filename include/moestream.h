@@ -202,20 +202,25 @@ int ms_pool_timing(ms_pool* pool, int layer, float* out3);
 
 /* Expert parallelism, no counterpart in the reference,
  * which runs on one device; the block it distributes is engine_120b.py:78-149.
- * Rank r of `world` holds experts [r * e_local, (r + 1) * e_local) in its pool,
- * expert r * e_local + i in slot i. The host moves the buffers between ranks
+ * Each rank holds its experts (and replicas) resident in its pool. The host
+ * moves the buffers between ranks
  * (an all-to-all over NCCL) and runs the experts with ms_expert_mlp (k = 1).
  *
  * ms_ep_pack: the T*top_k token/expert pairs of x (routing from ms_route:
- * inds int32 [T, top_k], scores bf16 [T, top_k]) packed destination-major:
+ * inds int32 [T, top_k], scores bf16 [T, top_k]) packed destination-major.
+ * With placement == NULL expert e goes to rank e / e_local, slot e % e_local.
+ * Otherwise placement is a device int32 table [n_experts][1 + 2*max_rep]:
+ * the number of replicas of expert e, then (rank, slot) of each replica;
+ * pair p = t*top_k + j of expert e goes to replica p % n_rep (replicas of hot
+ * experts balance the ranks' loads; every replica computes the same result):
  * send_x bf16 [T*top_k, d_model] (the token's row), send_meta int32
  * [T*top_k][2] (slot on the destination, score as f32 bits), send_counts int32
  * [world] (pairs per destination, device memory), pair_pos int32 [T*top_k]
  * (row of each pair in send_x). Rows inside a destination come in no fixed
  * order. */
 int ms_ep_pack(ms_pool* pool, const void* x, int T, const int32_t* inds, const void* scores,
-               int world, int e_local, void* send_x, int32_t* send_meta, int32_t* send_counts,
-               int32_t* pair_pos, void* stream);
+               int world, int e_local, const int32_t* placement, int max_rep, void* send_x,
+               int32_t* send_meta, int32_t* send_counts, int32_t* pair_pos, void* stream);
 
 /* ms_ep_combine: y[t] = sum over j of back[pair_pos[t*top_k + j]] (the
  * score-weighted expert outputs returned to their senders), summed in fp32 in

@@ -782,16 +782,18 @@ int ms_expert_mlp(ms_pool* p, const int32_t* slots, const float* scores, const v
 }
 
 int ms_ep_pack(ms_pool* p, const void* x, int T, const int32_t* inds, const void* scores, int world,
-               int e_local, void* send_x, int32_t* send_meta, int32_t* send_counts,
-               int32_t* pair_pos, void* stream) {
+               int e_local, const int32_t* placement, int max_rep, void* send_x,
+               int32_t* send_meta, int32_t* send_counts, int32_t* pair_pos, void* stream) {
   if (!p) return fail(MS_E_INVALID, "NULL pool");
   if (!x || !inds || !scores || !send_x || !send_meta || !send_counts || !pair_pos)
     return fail(MS_E_INVALID, "NULL argument");
   if (T <= 0) return fail(MS_E_INVALID, "T=%d must be positive", T);
   if (world <= 0 || world > 64) return fail(MS_E_INVALID, "world=%d outside [1, 64]", world);
-  if (e_local <= 0 || (long long)e_local * world != p->geom.n_experts)
+  if (!placement && (e_local <= 0 || (long long)e_local * world != p->geom.n_experts))
     return fail(MS_E_INVALID, "e_local=%d x world=%d must equal n_experts=%d", e_local, world,
                 p->geom.n_experts);
+  if (placement && (max_rep <= 0 || max_rep > world))
+    return fail(MS_E_INVALID, "max_rep=%d outside [1, world=%d]", max_rep, world);
   if (!aligned16(x) || !aligned16(send_x)) return fail(MS_E_INVALID, "x and send_x must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CK(cudaSetDevice(p->device));
@@ -807,6 +809,8 @@ int ms_ep_pack(ms_pool* p, const void* x, int T, const int32_t* inds, const void
   a.scores = static_cast<const uint16_t*>(scores);
   a.world = world;
   a.e_local = e_local;
+  a.placement = placement;
+  a.max_rep = max_rep;
   a.send_x = static_cast<uint16_t*>(send_x);
   a.send_meta = send_meta;
   a.counts = send_counts;

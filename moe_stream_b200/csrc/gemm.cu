@@ -662,13 +662,24 @@ cudaError_t launch_mlp_wide_prep(const MlpWideArgs& a, int sms, cudaStream_t s) 
 }
 
 // ------------------------------------------------ expert-parallel dispatch
-// Pairs are packed destination-major (rank = expert / e_local); inside a
-// destination in arrival order, which changes nothing in the result (every
-// row is computed on its own and returns to pair_pos).
+// Pairs are packed destination-major; inside a destination in arrival
+// order, which changes nothing in the result (every row is computed on its
+// own and returns to pair_pos). Pair p of expert e goes to replica
+// p % n_rep(e) of e under a placement table, else to rank e / e_local.
+__device__ __forceinline__ int2 ep_dest(const EpPackArgs& a, int p, int e) {
+  if (!a.placement) {
+    const int r = e / a.e_local;
+    return make_int2(r, e - r * a.e_local);
+  }
+  const int* row = a.placement + (long long)e * (1 + 2 * a.max_rep);
+  const int j = p % row[0];
+  return make_int2(row[1 + 2 * j], row[2 + 2 * j]);
+}
+
 __global__ void __launch_bounds__(256) k_ep_count(EpPackArgs a) {
   const int P = a.T * a.k;
   for (int p = blockIdx.x * 256 + threadIdx.x; p < P; p += gridDim.x * 256)
-    atomicAdd(&a.counts[a.inds[p] / a.e_local], 1);
+    atomicAdd(&a.counts[ep_dest(a, p, a.inds[p]).x], 1);
 }
 
 __global__ void __launch_bounds__(256) k_ep_pack(EpPackArgs a) {
@@ -696,10 +707,9 @@ __global__ void __launch_bounds__(256) k_ep_pack(EpPackArgs a) {
   for (int p = gw; p < P; p += warps) {
     int pos = 0;
     if (lane == 0) {
-      const int e = a.inds[p];
-      const int dest = e / a.e_local;
-      pos = s_start[dest] + atomicAdd(&a.cursor[dest], 1);
-      a.send_meta[2 * pos] = e - dest * a.e_local;
+      const int2 ds = ep_dest(a, p, a.inds[p]);
+      pos = s_start[ds.x] + atomicAdd(&a.cursor[ds.x], 1);
+      a.send_meta[2 * pos] = ds.y;
       a.send_meta[2 * pos + 1] = __float_as_int(bf2f(a.scores[p]));
       a.pair_pos[p] = pos;
     }

@@ -154,7 +154,9 @@ struct EpPackArgs {
   int T, k, d;
   const int* inds;            // [T, k] global expert ids
   const uint16_t* scores;     // bf16 [T, k]
-  int world, e_local;         // rank r owns experts [r * e_local, (r + 1) * e_local)
+  int world, e_local;         // without a placement: rank r owns experts [r*e_local, (r+1)*e_local)
+  const int* placement;       // or [E][1 + 2*max_rep]: n_rep, then (rank, slot) per replica
+  int max_rep;
   uint16_t* send_x;           // bf16 [T * k, d], destination-major
   int* send_meta;             // [T * k][2]: slot on the destination, score (f32 bits)
   int* counts;                // [world] pairs per destination (zeroed before)

@@ -20,12 +20,22 @@ One forward, per rank, on its own T_r tokens:
 Every row is computed on its own by the same kernels as on one device, so
 the output equals the single-device block's bit for bit.
 
+Placement. Plain sharding puts expert e on rank e // e_local. Under skewed
+routing (config 4's Zipf(1.1) router bias) the hottest expert alone takes
+more than a rank's share of the pairs, so `plan_placement` gives each rank a
+few spare slots, replicates the experts with the largest load per replica
+into them, and assigns every replica, longest first, to the least loaded
+rank; pair p of expert e then goes to replica p % n_rep(e). Replicas compute
+identical results, so the output stays bit-exact.
+
 `ep_forward` is the exchange protocol alone; the device work comes from an
 `ops` object (DeviceOps here), so the same protocol also runs on CPU ranks
 with another implementation of the four operations.
 """
 import ctypes
+import heapq
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -38,11 +48,14 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
-def ep_forward(x, ops, world, group=None):
-    """The expert-parallel MoE block on this rank's tokens x [T, d]."""
+def ep_forward(x, ops, world, group=None, mark=None):
+    """The expert-parallel MoE block on this rank's tokens x [T, d].
+    `mark(name)`, if given, is called at every phase boundary (timing)."""
+    mark = mark or (lambda name: None)
     T = x.shape[0]
     inds, scores = ops.route(x)
     send_x, send_meta, counts, pair_pos = ops.pack(x, inds, scores)
+    mark("routed+packed")
     recv_counts = torch.empty_like(counts)
     dist.all_to_all_single(recv_counts, counts, group=group)
     # split sizes travel to the host: the one synchronisation of the step
@@ -53,25 +66,94 @@ def ep_forward(x, ops, world, group=None):
     recv_meta = send_meta.new_empty((n_recv, 2))
     dist.all_to_all_single(recv_x, send_x, recv_splits, send_splits, group=group)
     dist.all_to_all_single(recv_meta, send_meta, recv_splits, send_splits, group=group)
+    mark("dispatched")
     y_recv = ops.experts(recv_x, recv_meta)
+    mark("experts")
     back = y_recv.new_empty((send_x.shape[0], y_recv.shape[1]))
     dist.all_to_all_single(back, y_recv, send_splits, recv_splits, group=group)
-    return ops.combine(back, pair_pos, T)
+    mark("returned")
+    y = ops.combine(back, pair_pos, T)
+    mark("combined")
+    return y
+
+
+def plan_placement(counts, world, slots_per_rank, max_rep=None):
+    """Expert placement from per-expert pair counts (e.g. one calibration
+    batch, summed over the ranks). Returns (table, slots): table int32
+    [E][1 + 2*max_rep] as ms_ep_pack reads it, slots[r] = the expert held in
+    each slot of rank r. Deterministic, so every rank computes the same plan."""
+    counts = np.asarray(counts, np.float64)
+    E = counts.size
+    max_rep = min(world, max_rep or world)
+    if world * slots_per_rank < E:
+        raise ValueError(f"{world} x {slots_per_rank} slots cannot hold {E} experts")
+    reps = np.ones(E, np.int64)
+    spare = world * slots_per_rank - E
+    share = counts.sum() / world
+    # replicate while some replica carries more than half a rank's share
+    heap = [(-counts[e], e) for e in range(E)]
+    heapq.heapify(heap)
+    while spare > 0 and heap:
+        neg, e = heapq.heappop(heap)
+        if -neg <= share / 2:
+            break
+        if reps[e] >= max_rep:
+            continue
+        reps[e] += 1
+        spare -= 1
+        heapq.heappush(heap, (-counts[e] / reps[e], e))
+    items = sorted(((counts[e] / reps[e], e) for e in range(E) for _ in range(reps[e])),
+                   key=lambda it: (-it[0], it[1]))
+    load = np.zeros(world)
+    slots = [[] for _ in range(world)]
+    for w, e in items:
+        cands = [r for r in range(world) if len(slots[r]) < slots_per_rank and e not in slots[r]]
+        if not cands:
+            continue                            # a replica with nowhere to go is dropped
+        r = min(cands, key=lambda r: (load[r], r))
+        slots[r].append(e)
+        load[r] += w
+    table = np.zeros((E, 1 + 2 * max_rep), np.int32)
+    for r in range(world):
+        for i, e in enumerate(slots[r]):
+            n = table[e, 0]
+            table[e, 1 + 2 * n] = r
+            table[e, 2 + 2 * n] = i
+            table[e, 0] = n + 1
+    if (table[:, 0] == 0).any():
+        raise RuntimeError("placement left an expert without a slot")
+    return table, slots
+
+
+def shard_placement(E, world):
+    """Plain sharding as a plan: expert e on rank e // (E / world)."""
+    e_local = E // world
+    table = np.zeros((E, 3), np.int32)
+    for e in range(E):
+        table[e] = (1, e // e_local, e % e_local)
+    return table, [list(range(r * e_local, (r + 1) * e_local)) for r in range(world)]
 
 
 class DeviceOps:
     """The four operations of ep_forward on this rank's GPU, through the
-    library: block is the rank's MoEBlock (router set on its pool, the pool
-    holding experts [rank * e_local, (rank + 1) * e_local) in slots 0..)."""
+    library: block is the rank's MoEBlock (router set on its pool). Without
+    a placement table the pool holds experts [rank * e_local, (rank + 1) *
+    e_local) in slots 0..; with one (plan_placement) it holds slots[rank]."""
 
-    def __init__(self, block, world):
+    def __init__(self, block, world, placement=None):
         self.block = block
         self.pool = block.pool
         self.world = world
         E = self.pool.geom.n_experts
-        if E % world:
+        if placement is None and E % world:
             raise ValueError(f"{E} experts do not shard over {world} ranks")
         self.e_local = E // world
+        self.placement = None
+        self.max_rep = 0
+        if placement is not None:
+            table = torch.as_tensor(np.ascontiguousarray(placement, np.int32))
+            self.max_rep = (table.shape[1] - 1) // 2
+            self.placement = table.to(f"cuda:{self.pool.device}")
         self.stream = None
 
     def route(self, x):
@@ -85,9 +167,11 @@ class DeviceOps:
         send_meta = torch.empty(T * k, 2, dtype=torch.int32, device=dev)
         counts = torch.empty(self.world, dtype=torch.int32, device=dev)
         pair_pos = torch.empty(T * k, dtype=torch.int32, device=dev)
+        table = _ptr(self.placement) if self.placement is not None else None
         _lib.check(pool._lib.ms_ep_pack(pool._h, _ptr(x), T, _ptr(inds), _ptr(scores), self.world,
-                                        self.e_local, _ptr(send_x), _ptr(send_meta), _ptr(counts),
-                                        _ptr(pair_pos), _stream_ptr(self.stream)))
+                                        self.e_local, table, self.max_rep, _ptr(send_x),
+                                        _ptr(send_meta), _ptr(counts), _ptr(pair_pos),
+                                        _stream_ptr(self.stream)))
         return send_x, send_meta, counts, pair_pos
 
     def experts(self, recv_x, recv_meta):
@@ -106,10 +190,23 @@ class DeviceOps:
         return y
 
 
-def load_local_experts(pool, layer, rank, world):
-    """Fill slot i of this rank's pool with expert rank * e_local + i of
-    `layer` from the attached store (ExpertPool._read), once."""
-    e_local = pool.geom.n_experts // world
-    for i in range(e_local):
-        pool._read(i, layer, rank * e_local + i)
+def load_local_experts(pool, layer, rank, world, slots=None):
+    """Fill this rank's slots from the attached store (ExpertPool._read),
+    once: slot i <- expert slots[i] of `layer` (a plan_placement row), or
+    expert rank * e_local + i without a plan."""
+    if slots is None:
+        e_local = pool.geom.n_experts // world
+        slots = [rank * e_local + i for i in range(e_local)]
+    for i, e in enumerate(slots):
+        pool._read(i, layer, int(e))
     torch.cuda.synchronize(pool.device)
+
+
+def routed_counts(ops, x, group=None):
+    """Pairs per expert of x's routing summed over the ranks (a calibration
+    input for plan_placement); host int64 array."""
+    inds, _ = ops.route(x)
+    c = torch.bincount(inds.reshape(-1).long(), minlength=ops.pool.geom.n_experts)
+    if dist.is_initialized():
+        dist.all_reduce(c, group=group)
+    return c.cpu().numpy()

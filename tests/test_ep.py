@@ -38,16 +38,18 @@ def _inputs(geom, T):
 
 
 class OracleOps:
-    """CPU stand-ins for the four device operations of ep_forward."""
+    """CPU stand-ins for the four device operations of ep_forward, with the
+    device pack's dispatch rule: pair p of expert e goes to replica
+    p % n_rep(e) of the placement table."""
 
-    def __init__(self, geom, rank, world, w, b, blobs):
+    def __init__(self, geom, rank, world, w, b, blobs, plan=None):
+        from moe_stream_b200.ep import shard_placement
         self.geom, self.rank, self.world = geom, rank, world
-        self.e_local = geom.n_experts // world
+        self.table, slots = plan if plan is not None else shard_placement(geom.n_experts, world)
         self.w = w.float().numpy()
         self.b = None if b is None else b.float().numpy()
         self.comps = [dict(c) for c in geom.components]
-        # slot i of this rank holds expert rank * e_local + i
-        self.local = {i: blobs[rank * self.e_local + i] for i in range(self.e_local)}
+        self.local = {i: blobs[e] for i, e in enumerate(slots[rank])}
 
     def route(self, x):
         inds, scores, _ = OM.route_gptoss(x.float().numpy(), self.w, self.geom.top_k, self.b)
@@ -56,13 +58,15 @@ class OracleOps:
     def pack(self, x, inds, scores):
         T, k = inds.shape
         flat = inds.reshape(-1).numpy()
-        dest = flat // self.e_local
+        rep = np.arange(T * k) % self.table[flat, 0]
+        dest = self.table[flat, 1 + 2 * rep]
+        slot = self.table[flat, 2 + 2 * rep]
         order = np.argsort(dest, kind="stable")          # pair index for each send row
         pair_pos = np.empty(T * k, np.int32)
         pair_pos[order] = np.arange(T * k, dtype=np.int32)
         send_x = x[torch.from_numpy(order // k)]
         meta = np.empty((T * k, 2), np.int32)
-        meta[:, 0] = (flat % self.e_local)[order]
+        meta[:, 0] = slot[order]
         meta[:, 1] = scores.reshape(-1).numpy()[order].view(np.int32)
         counts = np.bincount(dest, minlength=self.world).astype(np.int32)
         return send_x, torch.from_numpy(meta), torch.from_numpy(counts), torch.from_numpy(pair_pos)
@@ -91,7 +95,15 @@ def _free_port():
     return port
 
 
-def _rank_main(rank, world, port, T, out_dir):
+def _skewed_plan(geom, world):
+    """A placement with replicas: the planner on skewed counts, two spare
+    slots per rank."""
+    from moe_stream_b200.ep import plan_placement
+    counts = np.array([40.0 / (e + 1) for e in range(geom.n_experts)])
+    return plan_placement(counts, world, geom.n_experts // world + 2)
+
+
+def _rank_main(rank, world, port, T, out_dir, replicated):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -100,18 +112,19 @@ def _rank_main(rank, world, port, T, out_dir):
         geom = _geom()
         w, b, x, blobs = _inputs(geom, T)
         shard = T // world
-        ops = OracleOps(geom, rank, world, w, b, blobs)
+        plan = _skewed_plan(geom, world) if replicated else None
+        ops = OracleOps(geom, rank, world, w, b, blobs, plan)
         y = ep_forward(x[rank * shard:(rank + 1) * shard], ops, world)
         torch.save(y, os.path.join(out_dir, f"y{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ep_protocol_matches_single_process_oracle(world, tmp_path):
+@pytest.mark.parametrize("world,replicated", [(2, False), (4, False), (4, True)])
+def test_ep_protocol_matches_single_process_oracle(world, replicated, tmp_path):
     T = 24
-    mp.start_processes(_rank_main, args=(world, _free_port(), T, str(tmp_path)), nprocs=world,
-                       start_method="spawn")
+    mp.start_processes(_rank_main, args=(world, _free_port(), T, str(tmp_path), replicated),
+                       nprocs=world, start_method="spawn")
     y = torch.cat([torch.load(tmp_path / f"y{r}.pt") for r in range(world)]).float().numpy()
     geom = _geom()
     w, b, x, blobs = _inputs(geom, T)
@@ -128,15 +141,34 @@ def test_ep_pack_contract():
     pair, metadata (slot on the destination, score bits)."""
     geom = _geom()
     w, b, x, blobs = _inputs(geom, 10)
-    ops = OracleOps(geom, 0, 4, w, b, blobs)
+    plan = _skewed_plan(geom, 4)
+    ops = OracleOps(geom, 0, 4, w, b, blobs, plan)
     inds, scores = ops.route(x)
     send_x, meta, counts, pair_pos = ops.pack(x, inds, scores)
     flat = inds.reshape(-1).numpy()
     starts = np.concatenate([[0], np.cumsum(counts.numpy())[:-1]])
+    table, slots = plan
     for p in range(flat.size):
         pos = int(pair_pos[p])
-        dest = flat[p] // ops.e_local
+        j = p % table[flat[p], 0]
+        dest, slot = table[flat[p], 1 + 2 * j], table[flat[p], 2 + 2 * j]
         assert starts[dest] <= pos < starts[dest] + counts[dest]
-        assert int(meta[pos, 0]) == flat[p] % ops.e_local
+        assert int(meta[pos, 0]) == slot
+        assert slots[dest][slot] == flat[p]
         assert np.int32(meta[pos, 1]).view(np.float32) == scores.reshape(-1)[p].item()
         assert torch.equal(send_x[pos], x[p // geom.top_k])
+
+
+def test_plan_placement_balances_and_covers():
+    from moe_stream_b200.ep import plan_placement
+    counts = np.array([1000, 400, 200, 100] + [50] * 12, np.float64)
+    table, slots = plan_placement(counts, 4, 6)
+    assert all(len(r) <= 6 for r in slots)
+    assert (table[:, 0] >= 1).all()
+    for e in range(16):                        # replicas on distinct ranks, consistent slots
+        ranks = [table[e, 1 + 2 * j] for j in range(table[e, 0])]
+        assert len(set(ranks)) == len(ranks)
+        for j in range(table[e, 0]):
+            assert slots[table[e, 1 + 2 * j]][table[e, 2 + 2 * j]] == e
+    load = [sum(counts[e] / table[e, 0] for e in r) for r in slots]
+    assert max(load) <= 1.1 * counts.sum() / 4

@@ -1,8 +1,10 @@
 """Expert parallelism on real GPUs: two NCCL ranks, each holding half of a
-gpt-oss-shaped layer's experts, run the expert-parallel block on their half
-of the tokens; the gathered output must equal, bit for bit, one GPU running
-the whole layer through ms_moe_block (every row is computed by the same
-kernels in the same order either way). Needs two GPUs; skipped otherwise.
+gpt-oss-shaped layer's experts (plain sharding, and a placement that
+replicates the hottest experts into spare slots), run the expert-parallel
+block on their half of the tokens; the gathered output must equal, bit for
+bit, one GPU running the whole layer through ms_moe_block (every row is
+computed by the same kernels in the same order either way). Needs two GPUs;
+skipped otherwise.
 """
 import os
 import socket
@@ -24,12 +26,13 @@ def _free_port():
     return port
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, replicated):
     import datetime
     import torch.distributed as dist
     from moe_stream_b200 import geometry, store as S
     from moe_stream_b200.block import MoEBlock
-    from moe_stream_b200.ep import DeviceOps, ep_forward, load_local_experts
+    from moe_stream_b200.ep import (DeviceOps, ep_forward, load_local_experts, plan_placement,
+                                    routed_counts)
     from moe_stream_b200.pool import ExpertPool
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -43,13 +46,22 @@ def _rank_main(rank, world, port, out_dir):
         w, b = S.router_weights(geom, SEED, 0, zipf_s=1.1)
         x = S.rms_norm_tokens(T, geom.d_model, seed=SEED + 1, device="cuda")
         blobs = S.make_layer_blobs(geom, SEED, 0).cpu()
-        pool = ExpertPool(geom, E // world, depths=(), max_tokens=T)
+        spare = 4 if replicated else 0
+        pool = ExpertPool(geom, E // world + spare, depths=(), max_tokens=T)
         st = torch.from_numpy(pool.alloc_store()).view(geom.n_keys, geom.blob_bytes)
         st.copy_(blobs)
-        load_local_experts(pool, 0, rank, world)
         block = MoEBlock(pool, 0, w, b)
         shard = T // world
-        y = ep_forward(x[rank * shard:(rank + 1) * shard].contiguous(), DeviceOps(block, world), world)
+        xr = x[rank * shard:(rank + 1) * shard].contiguous()
+        if replicated:
+            table, slots = plan_placement(routed_counts(DeviceOps(block, world), xr), world,
+                                          E // world + spare)
+            load_local_experts(pool, 0, rank, world, slots[rank])
+            ops = DeviceOps(block, world, placement=table)
+        else:
+            load_local_experts(pool, 0, rank, world)
+            ops = DeviceOps(block, world)
+        y = ep_forward(xr, ops, world)
         torch.cuda.synchronize()
         pool.status()
         parts = [torch.empty_like(y) for _ in range(world)]
@@ -71,13 +83,14 @@ def _rank_main(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_matches_one_gpu(lib, cuda, tmp_path):
+@pytest.mark.parametrize("replicated", [False, True])
+def test_expert_parallel_matches_one_gpu(replicated, lib, cuda, tmp_path):
     import torch.multiprocessing as mp
     world = 2
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world,
-                       start_method="spawn")
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), replicated),
+                       nprocs=world, start_method="spawn")
     y_ep = torch.load(tmp_path / "y_ep.pt")
     y_ref = torch.load(tmp_path / "y_ref.pt")
     assert torch.isfinite(y_ep.float()).all()
