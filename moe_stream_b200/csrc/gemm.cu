@@ -40,7 +40,7 @@
 // warp 1 the MMAs, warp 2 owns the TMEM allocation, warps 4-19 dequantise
 // (four per TMEM lane quarter, each taking a quarter of a K tile's columns),
 // warps 20-23 drain finished accumulators (one per lane quarter). mbarrier
-// rings hand the work over: tokens + codes (TMA -> dequant/MMA, 6 deep),
+// rings hand the work over: tokens + codes (TMA -> dequant/MMA, 8 deep),
 // weights in TMEM (dequant -> MMA, 4 deep) and two accumulators (MMA <->
 // epilogue), so one item's epilogue overlaps the next item's main loop.
 // Every wait is bounded and reports MS_E_TIMEOUT instead of hanging.
@@ -57,13 +57,13 @@
 namespace ms {
 
 constexpr int GM_THREADS = 768;              // 24 warps, see the role list above
-constexpr int GM_STAGES = 6;                  // token + code tiles
+constexpr int GM_STAGES = 8;                  // token + code tiles
 constexpr int GM_A_STAGES = 4;                // weight tiles in TMEM
 constexpr int GM_TOK = GEMM_TILE_ROWS;        // tokens per tile (MMA N, at most)
 constexpr int GM_X_BYTES = GM_TOK * 128;      // 128 tokens x 64 fp16
 constexpr int GM_P_BYTES = 128 * 32;          // 128 weight rows x 64 nibbles
-constexpr int GM_OFF_P = GM_STAGES * GM_X_BYTES;                   // 96 KB
-constexpr int GM_OFF_BAR = GM_OFF_P + GM_STAGES * GM_P_BYTES;      // 120 KB (> half an SM:
+constexpr int GM_OFF_P = GM_STAGES * GM_X_BYTES;                   // 128 KB
+constexpr int GM_OFF_BAR = GM_OFF_P + GM_STAGES * GM_P_BYTES;      // 160 KB (> half an SM:
 constexpr int GM_SMEM = GM_OFF_BAR + 256 + 1024;                   //  one CTA per SM)
 // TMEM columns: accumulators [0, 128) and [128, 256); weight stage s at
 // 256 + 64 s (hi, then lo)
