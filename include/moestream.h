@@ -166,7 +166,7 @@ int ms_route(ms_pool* pool, int layer, const void* x, int T, int32_t* inds,
 /* streaming_call (engine_v3.py:493-609, engine_120b.py:78-149): route,
  * prefetch layer+d for every configured depth, acquire this layer's experts,
  * fill misses from the store, run the 4-bit expert MLPs and the weighted
- * combine. x, y bf16 [T, d_model] device buffers; T <= max_tokens.
+ * combine. Prefetch fills run on the pool's side stream (ms_pool_join). x, y bf16 [T, d_model] device buffers; T <= max_tokens.
  * Enqueued on `stream`; does not synchronise. Pool exhaustion is reported by
  * the next ms_pool_status / ms_pool_stats call. */
 int ms_moe_block(ms_pool* pool, int layer, const void* x, int T, void* y,
@@ -175,6 +175,17 @@ int ms_moe_block(ms_pool* pool, int layer, const void* x, int T, void* y,
 /* Sticky device-side status of asynchronous block calls (MS_OK or the first
  * MS_E_* seen since the last call); clears it. Synchronises `stream`. */
 int ms_pool_status(ms_pool* pool, void* stream);
+
+/* No reference counterpart (the reference's prefetch copies are synchronous
+ * MLX reads, engine_v3.py:383-396). ms_moe_block copies the slots its
+ * prefetches fill on a side stream of the pool, forked after the route step
+ * and joined into the stream of the next call that reads the arena (the
+ * next block call's expert kernels, ms_expert_mlp, the pool operations).
+ * ms_pool_join makes `stream` wait for the fills still pending. Call it on
+ * the capturing stream before ending a CUDA graph capture of block calls
+ * (the capture must join every stream it forked); the other entry points
+ * join by themselves. */
+int ms_pool_join(ms_pool* pool, void* stream);
 
 /* kernels.moe_expert_mlp (kernels.py:231-252), generalised to T tokens:
  * slots int32 [T, k] and scores f32 [T, k] (device), x bf16 [T, d_model],

@@ -69,6 +69,7 @@ EXPORTS = {
     "ms_moe_block": [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
                      ctypes.c_void_p, ctypes.c_void_p],
     "ms_pool_status": [ctypes.c_void_p, ctypes.c_void_p],
+    "ms_pool_join": [ctypes.c_void_p, ctypes.c_void_p],
     "ms_expert_mlp": [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                       ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p],
     "ms_pool_profile": [ctypes.c_void_p, ctypes.c_int],

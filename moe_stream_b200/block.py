@@ -141,16 +141,21 @@ class DecodeGraph:
         self.blocks = blocks
         self.x = torch.zeros(len(blocks), T, pool.geom.d_model, dtype=torch.bfloat16, device=dev)
         self.y = torch.zeros_like(self.x)
+        self.pool = pool
         self.graph = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream(device=dev)
+        pool.join(torch.cuda.current_stream(dev))
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.graph(self.graph, stream=s):
             for layer, b in enumerate(blocks):
                 b(self.x[layer], out=self.y[layer])
+            pool.join(s)        # the last layer's side-stream prefetch fills
         torch.cuda.current_stream(dev).wait_stream(s)
 
     def step(self, x=None):
         if x is not None:
             self.x.copy_(x, non_blocking=True)
+        # eager block calls since the capture may have left fills pending
+        self.pool.join(torch.cuda.current_stream(self.y.device))
         self.graph.replay()
         return self.y

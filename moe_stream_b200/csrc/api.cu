@@ -110,6 +110,18 @@ struct ms_pool {
   int* ep_scratch = nullptr;    // [128]: counts and cursors of ms_ep_pack
   bool profile = false;
   std::vector<cudaEvent_t> prof_ev;   // [n_layers][4]
+  // prefetch fills of ms_moe_block run on a side stream: forked after the
+  // route step, joined before the next call's expert kernels (the only
+  // readers of the slots they fill)
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_pf[2] = {nullptr, nullptr};
+  int2* pf_ring = nullptr;      // [2][max_fills]: one half per call, alternating
+  int* pf_cnt = nullptr;        // [2] fill counts, [2] error sink of ring fills
+  int pf_parity = 0;            // ring half (and event) of the next fork
+  bool pf_pending = false;      // ev_pf[pf_slot] not yet joined
+  int pf_slot = 0;
+  bool pf_captured = false;     // that fork was recorded inside a stream capture
+  unsigned long long pf_capture_id = 0;
 };
 
 namespace {
@@ -310,6 +322,12 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   if ((rc = palloc(p, &t.pend_list, t.n_slots))) return bail(rc);
   if ((rc = palloc(p, &t.fills, t.max_fills))) return bail(rc);
   if ((rc = palloc(p, &t.ctr, 1))) return bail(rc);
+  if ((rc = palloc(p, &p->pf_ring, 2 * (size_t)t.max_fills))) return bail(rc);
+  if ((rc = palloc(p, &p->pf_cnt, 3))) return bail(rc);
+  CK(cudaMemset(p->pf_cnt, 0, 3 * sizeof(int)));
+  CK(cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking));
+  CK(cudaEventCreateWithFlags(&p->ev_fork, cudaEventDisableTiming));
+  for (auto& e : p->ev_pf) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   CK(cudaMemset(t.key_of, 0xff, sizeof(int) * t.n_slots));
   CK(cudaMemset(t.slot_of, 0xff, sizeof(int) * t.n_keys));
   CK(cudaMemset(t.freq, 0, sizeof(int) * t.n_keys));
@@ -358,6 +376,9 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
       cudaSuccess)
     return bail(fail(MS_E_NOMEM, "cudaMallocHost failed"));
   (void)kp;
+  // the fill and route kernels run beside the expert kernels (the fills on
+  // the side stream): keep every SM on its largest shared-memory split
+  CK(route_prefer_shared());
   if ((rc = setup_wide(p))) return bail(rc);
   CK(cudaDeviceSynchronize());
   *out = p;
@@ -370,6 +391,10 @@ int ms_pool_destroy(ms_pool* p) {
   cudaDeviceSynchronize();
   for (void* b : p->dev_blocks) cudaFree(b);
   for (cudaEvent_t e : p->prof_ev) cudaEventDestroy(e);
+  if (p->ev_fork) cudaEventDestroy(p->ev_fork);
+  for (cudaEvent_t e : p->ev_pf)
+    if (e) cudaEventDestroy(e);
+  if (p->side) cudaStreamDestroy(p->side);
   if (p->h_pinned) cudaFreeHost(p->h_pinned);
   if (p->store_owned && p->store_host) cudaFreeHost(p->store_host);
   if (p->store_registered && p->store_host) cudaHostUnregister(p->store_host);
@@ -428,6 +453,41 @@ int ms_set_router(ms_pool* p, int layer, const void* w_r, const void* b_r) {
   return MS_OK;
 }
 
+// Make stream s wait for the pending side-stream prefetch fills. Inside a
+// capture the wait is a graph edge; fills forked before the capture began
+// are waited for on the host instead (a capture cannot depend on them).
+static int join_side(ms_pool* p, cudaStream_t s) {
+  if (!p->pf_pending) return MS_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  unsigned long long id = 0;
+  CK(cudaStreamGetCaptureInfo(s, &cs, &id));
+  const bool cap = cs == cudaStreamCaptureStatusActive;
+  if (cap == p->pf_captured && (!cap || id == p->pf_capture_id)) {
+    CK(cudaStreamWaitEvent(s, p->ev_pf[p->pf_slot], 0));
+  } else if (!p->pf_captured) {
+    CK(cudaEventSynchronize(p->ev_pf[p->pf_slot]));
+  } else {
+    return fail(MS_E_STATE,
+                "prefetch fills forked inside a stream capture were not joined into it "
+                "(call ms_pool_join on the capturing stream before ending the capture)");
+  }
+  p->pf_pending = false;
+  return MS_OK;
+}
+
+int ms_pool_join(ms_pool* p, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  CK(cudaSetDevice(p->device));
+  return join_side(p, static_cast<cudaStream_t>(stream));
+}
+
+// CTAs of a fill kernel. The store is read over PCIe (~50 GB/s, a few µs
+// of latency): 32 CTAs x 16 KiB in flight cover that bandwidth-delay
+// product several times over, and more CTAs only crowd the memory pipelines
+// of the SMs that the kernels running beside a side-stream fill also use
+// (296 CTAs cost the decode stack ~8 % of its throughput).
+constexpr int FILL_CTAS = 32;
+
 static FillArgs fill_args(ms_pool* p) {
   FillArgs f{};
   f.store = p->store_dev;
@@ -455,8 +515,9 @@ static int pool_op(ms_pool* p, int op, int layer, const int32_t* experts, int n,
     r.experts[i] = experts[i];
   }
   CK(cudaSetDevice(p->device));
+  if (int rc = join_side(p, s)) return rc;
   CK(launch_pool_op(p->tab, r, p->d_slots, p->d_opstatus, s));
-  CK(launch_fill(fill_args(p), p->sm_count * 2, s));
+  CK(launch_fill(fill_args(p), FILL_CTAS, s));
   return MS_OK;
 }
 
@@ -492,6 +553,7 @@ int ms_pool_read(ms_pool* p, int slot, int layer, int expert, void* stream) {
   if (off + blob > p->store_bytes)
     return fail(MS_E_IO, "short read: blob (%d, %d) lies past the end of the store", layer, expert);
   CK(cudaSetDevice(p->device));
+  if (int rc = join_side(p, static_cast<cudaStream_t>(stream))) return rc;
   CK(cudaMemcpyAsync(p->arena + (size_t)slot * blob, p->store_host + off, blob,
                      cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream)));
   return MS_OK;
@@ -541,7 +603,8 @@ int ms_pool_arena(ms_pool* p, void** base, size_t* bytes) {
 }
 
 static int route_common(ms_pool* p, int layer, const void* x, int T, cudaStream_t s, bool block,
-                        bool wide, int32_t* inds_out, void* scores_out, int32_t* pred_out) {
+                        bool wide, int32_t* inds_out, void* scores_out, int32_t* pred_out,
+                        int ring = -1) {
   if (layer < 0 || layer >= p->geom.n_layers) return fail(MS_E_INVALID, "layer %d out of range", layer);
   if (T <= 0 || T > p->cfg.max_tokens)
     return fail(MS_E_INVALID, "T=%d outside [1, max_tokens=%d]", T, p->cfg.max_tokens);
@@ -582,6 +645,10 @@ static int route_common(ms_pool* p, int layer, const void* x, int T, cudaStream_
   a.do_groups = block ? 1 : 0;
   a.grp = p->grp;
   a.pair_slot = block ? p->pair_slot : nullptr;
+  if (ring >= 0) {
+    a.pf_ring = p->pf_ring + (size_t)ring * p->tab.max_fills;
+    a.pf_cnt = p->pf_cnt + ring;
+  }
   CK(cudaSetDevice(p->device));
   if (wide) {
     CK(launch_route_wide(a, p->wa, s));
@@ -704,11 +771,43 @@ int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* str
   const bool wide = p->wide && (T * k >= p->wide_min_pairs || T > p->narrow_tokens);
   if (!wide && T > p->narrow_tokens)
     return fail(MS_E_INVALID, "T=%d exceeds the %d tokens of the decode scratch", T, p->narrow_tokens);
-  int rc = route_common(p, layer, x, T, s, true, wide, nullptr, nullptr, nullptr);
+  // decode: this call's prefetch fills (slots of later layers) go to the
+  // side stream and overlap everything up to the next call's expert kernels
+  bool fork = false;
+  for (int i = 0; i < p->cfg.n_depths; ++i) fork |= layer + p->cfg.depths[i] < p->geom.n_layers;
+  fork = fork && !wide;
+  const int q = p->pf_parity;
+  int rc = route_common(p, layer, x, T, s, true, wide, nullptr, nullptr, nullptr, fork ? q : -1);
   if (rc) return rc;
   if (ev) CK(cudaEventRecordWithFlags(ev[1], s, rec_flags));
-  CK(launch_fill(fill_args(p), p->sm_count * 2, s));
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  unsigned long long cap_id = 0;
+  if (fork) {
+    CK(cudaStreamGetCaptureInfo(s, &cs, &cap_id));
+    CK(cudaEventRecord(p->ev_fork, s));
+    CK(cudaStreamWaitEvent(p->side, p->ev_fork, 0));
+    FillArgs f = fill_args(p);
+    f.ring = p->pf_ring + (size_t)q * p->tab.max_fills;
+    f.ring_cnt = p->pf_cnt + q;
+    f.ring_err = p->pf_cnt + 2;
+    CK(launch_fill(f, FILL_CTAS, p->side));
+    CK(cudaEventRecord(p->ev_pf[q], p->side));
+  }
+  FillArgs fa = fill_args(p);
+  fa.acquire_only = fork ? 1 : 0;
+  fa.pdl = (fork && !ev) ? 1 : 0;
+  CK(launch_fill(fa, FILL_CTAS, s));
   if (ev) CK(cudaEventRecordWithFlags(ev[2], s, rec_flags));
+  // the previous call's prefetch fills must land before any expert kernel
+  rc = join_side(p, s);
+  if (fork) {
+    p->pf_pending = true;
+    p->pf_slot = q;
+    p->pf_captured = cs == cudaStreamCaptureStatusActive;
+    p->pf_capture_id = cap_id;
+    p->pf_parity = q ^ 1;
+  }
+  if (rc) return rc;
   if (wide) {
     if ((rc = wide_experts(p, x, T, k, p->inds, p->scores_f, p->pair_slot, y, s))) return rc;
   } else {
@@ -723,11 +822,15 @@ int ms_pool_status(ms_pool* p, void* stream) {
   if (!p) return fail(MS_E_INVALID, "NULL pool");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CK(cudaSetDevice(p->device));
+  if (int rc = join_side(p, s)) return rc;
   CK(cudaStreamSynchronize(s));
-  int st = 0;
+  int st = 0, st_pf = 0;
   CK(cudaMemcpy(&st, &p->tab.ctr->status, sizeof(int), cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(&st_pf, p->pf_cnt + 2, sizeof(int), cudaMemcpyDeviceToHost));
   int zero = 0;
   CK(cudaMemcpy(&p->tab.ctr->status, &zero, sizeof(int), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(p->pf_cnt + 2, &zero, sizeof(int), cudaMemcpyHostToDevice));
+  if (!st) st = st_pf;
   if (st == MS_E_EXHAUSTED) return fail(st, "pool exhausted: every slot pinned or pending");
   if (st) return fail(st, "device-side error %d in an earlier block call", st);
   return MS_OK;
@@ -742,6 +845,7 @@ int ms_expert_mlp(ms_pool* p, const int32_t* slots, const float* scores, const v
   if (!aligned16(x) || !aligned16(y)) return fail(MS_E_INVALID, "x and y must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CK(cudaSetDevice(p->device));
+  if (int rc = join_side(p, s)) return rc;
   // wide batches (and any k other than top_k): slot-keyed grouped GEMM
   const long long P = (long long)T * k;
   const bool wide = p->wide && P <= p->max_pairs &&

@@ -1,0 +1,137 @@
+// Pieces of the decode expert kernels (expert.cu: k_up / k_down): the
+// 16-row tile dot product on tensor cores from shared memory, the
+// activations with MLX's rounding points, and the shared-memory layouts of
+// the weight tiles.
+#pragma once
+#include "ms_common.cuh"
+#include "frag.cuh"
+
+namespace ms {
+
+constexpr int EX_THREADS = 256;
+constexpr int EX_WARPS = EX_THREADS / 32;
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// The activations keep MLX's rounding points: gather_qmm returns bf16, and
+// every elementwise op of the SwiGLU rounds its result to bf16
+// (engine_v3.py:592-597, engine_120b.py:136-143), so the block tracks the
+// reference's arithmetic, not a more precise variant of it.
+// 1/(1+e^-v); __frcp_rn is the correctly rounded reciprocal, i.e. 1.f / x
+__device__ __forceinline__ float sigm(float v) { return __frcp_rn(1.f + expf(-v)); }
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  // activations.swiglu(gate, x) = silu(gate) * x, silu(v) = v * sigmoid(v)
+  return bfr(bfr(g * bfr(sigm(g))) * u);
+}
+
+__device__ __forceinline__ float clamped_swiglu(float g, float u) {
+  // gpt_oss.swiglu(x_linear=u, x_glu=g): alpha 1.702 (a bf16 1.703125 once it
+  // meets a bf16 operand), limit 7, (linear + 1) (engine_120b.py:27-29)
+  g = fminf(g, 7.f);
+  u = fminf(fmaxf(u, -7.f), 7.f);
+  const float og = bfr(g * bfr(sigm(bfr(1.703125f * g))));
+  return bfr(og * bfr(u + 1.f));
+}
+
+// Padded shared-memory row stride for a weight row of `row_bytes`: a stride
+// of 8 (mod 32) words puts the 8 rows a warp reads at once on disjoint bank
+// octets, so the 8-byte fragment loads take the minimum two wavefronts.
+__host__ __device__ constexpr int padded_stride(int row_bytes) {
+  int s = row_bytes;
+  while (((s >> 2) & 31) != 8) s += 16;
+  return s;
+}
+
+// Activation fragments (frag layout) of quantisation groups [kg0, kg1) for
+// lane quad position c. SRC 0: read-only path (written before the launch);
+// 1: through L2 (written by other CTAs of the same launch); 2: generic
+// loads (a shared-memory copy, or global memory).
+template <int KPW, int SRC>
+__device__ __forceinline__ void load_frags(uint4* b0, uint4* b1, const __half* frag_b, int kg0,
+                                           int kg1, int c) {
+#pragma unroll
+  for (int q = 0; q < KPW; ++q) {
+    b0[q] = make_uint4(0, 0, 0, 0);
+    b1[q] = b0[q];
+    const int kg = kg0 + q;
+    if (frag_b && kg < kg1) {
+      const uint4* fb = reinterpret_cast<const uint4*>(frag_b + kg * 64);
+      if (SRC == 0) {
+        b0[q] = __ldg(fb + c);
+        b1[q] = __ldg(fb + 4 + c);
+      } else if (SRC == 1) {
+        b0[q] = __ldcg(fb + c);
+        b1[q] = __ldcg(fb + 4 + c);
+      } else {
+        b0[q] = fb[c];
+        b1[q] = fb[4 + c];
+      }
+    }
+  }
+}
+
+// Dot products of a 16-row tile held in shared memory (rows at `stride`
+// bytes) over quantisation groups [kg0, kg1), for the 8 activation columns of
+// this pass, from activation fragments b0/b1 (load_frags). Scales/biases:
+// sS/sB [16][G] relative to the tile; per-group activation sums of the two
+// columns of this lane at sum_c0 / sum_c1.
+template <int KPW>
+__device__ __forceinline__ void tile_dot_frags(float* tot, const uint8_t* At, int stride, int G,
+                                               int kg0, int kg1, int g4, int c, const uint16_t* sS,
+                                               const uint16_t* sB, const uint4* b0, const uint4* b1,
+                                               const float* sum_c0, const float* sum_c1) {
+#pragma unroll
+  for (int q = 0; q < KPW; ++q) {
+    const int kg = kg0 + q;
+    if (kg >= kg1) break;
+    const uint2 ra = *reinterpret_cast<const uint2*>(At + g4 * stride + kg * 32 + 8 * c);
+    const uint2 rb = *reinterpret_cast<const uint2*>(At + (g4 + 8) * stride + kg * 32 + 8 * c);
+    float cc[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_group(cc, ra, rb, b0[q], b1[q]);
+    float xs0 = 0.f, xp0 = 0.f, xs1 = 0.f, xp1 = 0.f;
+    if (sum_c0) { const float2 v = *reinterpret_cast<const float2*>(sum_c0 + kg * 2); xs0 = v.x; xp0 = v.y; }
+    if (sum_c1) { const float2 v = *reinterpret_cast<const float2*>(sum_c1 + kg * 2); xs1 = v.x; xp1 = v.y; }
+    const float s0 = bf2f(sS[g4 * G + kg]), s1 = bf2f(sS[(g4 + 8) * G + kg]);
+    const float q0 = bf2f(sB[g4 * G + kg]), q1 = bf2f(sB[(g4 + 8) * G + kg]);
+    tot[0] += s0 * (cc[0] - 1024.f * xp0) + q0 * xs0;
+    tot[1] += s0 * (cc[1] - 1024.f * xp1) + q0 * xs1;
+    tot[2] += s1 * (cc[2] - 1024.f * xp0) + q1 * xs0;
+    tot[3] += s1 * (cc[3] - 1024.f * xp1) + q1 * xs1;
+  }
+}
+
+// tile_dot_frags with the fragments read from global memory (frag layout)
+// by the read-only path.
+template <int KPW>
+__device__ __forceinline__ void tile_dot_smem(float* tot, const uint8_t* At, int stride, int G,
+                                              int kg0, int kg1, int g4, int c, const uint16_t* sS,
+                                              const uint16_t* sB, const __half* frag_b,
+                                              const float* sum_c0, const float* sum_c1) {
+  uint4 b0[KPW], b1[KPW];
+  load_frags<KPW, 0>(b0, b1, frag_b, kg0, kg1, c);
+  tile_dot_frags<KPW>(tot, At, stride, G, kg0, kg1, g4, c, sS, sB, b0, b1, sum_c0, sum_c1);
+}
+
+struct UpSmem {
+  static __host__ __device__ int stride(int K) { return padded_stride(K / 2); }
+  static __host__ __device__ int a_bytes(int K) { return 16 * stride(K); }
+  static __host__ __device__ int sb_bytes(int G) { return 16 * G * 2; }
+  static __host__ __device__ int total(int K) {
+    const int G = K / 64;
+    return 2 * a_bytes(K) + 4 * sb_bytes(G) + EX_WARPS * 2 * 4 * 32 * 4 + 16;
+  }
+};
+
+struct DownSmem {
+  static __host__ __device__ int stride(int F) { return padded_stride(F / 2); }
+  static __host__ __device__ int a_bytes(int F, int RT) { return RT * 16 * stride(F); }
+  static __host__ __device__ int sb_bytes(int GF, int RT) { return RT * 16 * GF * 2; }
+  static __host__ __device__ int total(int F, int RT) {
+    const int GF = F / 64;
+    return a_bytes(F, RT) + 2 * sb_bytes(GF, RT) + EX_WARPS * 4 * 32 * 4 + 8 * GF * 2 * 4 + 16;
+  }
+};
+
+}  // namespace ms

@@ -38,6 +38,8 @@ struct RouteArgs {
   int do_groups;
   Groups grp;
   int* pair_slot;             // [T, k] or null
+  int2* pf_ring;              // this call's half of the prefetch-fill ring, or null
+  int* pf_cnt;                // its fill count
 };
 
 struct PoolReq {
@@ -55,6 +57,11 @@ struct FillArgs {
   const int2* fills;
   int max_fills;
   TableCtr* ctr;
+  int acquire_only;           // fills[n_fill_pf, n_fill) only: the prefetch part runs elsewhere
+  const int2* ring;           // else: this list of ring_cnt fills (a prefetch-fill ring half)
+  const int* ring_cnt;
+  int* ring_err;              // error sink of ring fills
+  int pdl;                    // launched as a programmatic dependent of the route step
 };
 
 struct MlpPrepArgs {
@@ -167,6 +174,7 @@ struct EpPackArgs {
 cudaError_t launch_mlp_wide_prep(const MlpWideArgs& a, int sms, cudaStream_t s);
 cudaError_t launch_ep_pack(const EpPackArgs& a, int sms, cudaStream_t s);
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s);
+cudaError_t route_prefer_shared();
 cudaError_t launch_route_wide(const RouteArgs& a, const WideArgs& w, cudaStream_t s);
 cudaError_t launch_scatter(const ScatterArgs& a, int grid, cudaStream_t s);
 // Persistent grouped GEMM over at most max_items (token tile, feature tile)

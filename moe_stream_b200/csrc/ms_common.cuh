@@ -31,7 +31,7 @@ struct TableCtr {
   int n_pin;             // pin_list length
   int n_fill;            // fills produced by the current call
   int status;            // sticky error code (0 / negative MS_E_*)
-  int pad;
+  int n_fill_pf;         // fills[0, n_fill_pf) of the current call came from its prefetches
   long long st[ST_N];
 };
 

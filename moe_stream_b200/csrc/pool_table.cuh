@@ -21,6 +21,7 @@ namespace ms {
 struct OpCtx {
   long long clock, use_clock;
   int n_free, n_pend, n_pin, n_fill;
+  int n_fill_pf;            // n_fill when the call's prefetch requests were done
   int status;
   int victim_key;           // key evicted by the last warp_alloc, -1 if none
   int n_pend0;              // pending keys left by earlier calls (0 on the fused path)
@@ -32,7 +33,7 @@ __device__ __forceinline__ void op_load(const DevTable& T, OpCtx* c, int lane) {
     const TableCtr g = *T.ctr;                 // all loads issued before any store
     c->clock = g.clock; c->use_clock = g.use_clock;
     c->n_free = g.n_free; c->n_pend = g.n_pend; c->n_pin = g.n_pin;
-    c->n_fill = 0; c->status = 0; c->victim_key = -1; c->n_pend0 = g.n_pend;
+    c->n_fill = 0; c->n_fill_pf = 0; c->status = 0; c->victim_key = -1; c->n_pend0 = g.n_pend;
     for (int i = 0; i < ST_N; ++i) c->st[i] = g.st[i];
   }
   __syncwarp();
@@ -47,7 +48,7 @@ __device__ __forceinline__ void op_store(const DevTable& T, OpCtx* c, int lane) 
     g.n_fill = c->n_fill;
     const int prev = T.ctr->status;            // sticky: the first error stays
     g.status = prev ? prev : c->status;
-    g.pad = 0;
+    g.n_fill_pf = c->n_fill_pf;
     for (int i = 0; i < ST_N; ++i) g.st[i] = c->st[i];
     *T.ctr = g;
   }

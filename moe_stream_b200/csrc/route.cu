@@ -126,8 +126,19 @@ __device__ __forceinline__ void warp_pool_step(const RouteArgs& A, int (*s_pred)
   kc_add(Tb, s_kc, ra, A.layer, s_acq, n_acq, false, lane);
   kc_load(Tb, s_op, s_kc, lane);
   for (int dd = 0; dd < A.n_pred; ++dd) warp_prefetch(Tb, s_op, s_kc, rp[dd], lane);
+  __syncwarp();
+  if (lane == 0) s_op->n_fill_pf = s_op->n_fill;
+  __syncwarp();
   warp_acquire(Tb, s_op, s_kc, ra, s_slots, s_waits, lane);
   op_store(Tb, s_op, lane);
+  if (A.pf_ring) {
+    // the prefetch fills leave the per-call list for this call's ring half,
+    // which the side-stream fill reads while later calls rewrite the list
+    const int n = min(s_op->n_fill_pf, Tb.max_fills);
+    for (int i = lane; i < n; i += 32) A.pf_ring[i] = Tb.fills[i];
+    if (lane == 0) *A.pf_cnt = n;
+    __syncwarp();
+  }
 }
 
 __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
@@ -547,6 +558,8 @@ __global__ void k_pool_op(DevTable Tb, PoolReq R, int* slots_out, int* op_status
   int st = 0;
   if (R.op == 0) {
     warp_prefetch(Tb, &s_op, &s_kc, r, lane);
+    __syncwarp();
+    if (lane == 0) s_op.n_fill_pf = s_op.n_fill;
   } else {
     st = warp_acquire(Tb, &s_op, &s_kc, r, s_slots, s_waits, lane);
     for (int i = lane; i < R.n; i += 32) slots_out[i] = s_slots[i];
@@ -559,14 +572,33 @@ __global__ void k_pool_op(DevTable Tb, PoolReq R, int* slots_out, int* op_status
 // is mapped pinned host memory read directly by the SMs, so the fill list
 // never has to travel to the host.
 __global__ void __launch_bounds__(256) k_fill(FillArgs F) {
-  const int n = min(F.ctr->n_fill, F.max_fills);
+  if (F.pdl) {
+    // a programmatic dependent of the route step: let the expert kernels
+    // launch now; the fill list is read once the route step has finished
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  }
+  const int2* list;
+  int first, n;
+  int* err;
+  if (F.ring) {
+    list = F.ring;
+    first = 0;
+    n = min(*F.ring_cnt, F.max_fills);
+    err = F.ring_err;
+  } else {
+    list = F.fills;
+    n = min(F.ctr->n_fill, F.max_fills);
+    first = F.acquire_only ? min(F.ctr->n_fill_pf, n) : 0;
+    err = &F.ctr->status;
+  }
   const long long chunks = F.blob / 16384;
-  const long long total = (long long)n * chunks;
+  const long long total = (long long)(n - first) * chunks;
   for (long long i = blockIdx.x; i < total; i += gridDim.x) {
-    const int2 f = F.fills[i / chunks];
+    const int2 f = list[first + i / chunks];
     const long long part = i % chunks;
     if (f.y < 0 || (long long)f.y >= F.store_keys) {
-      if (threadIdx.x == 0) atomicCAS(&F.ctr->status, 0, -7);
+      if (threadIdx.x == 0) atomicCAS(err, 0, -7);
       continue;
     }
     const uint4* src = reinterpret_cast<const uint4*>(F.store + (long long)f.y * F.blob + part * 16384);
@@ -612,6 +644,23 @@ __global__ void __launch_bounds__(RT_THREADS) k_mlp_prep(MlpPrepArgs A) {
 }
 
 // ----------------------------------------------------------------- launchers
+// The kernels that run beside the expert kernels (the route step before
+// them, the fills on the pool's side stream) ask for the largest
+// shared-memory carveout: an SM can only change its L1/shared split once it
+// has drained, so a long fill CTA on a small-shared configuration would keep
+// the expert kernels' CTAs off that SM until the fill ends.
+cudaError_t route_prefer_shared() {
+  const void* fns[] = {reinterpret_cast<const void*>(k_route_step),
+                       reinterpret_cast<const void*>(k_fill),
+                       reinterpret_cast<const void*>(k_mlp_prep)};
+  for (const void* f : fns) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s) {
   k_route_step<<<grid, RT_THREADS, 0, s>>>(a);
   return cudaGetLastError();
@@ -631,8 +680,20 @@ cudaError_t launch_pool_op(const DevTable& t, const PoolReq& r, int* slots_out, 
   return cudaGetLastError();
 }
 cudaError_t launch_fill(const FillArgs& f, int grid, cudaStream_t s) {
-  k_fill<<<grid, 256, 0, s>>>(f);
-  return cudaGetLastError();
+  if (!f.pdl) {
+    k_fill<<<grid, 256, 0, s>>>(f);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_fill, f);
 }
 cudaError_t launch_mlp_prep(const MlpPrepArgs& a, cudaStream_t s) {
   const size_t smem = ((a.n_slots + 1 + 31) / 32) * sizeof(unsigned);

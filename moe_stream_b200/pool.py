@@ -218,6 +218,11 @@ class ExpertPool:
         """Raise the first device-side error of earlier asynchronous calls."""
         _lib.check(self._lib.ms_pool_status(self._h, _stream_ptr(stream)))
 
+    def join(self, stream=None):
+        """Make `stream` wait for the prefetch fills still running on the
+        pool's side stream (needed before ending a graph capture)."""
+        _lib.check(self._lib.ms_pool_join(self._h, _stream_ptr(stream)))
+
     def close(self):
         if getattr(self, "_h", None) is not None and self._h.value:
             self.views = {}

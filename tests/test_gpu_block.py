@@ -222,3 +222,49 @@ def test_decode_stack_slot_tables_match_oracle(model, lib, cuda):
         assert (s["prefetch"], s["cache"], s["miss"]) == (ref["prefetch"], ref["cache"], ref["miss"])
     finally:
         pool.close()
+
+
+def test_side_stream_fills_match_serialised_calls(lib, cuda):
+    """Prefetch fills run on the pool's side stream and overlap the next
+    call's route step. A decode stack replayed from a CUDA graph (no host
+    synchronisation anywhere) must produce the same outputs and the same
+    slot table, bit for bit, as the same calls made one at a time with a
+    full synchronisation after each (every fill long finished)."""
+    from moe_stream_b200.block import DecodeGraph
+    L, steps = 4, 6
+    geom = geometry.qwen3(n_layers=L)
+    g = torch.Generator().manual_seed(21)
+    xs = []
+    for _ in range(steps):
+        h = torch.randn(1, geom.d_model, generator=g)
+        row = []
+        for _ in range(L):
+            row.append((h / h.pow(2).mean().sqrt()).to(torch.bfloat16))
+            h = h + 0.1 * torch.randn(1, geom.d_model, generator=g)
+        xs.append(torch.stack(row).cuda())          # [L, 1, d]
+    outs = {}
+    for mode in ("serial", "graph"):
+        pool, st, blocks = make_pool(geom, geom.n_keys // 2, range(L), range(geom.n_experts),
+                                     seed=4, zipf=1.1, max_tokens=1)
+        try:
+            ys = []
+            if mode == "serial":
+                for step in range(steps):
+                    for layer in range(L):
+                        ys.append(blocks[layer](xs[step][layer]).clone())
+                        torch.cuda.synchronize()
+                        pool.status()
+            else:
+                graph = DecodeGraph(blocks)
+                for step in range(steps):
+                    ys.extend(y.clone() for y in graph.step(xs[step]))
+                torch.cuda.synchronize()
+                pool.status()
+            outs[mode] = (torch.stack(ys).cpu(), pool.table().tolist(), pool.stats())
+        finally:
+            pool.close()
+    (ya, ta, sa), (yb, tb, sb) = outs["serial"], outs["graph"]
+    assert ta == tb
+    assert (sa["prefetch"], sa["cache"], sa["miss"]) == (sb["prefetch"], sb["cache"], sb["miss"])
+    assert torch.equal(ya, yb)
+
