@@ -796,6 +796,15 @@ int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* str
   FillArgs fa = fill_args(p);
   fa.acquire_only = fork ? 1 : 0;
   fa.pdl = (fork && !ev) ? 1 : 0;
+  // the next layer's call reads the router of layer+1+depth for its
+  // speculation before anything else, usually its first touch this step
+  if (!wide && p->cfg.n_depths > 0) {
+    const int nxt = layer + 1 + p->cfg.depths[0];
+    if (nxt < p->geom.n_layers && p->w_r[nxt]) {
+      fa.l2_next = p->w_r[nxt];
+      fa.l2_next_bytes = (unsigned)((size_t)p->geom.n_experts * p->geom.d_model * 2) & ~15u;
+    }
+  }
   CK(launch_fill(fa, FILL_CTAS, s));
   if (ev) CK(cudaEventRecordWithFlags(ev[2], s, rec_flags));
   // the previous call's prefetch fills must land before any expert kernel

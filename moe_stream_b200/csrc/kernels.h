@@ -62,6 +62,8 @@ struct FillArgs {
   const int* ring_cnt;
   int* ring_err;              // error sink of ring fills
   int pdl;                    // launched as a programmatic dependent of the route step
+  const void* l2_next;        // bytes the next block call's route step will read first
+  unsigned l2_next_bytes;     // (a multiple of 16), prefetched into L2; 0 for none
 };
 
 struct MlpPrepArgs {

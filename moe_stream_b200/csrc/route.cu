@@ -158,6 +158,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
     for (int t = 0; t < T; ++t) {
       const uint16_t* x = A.x + (long long)t * d;
       float acc = 0.f;
+#pragma unroll 8
       for (int ch = lane; ch < nchunk; ch += 32) {
         const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w) + ch);
         const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x) + ch);
@@ -215,30 +216,35 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
 
   const int kp = A.kp;
   const bool small = T * k <= SMALL_P;
-  for (int t = warp; t < T; t += RT_THREADS / 32) {
+  // one task per (token, router): task part 0 routes the token, part d >= 1
+  // is the speculation of prefetch depth d-1 -- top-(k*widen) of the target
+  // layer's raw logits (engine_v3.py:476-483, 509-514). Tasks go to warps
+  // round-robin, so a token's routing and its predictions run side by side.
+  const int parts = 1 + A.n_pred;
+  for (int task = warp; task < T * parts; task += RT_THREADS / 32) {
+    const int t = task / parts, part = task % parts;
     const float* lg = A.logits + (long long)t * rows;
     uint16_t* vals = s_vals[warp];
     int* sel = s_sel[warp];
-    const float sc = route_token(lg, A.geo, vals, sel, lane);
-    if (lane < k) {
-      const int e = sel[lane];
-      A.inds[t * k + lane] = e;
-      A.scores[t * k + lane] = f2bf(sc);
-      A.scores_f[t * k + lane] = sc;
-      if (small) s_inds[t * k + lane] = e;
-      atomicOr(&s_acq_mask[e >> 5], 1u << (e & 31));
-    }
-    __syncwarp();
-    // speculation: top-(k*widen) of the target layer's raw logits
-    // (engine_v3.py:476-483, 509-514)
-    for (int dd = 0; dd < A.n_pred; ++dd) {
-      predict_token(lg + (dd + 1) * E, E, kp, vals, sel, lane);
+    if (part == 0) {
+      const float sc = route_token(lg, A.geo, vals, sel, lane);
+      if (lane < k) {
+        const int e = sel[lane];
+        A.inds[t * k + lane] = e;
+        A.scores[t * k + lane] = f2bf(sc);
+        A.scores_f[t * k + lane] = sc;
+        if (small) s_inds[t * k + lane] = e;
+        atomicOr(&s_acq_mask[e >> 5], 1u << (e & 31));
+      }
+    } else {
+      const int dd = part - 1;
+      predict_token(lg + part * E, E, kp, vals, sel, lane);
       for (int j = lane; j < kp; j += 32) {
         atomicOr(&s_pred_mask[dd][sel[j] >> 5], 1u << (sel[j] & 31));
         if (dd == 0 && A.pred_out) A.pred_out[t * kp + j] = sel[j];
       }
-      __syncwarp();
     }
+    __syncwarp();
   }
   __syncthreads();
 
@@ -576,8 +582,21 @@ __global__ void __launch_bounds__(256) k_fill(FillArgs F) {
     // a programmatic dependent of the route step: let the expert kernels
     // launch now; the fill list is read once the route step has finished
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
   }
+  if (F.l2_next_bytes && threadIdx.x == 0) {
+    // the next block call's router rows that are not in L2 yet (read-only
+    // weights, so this may run before the wait): one slice per CTA
+    const unsigned slice = ((F.l2_next_bytes / gridDim.x) + 15u) & ~15u;
+    const unsigned off = slice * blockIdx.x;
+    if (off < F.l2_next_bytes) {
+      const unsigned n = min(slice, F.l2_next_bytes - off);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                       static_cast<const uint8_t*>(F.l2_next) + off),
+                   "r"(n)
+                   : "memory");
+    }
+  }
+  if (F.pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
   const int2* list;
   int first, n;
   int* err;
