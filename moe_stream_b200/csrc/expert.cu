@@ -27,8 +27,10 @@
 
 namespace ms {
 
+// Qwen3 shapes (KPW 4): three CTAs per SM, so a batch-1 layer's 384 tiles
+// fit one wave; the wider rows of the other shapes keep two.
 template <int MODEL, int KPW>
-__global__ void __launch_bounds__(EX_THREADS) k_up(ExpArgs A) {
+__global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2) k_up(ExpArgs A) {
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_wait();                                   // slots and groups come from the route step
   pdl_trigger();
@@ -65,8 +67,7 @@ __global__ void __launch_bounds__(EX_THREADS) k_up(ExpArgs A) {
     }
   }
   __syncthreads();
-  bool ok = true;
-  if (slot >= 0) ok = mbar_wait(bar, 0, A.status);
+  bool ok = true, waited = false;
 
   for (int n0 = 0; n0 < m; n0 += 8) {
     const int* pairs = A.grp.grp_pairs + start + n0;
@@ -77,11 +78,20 @@ __global__ void __launch_bounds__(EX_THREADS) k_up(ExpArgs A) {
     const __half* fb = pb >= 0 ? A.xfrag + (long long)(pb / k) * G * 64 : nullptr;
     const float* s0 = pc0 >= 0 ? A.xsum + (long long)(pc0 / k) * G * 2 : nullptr;
     const float* s1 = pc1 >= 0 ? A.xsum + (long long)(pc1 / k) * G * 2 : nullptr;
+    // the activations come in while the tile's weights are still in flight
+    uint4 b0[KPW], b1[KPW];
+    float2 v0[KPW], v1[KPW];
+    load_frags<KPW, 0>(b0, b1, (slot >= 0) ? fb : nullptr, kg0, kg1, c);
+    load_sums<KPW>(v0, v1, s0, s1, kg0, kg1);
+    if (!waited) {
+      if (slot >= 0) ok = mbar_wait(bar, 0, A.status);
+      waited = true;
+    }
     float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f};
     if (slot >= 0 && ok && kg0 < kg1) {
-      tile_dot_smem<KPW>(tg, sA[0], stride, G, kg0, kg1, g4, c, sSB, sSB + sbn, fb, s0, s1);
-      tile_dot_smem<KPW>(tu, sA[1], stride, G, kg0, kg1, g4, c, sSB + 2 * sbn, sSB + 3 * sbn, fb,
-                         s0, s1);
+      tile_dot_regs<KPW>(tg, sA[0], stride, G, kg0, kg1, g4, c, sSB, sSB + sbn, b0, b1, v0, v1);
+      tile_dot_regs<KPW>(tu, sA[1], stride, G, kg0, kg1, g4, c, sSB + 2 * sbn, sSB + 3 * sbn, b0, b1,
+                         v0, v1);
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -195,6 +205,11 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
   for (int n0 = 0; n0 < m; n0 += 8) {
     const int* pairs = A.grp.grp_pairs + start + n0;
     const int nn = min(8, m - n0);
+    const int pb = (g4 < nn) ? pairs[g4] : -1;
+    // h fragments requested before the sums' round trip, so the two overlap
+    uint4 b0[KPW], b1[KPW];
+    load_frags<KPW, 0>(b0, b1, (pb >= 0 && slot >= 0) ? A.hfrag + (long long)pb * G * 64 : nullptr,
+                       kg0, kg1, c);
     // per-group sums of h for this pass's columns: 4 row-tile partials each
     for (int i = threadIdx.x; i < nn * G; i += EX_THREADS) {
       const int col = i / G, kg = i % G;
@@ -205,12 +220,10 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
       s_sums[(col * G + kg) * 2 + 1] = (a.y + a.w) + (b.y + b.w);
     }
     __syncthreads();
-    const int pb = (g4 < nn) ? pairs[g4] : -1;
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
     if (slot >= 0 && ok && kg0 < kg1) {
-      tile_dot_smem<KPW>(tot, sA + sub * 16 * stride, stride, G, kg0, kg1, g4, c,
-                         sS + sub * 16 * G, sB + sub * 16 * G,
-                         pb >= 0 ? A.hfrag + (long long)pb * G * 64 : nullptr,
+      tile_dot_frags<KPW>(tot, sA + sub * 16 * stride, stride, G, kg0, kg1, g4, c,
+                         sS + sub * 16 * G, sB + sub * 16 * G, b0, b1,
                          (2 * c < nn) ? s_sums + (2 * c) * G * 2 : nullptr,
                          (2 * c + 1 < nn) ? s_sums + (2 * c + 1) * G * 2 : nullptr);
     }

@@ -77,6 +77,47 @@ __device__ __forceinline__ void load_frags(uint4* b0, uint4* b1, const __half* f
 // this pass, from activation fragments b0/b1 (load_frags). Scales/biases:
 // sS/sB [16][G] relative to the tile; per-group activation sums of the two
 // columns of this lane at sum_c0 / sum_c1.
+// Per-group activation sums (X, X') of the two columns of this lane for
+// groups [kg0, kg1), into registers (zeros where a column is absent).
+template <int KPW>
+__device__ __forceinline__ void load_sums(float2* v0, float2* v1, const float* sum_c0,
+                                          const float* sum_c1, int kg0, int kg1) {
+#pragma unroll
+  for (int q = 0; q < KPW; ++q) {
+    const int kg = kg0 + q;
+    v0[q] = make_float2(0.f, 0.f);
+    v1[q] = v0[q];
+    if (kg < kg1) {
+      if (sum_c0) v0[q] = *reinterpret_cast<const float2*>(sum_c0 + kg * 2);
+      if (sum_c1) v1[q] = *reinterpret_cast<const float2*>(sum_c1 + kg * 2);
+    }
+  }
+}
+
+// The dot product with fragments and sums already in registers.
+template <int KPW>
+__device__ __forceinline__ void tile_dot_regs(float* tot, const uint8_t* At, int stride, int G,
+                                              int kg0, int kg1, int g4, int c, const uint16_t* sS,
+                                              const uint16_t* sB, const uint4* b0, const uint4* b1,
+                                              const float2* v0, const float2* v1) {
+#pragma unroll
+  for (int q = 0; q < KPW; ++q) {
+    const int kg = kg0 + q;
+    if (kg >= kg1) break;
+    const uint2 ra = *reinterpret_cast<const uint2*>(At + g4 * stride + kg * 32 + 8 * c);
+    const uint2 rb = *reinterpret_cast<const uint2*>(At + (g4 + 8) * stride + kg * 32 + 8 * c);
+    float cc[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_group(cc, ra, rb, b0[q], b1[q]);
+    const float xs0 = v0[q].x, xp0 = v0[q].y, xs1 = v1[q].x, xp1 = v1[q].y;
+    const float s0 = bf2f(sS[g4 * G + kg]), s1 = bf2f(sS[(g4 + 8) * G + kg]);
+    const float q0 = bf2f(sB[g4 * G + kg]), q1 = bf2f(sB[(g4 + 8) * G + kg]);
+    tot[0] += s0 * (cc[0] - 1024.f * xp0) + q0 * xs0;
+    tot[1] += s0 * (cc[1] - 1024.f * xp1) + q0 * xs1;
+    tot[2] += s1 * (cc[2] - 1024.f * xp0) + q1 * xs0;
+    tot[3] += s1 * (cc[3] - 1024.f * xp1) + q1 * xs1;
+  }
+}
+
 template <int KPW>
 __device__ __forceinline__ void tile_dot_frags(float* tot, const uint8_t* At, int stride, int G,
                                                int kg0, int kg1, int g4, int c, const uint16_t* sS,
