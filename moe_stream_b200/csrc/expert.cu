@@ -55,15 +55,16 @@ __global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2) 
   if (threadIdx.x == 0 && slot >= 0) {
     mbar_init(bar, 1);
     fence_barrier_init();
+    const uint64_t pol = l2_evict_first();     // the weights stream through L2
     const unsigned bytes = 2u * 16u * row_bytes + 4u * UpSmem::sb_bytes(G);
     mbar_expect_tx(bar, bytes);
     for (int p = 0; p < 2; ++p) {
       const uint8_t* W = blob + A.geo.off[p][0] + (long long)rt * 16 * row_bytes;
-      for (int r = 0; r < 16; ++r) bulk_g2s(sA[p] + r * stride, W + r * row_bytes, row_bytes, bar);
-      bulk_g2s(sSB + (2 * p) * sbn, blob + A.geo.off[p][1] + (long long)rt * 16 * G * 2,
-               UpSmem::sb_bytes(G), bar);
-      bulk_g2s(sSB + (2 * p + 1) * sbn, blob + A.geo.off[p][2] + (long long)rt * 16 * G * 2,
-               UpSmem::sb_bytes(G), bar);
+      for (int r = 0; r < 16; ++r) bulk_g2s_hint(sA[p] + r * stride, W + r * row_bytes, row_bytes, bar, pol);
+      bulk_g2s_hint(sSB + (2 * p) * sbn, blob + A.geo.off[p][1] + (long long)rt * 16 * G * 2,
+                    UpSmem::sb_bytes(G), bar, pol);
+      bulk_g2s_hint(sSB + (2 * p + 1) * sbn, blob + A.geo.off[p][2] + (long long)rt * 16 * G * 2,
+                    UpSmem::sb_bytes(G), bar, pol);
     }
   }
   __syncthreads();
@@ -189,13 +190,14 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
   if (threadIdx.x == 0 && slot >= 0) {
     mbar_init(bar, 1);
     fence_barrier_init();
+    const uint64_t pol = l2_evict_first();     // the weights stream through L2
     mbar_expect_tx(bar, (unsigned)(RT * 16 * row_bytes + 2 * DownSmem::sb_bytes(G, RT)));
     const uint8_t* W = blob + A.geo.off[2][0] + (long long)blockIdx.x * RT * 16 * row_bytes;
-    for (int r = 0; r < RT * 16; ++r) bulk_g2s(sA + r * stride, W + r * row_bytes, row_bytes, bar);
-    bulk_g2s(sS, blob + A.geo.off[2][1] + (long long)blockIdx.x * RT * 16 * G * 2,
-             DownSmem::sb_bytes(G, RT), bar);
-    bulk_g2s(sB, blob + A.geo.off[2][2] + (long long)blockIdx.x * RT * 16 * G * 2,
-             DownSmem::sb_bytes(G, RT), bar);
+    for (int r = 0; r < RT * 16; ++r) bulk_g2s_hint(sA + r * stride, W + r * row_bytes, row_bytes, bar, pol);
+    bulk_g2s_hint(sS, blob + A.geo.off[2][1] + (long long)blockIdx.x * RT * 16 * G * 2,
+                  DownSmem::sb_bytes(G, RT), bar, pol);
+    bulk_g2s_hint(sB, blob + A.geo.off[2][2] + (long long)blockIdx.x * RT * 16 * G * 2,
+                  DownSmem::sb_bytes(G, RT), bar, pol);
   }
   pdl_wait();                                   // h and its sums come from k_up
   __syncthreads();

@@ -33,6 +33,25 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
       : "memory");
 }
 
+// L2 policy for data read once and not again soon (a decode step streams
+// ~1 GB of expert weights through a 126 MB L2): its lines go first, so the
+// router rows, the slot table and the kernels' code stay resident.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// bulk_g2s with an L2 cache policy (l2_evict_first).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, unsigned bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, "
+      "[%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned phase) {
   uint32_t ok;
   asm volatile(
