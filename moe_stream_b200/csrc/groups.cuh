@@ -9,6 +9,20 @@
 namespace ms {
 
 // Sorted list of the set bits of mask[0..nw) (nw <= 32*32), by one warp.
+// The same for a few mask words (an expert mask, nw <= 8): lane l handles
+// bit l of every word, so the list is a handful of independent steps
+// instead of a scan and a per-lane bit loop.
+__device__ __forceinline__ int warp_small_mask_to_list(const unsigned* mask, int nw, int* out, int lane) {
+  int total = 0;
+  for (int w = 0; w < nw; ++w) {
+    const unsigned m = mask[w];
+    if ((m >> lane) & 1u) out[total + __popc(m & ((1u << lane) - 1u))] = w * 32 + lane;
+    total += __popc(m);
+  }
+  __syncwarp();
+  return total;
+}
+
 __device__ __forceinline__ int warp_mask_to_list(const unsigned* mask, int nw, int* out, int lane) {
   int total = 0;
   for (int base = 0; base < nw; base += 32) {

@@ -249,10 +249,10 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
   __syncthreads();
 
   if (warp == 0) {
-    const int n_acq = warp_mask_to_list(s_acq_mask, (E + 31) / 32, s_acq, lane);
+    const int n_acq = warp_small_mask_to_list(s_acq_mask, (E + 31) / 32, s_acq, lane);
     if (lane == 0) s_n_acq = n_acq;
     for (int dd = 0; dd < A.n_pred; ++dd) {
-      const int n = warp_mask_to_list(s_pred_mask[dd], (E + 31) / 32, s_pred[dd], lane);
+      const int n = warp_small_mask_to_list(s_pred_mask[dd], (E + 31) / 32, s_pred[dd], lane);
       if (lane == 0) s_n_pred[dd] = n;
     }
     __syncwarp();
@@ -262,7 +262,23 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
       for (int i = lane; i < n_acq; i += 32) s_slots[i] = -1;
     }
     __syncwarp();
-    if (A.do_groups && small) {
+    if (A.do_groups && T == 1) {
+      // one token: its k experts are distinct, so group g is the g-th
+      // smallest of them with that one pair; g is the expert's rank in the
+      // acquired mask
+      if (lane < k) {
+        const int e = s_inds[lane];
+        int g = __popc(s_acq_mask[e >> 5] & ((1u << (e & 31)) - 1u));
+        for (int w = 0; w < (e >> 5); ++w) g += __popc(s_acq_mask[w]);
+        A.grp.grp_start[g] = g;
+        A.grp.grp_count[g] = 1;
+        A.grp.grp_key[g] = e;
+        A.grp.grp_slot[g] = s_slots[g];
+        A.grp.grp_pairs[g] = lane;
+        if (A.pair_slot) A.pair_slot[lane] = s_slots[g];
+      }
+      if (lane == 0) *A.grp.n_groups = k;
+    } else if (A.do_groups && small) {
       // pairs grouped by expert in one warp: everything is computed in
       // shared memory first and written out once at the end
       const int P = T * k;
