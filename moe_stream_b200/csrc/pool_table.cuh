@@ -169,8 +169,16 @@ __device__ __forceinline__ void kc_add(const DevTable& T, KeyCache* kc, Req& r, 
   r.n = n;
   r.base = kc->n;
   if (!may_repeat) {
-    for (int i = lane; i < n; i += 32) r.ci[i] = r.base + i;
+    const int base = r.base;
+    for (int i = lane; i < n; i += 32) {
+      r.ci[i] = base + i;
+      kc->key[base + i] = layer * T.n_experts + experts[i];
+    }
     r.n_uniq = n;
+    __syncwarp();
+    if (lane == 0) kc->n = base + n;
+    __syncwarp();
+    return;
   } else {
     // first occurrence of each expert (n is small on this path)
     for (int i = lane; i < n; i += 32) {
@@ -290,25 +298,41 @@ __device__ __forceinline__ void add_fill0(const DevTable& T, OpCtx* c, int slot,
 
 // prefetch (engine_v3.py:383-396) of request r in caller order; stops at the
 // first exhaustion and counts one bail.
+// The items are visited in order as in the reference, but 32 at a time: the
+// lanes test their items at once and the warp jumps to the next one that
+// needs a slot (usually none). An allocation may evict the key of a later
+// item (kc_alloc updates its cache entry), so the test is repeated after
+// each one, for the items after it only.
 __device__ __forceinline__ void warp_prefetch(const DevTable& T, OpCtx* c, KeyCache* kc, const Req& r,
                               int lane) {
-  for (int i = 0; i < r.n; ++i) {
-    const int ci = r.ci[i];
-    int skip = 0;
-    if (lane == 0) skip = kc->slot[ci] >= 0 || (kc->flags[ci] & KF_PENDING);
-    if (__shfl_sync(MS_FULL, skip, 0)) continue;
-    __syncwarp();                            // lane 0's writes before the collective scan
-    const int slot = kc_alloc(T, c, kc, ci, lane);
-    if (slot < 0) {
-      if (lane == 0) c->st[ST_BAIL] += 1;
+  for (int base = 0; base < r.n; base += 32) {
+    int next = base;                         // first item not visited yet
+    while (true) {
+      const int i = base + lane;
+      bool need = false;
+      if (i < r.n && i >= next) {
+        const int ci = r.ci[i];
+        need = kc->slot[ci] < 0 && !(kc->flags[ci] & KF_PENDING);
+      }
+      const unsigned m = __ballot_sync(MS_FULL, need);
+      if (!m) break;
+      const int i0 = base + __ffs(m) - 1;
+      const int ci = r.ci[i0];
+      __syncwarp();                          // lane 0's writes before the collective scan
+      const int slot = kc_alloc(T, c, kc, ci, lane);
+      if (slot < 0) {
+        if (lane == 0) c->st[ST_BAIL] += 1;
+        __syncwarp();
+        return;
+      }
+      if (lane == 0) {
+        c->st[ST_ISSUED] += 1;
+        setflags0(T, kc, ci, (uint8_t)(kc->flags[ci] | KF_PENDING));
+        T.pend_list[c->n_pend++] = kc->key[ci];
+        add_fill0(T, c, slot, kc->key[ci]);
+      }
       __syncwarp();
-      return;
-    }
-    if (lane == 0) {
-      c->st[ST_ISSUED] += 1;
-      setflags0(T, kc, ci, (uint8_t)(kc->flags[ci] | KF_PENDING));
-      T.pend_list[c->n_pend++] = kc->key[ci];
-      add_fill0(T, c, slot, kc->key[ci]);
+      next = i0 + 1;
     }
   }
   __syncwarp();
@@ -378,7 +402,7 @@ __device__ __forceinline__ bool warp_acquire_resident(const DevTable& T, OpCtx* 
   const long long uc0 = c->use_clock;
   const unsigned lt = (1u << lane) - 1u;
   int waits_before = 0;
-  long long n_pf = 0, n_cache = 0, n_reads = 0;
+  int n_pf = 0, n_cache = 0, n_reads = 0;         // per call: at most n each
   for (int base = 0; base < n; base += 32) {
     const int i = base + lane;
     const int ci = i < n ? r.ci[i] : 0;
