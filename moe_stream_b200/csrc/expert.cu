@@ -253,6 +253,9 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
     __syncthreads();
   }
 
+  // the next kernel in the stream (the next layer's route step) may launch
+  // while the arrivals and combines finish; it waits for this grid itself
+  pdl_trigger();
   // ---- arrival: the last CTA of a row tile combines all tokens' k parts
   __threadfence();
   __syncthreads();

@@ -149,6 +149,10 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
   const int gw = blockIdx.x * (RT_THREADS / 32) + warp;
   const int nchunk = d / 8;  // 16-byte chunks of a row
 
+  // a programmatic dependent of the previous kernel in the stream (the
+  // previous layer's k_down triggers once its dot products are done): wait
+  // for that grid before touching anything
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // ---------------------------------------------------------------- phase 1
   for (int r = gw; r < rows; r += nwarps_total) {
     const int which = r / E, e = r % E;
@@ -697,8 +701,16 @@ cudaError_t route_prefer_shared() {
 }
 
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s) {
-  k_route_step<<<grid, RT_THREADS, 0, s>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(RT_THREADS);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_route_step, a);
 }
 cudaError_t launch_route_wide(const RouteArgs& a, const WideArgs& w, cudaStream_t s) {
   const int rows = a.geo.n_experts * (1 + a.n_pred);
