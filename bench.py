@@ -627,7 +627,8 @@ def gpu_arm(args):
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "u4 weights x f16 MMA, f32 accumulate",
-            "data": "synthetic (seeded N(0,0.02) weights, MLX affine 4-bit g64; see DESIGN.md)",
+            "data": "synthetic (seeded N(0,0.02) weights, MLX affine 4-bit g64, Zipf(1.1) router "
+                    "bias, h_{l+1} = h_l + 0.1 N(0,1) hidden states)",
             "config": {"workload": WORKLOAD, "n_layers": N_LAYERS, "n_slots": N_SLOTS,
                        "n_experts_total": geom.n_keys, "top_k": geom.top_k, "batch": 1,
                        "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
