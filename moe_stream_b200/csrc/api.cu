@@ -467,6 +467,9 @@ static int join_side(ms_pool* p, cudaStream_t s) {
   } else if (!p->pf_captured) {
     CK(cudaEventSynchronize(p->ev_pf[p->pf_slot]));
   } else {
+    // a capture that ended without joining its fork cannot be waited for
+    // from here; report it once and forget the fork
+    p->pf_pending = false;
     return fail(MS_E_STATE,
                 "prefetch fills forked inside a stream capture were not joined into it "
                 "(call ms_pool_join on the capturing stream before ending the capture)");
