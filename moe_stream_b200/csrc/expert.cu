@@ -35,9 +35,12 @@ __global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2) 
   pdl_wait();                                   // slots and groups come from the route step
   pdl_trigger();
   const int g = blockIdx.y;
-  if (g >= *A.grp.n_groups) return;
+  // the group's metadata in one round trip with the group count (every g
+  // of the grid lies inside the group arrays; past n_groups it is unused)
+  const int n_groups = *A.grp.n_groups;
   const int slot = A.grp.grp_slot[g];
   const int m = A.grp.grp_count[g], start = A.grp.grp_start[g];
+  if (g >= n_groups) return;
   const int rt = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g4 = lane >> 2, c = lane & 3;
   const int K = A.geo.d_model, G = K / 64, F = A.geo.d_ff, GF = F / 64;
@@ -162,12 +165,12 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
   // filled slots can be read now; only h (k_up's output) needs pdl_wait
   const int g = blockIdx.y;
   const int n_groups = *A.grp.n_groups;
+  const int slot = A.grp.grp_slot[g];           // one round trip, as in k_up
+  const int m = A.grp.grp_count[g], start = A.grp.grp_start[g];
   if (g >= n_groups) {
     pdl_wait();
     return;
   }
-  const int slot = A.grp.grp_slot[g];
-  const int m = A.grp.grp_count[g], start = A.grp.grp_start[g];
   constexpr int WPT = EX_WARPS / RT;            // warps per row tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g4 = lane >> 2, c = lane & 3;
   const int sub = warp / WPT, wk = warp % WPT;
