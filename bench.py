@@ -51,6 +51,9 @@ def parse():
                          "gpt-oss layer on T=16384 tokens with its 128 experts sharded over "
                          "the ranks (run under torchrun), NCCL all-to-all dispatch/combine")
     ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=1,
+                    help="stack case: tokens per decode step (a multi-token verify batch); "
+                         "each token its own hidden-state sequence")
     ap.add_argument("--model", choices=["qwen3", "gptoss"], default="qwen3")
     ap.add_argument("--no-replicas", action="store_true",
                     help="ep: plain sharding, no replicas of hot experts")
@@ -510,7 +513,8 @@ def gpu_arm(args):
     dev = torch.device(f"cuda:{torch.cuda.current_device()}")
 
     geom = geometry.qwen3(N_LAYERS)
-    pool = ExpertPool(geom, N_SLOTS, evict="lfu", depths=(1,), pf_widen=1, max_tokens=1)
+    TB = args.batch
+    pool = ExpertPool(geom, N_SLOTS, evict="lfu", depths=(1,), pf_widen=1, max_tokens=TB)
     store = pool.alloc_store()
     st_t = torch.from_numpy(store).view(geom.n_keys, geom.blob_bytes)
     t_gen = time.perf_counter()
@@ -524,15 +528,17 @@ def gpu_arm(args):
     blocks = [MoEBlock(pool, l, w, b) for l, (w, b) in enumerate(routers)]
 
     W, K = args.warmup, args.steps
-    X_cpu = S.decode_inputs(W + 2 * K + 64, N_LAYERS, geom.d_model, SEED + rank)
-    X = X_cpu[:W + K].to(dev).unsqueeze(2)          # [steps, L, 1, d]
+    # [steps, L, TB, d]: token i of a step follows its own sequence
+    X_cpu = torch.stack([S.decode_inputs(W + 2 * K + 64, N_LAYERS, geom.d_model, SEED + rank + 1000 * i)
+                         for i in range(TB)], dim=2)
+    X = X_cpu[:W + K].to(dev)
 
     # one eager token before capture, then the graph
     for layer, b in enumerate(blocks):
         b(X[0, layer])
     torch.cuda.synchronize()
     pool.status()
-    g = DecodeGraph(blocks, T=1)
+    g = DecodeGraph(blocks, T=TB)
     for t in range(1, W):
         g.step(X[t])
     torch.cuda.synchronize()
@@ -564,7 +570,7 @@ def gpu_arm(args):
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms_max = float(tt.item())
-    tok_s = world * K / (ms_max / 1e3)
+    tok_s = world * K * TB / (ms_max / 1e3)
     d = {k: s1[k] - s0[k] for k in ("total", "prefetch", "cache", "miss")}
     hit = {"cache": d["cache"] / max(1, d["total"]),
            "resident_at_acquire": (d["cache"] + d["prefetch"]) / max(1, d["total"]),
@@ -575,11 +581,11 @@ def gpu_arm(args):
     from moe_stream_b200 import _lib
     import ctypes
     _lib.check(pool._lib.ms_pool_profile(pool._h, 1))
-    gp = DecodeGraph(blocks, T=1)
+    gp = DecodeGraph(blocks, T=TB)
     n_prof = 16
     acc = [[0.0, 0.0, 0.0] for _ in range(N_LAYERS)]
     buf = (ctypes.c_float * 3)()
-    Xp = X_cpu[W + K:W + K + n_prof].to(dev).unsqueeze(2)
+    Xp = X_cpu[W + K:W + K + n_prof].to(dev)
     for t in range(n_prof):
         gp.step(Xp[t])
         torch.cuda.synchronize()
@@ -590,13 +596,16 @@ def gpu_arm(args):
     _lib.check(pool._lib.ms_pool_profile(pool._h, 0))
     per_layer = [sum(acc[l][i] for l in range(N_LAYERS)) / (N_LAYERS * n_prof) for i in range(3)]
     expert_ms = per_layer[2]
-    bytes_per_layer = geom.top_k * geom.payload_bytes     # 8 distinct experts at T=1
+    # the distinct experts a layer reads: top_k at batch 1, the union of the
+    # tokens' picks otherwise (every acquired key of the timed steps)
+    distinct = d["total"] / (K * N_LAYERS)
+    bytes_per_layer = (geom.top_k if TB == 1 else distinct) * geom.payload_bytes
     peaks, peak_kind = measured_peaks()
     achieved = bytes_per_layer / (expert_ms * 1e-3) / 1e9
     del gp
 
     # ----------------------------------------------------------- e2e
-    Xh = X_cpu[W + K + n_prof:W + 2 * K + n_prof].unsqueeze(2).pin_memory()
+    Xh = X_cpu[W + K + n_prof:W + 2 * K + n_prof].pin_memory()
     Yh = torch.empty_like(Xh).pin_memory()
     barrier()
     torch.cuda.synchronize()
@@ -613,24 +622,25 @@ def gpu_arm(args):
         tt = torch.tensor([ems], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ems = float(tt.item())
-    e2e = {"value": world * K / (ems / 1e3), "unit": "tok/s",
+    e2e = {"value": world * K * TB / (ems / 1e3), "unit": "tok/s",
            "h2d_bytes_per_step": int(Xh[0].numel() * 2), "d2h_bytes_per_step": int(Yh[0].numel() * 2),
            "path": "DecodeGraph over MoEBlock.__call__ (ms_moe_block), pinned host x in / y out"}
     pool.status()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(geom, store, routers, X_cpu, args.cpu_sample_layers)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and TB == 1:
+        cpu = cpu_baseline(geom, store, routers, X_cpu[:, :, 0], args.cpu_sample_layers)
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world,
+            "metric": METRIC if TB == 1 else METRIC.replace("batch 1", f"batch {TB}"),
+            "value": tok_s, "unit": "tok/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "u4 weights x f16 MMA, f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, MLX affine 4-bit g64, Zipf(1.1) router "
                     "bias, h_{l+1} = h_l + 0.1 N(0,1) hidden states)",
             "config": {"workload": WORKLOAD, "n_layers": N_LAYERS, "n_slots": N_SLOTS,
-                       "n_experts_total": geom.n_keys, "top_k": geom.top_k, "batch": 1,
+                       "n_experts_total": geom.n_keys, "top_k": geom.top_k, "batch": TB,
                        "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
                        "l2": "inputs larger than L2: 1.02 GB of expert weights per step"},
             "hit_rate": hit,
@@ -641,10 +651,13 @@ def gpu_arm(args):
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
                          "peak_kind": peak_kind,
                          "kernel": "k_up + k_down (expert MLP of one layer)",
-                         "algorithmic_bytes_per_launch": bytes_per_layer},
+                         "algorithmic_bytes_per_launch": bytes_per_layer,
+                         "distinct_experts_per_layer": geom.top_k if TB == 1 else distinct},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": 4 * N_LAYERS * K,
+            # per layer: route step, demand fill, k_up, k_down, and the
+            # side-stream prefetch fill on every layer with a next layer
+            "gpu_launches": (4 * N_LAYERS + (N_LAYERS - 1)) * K,
             "clocks": clk,
             "setup_s": {"store_generation": t_gen},
         }
