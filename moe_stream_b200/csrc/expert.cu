@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2) 
     // the activations come in while the tile's weights are still in flight
     uint4 b0[KPW], b1[KPW];
     float2 v0[KPW], v1[KPW];
-    load_frags<KPW, 0>(b0, b1, (slot >= 0) ? fb : nullptr, kg0, kg1, c);
+    load_frags<KPW>(b0, b1, (slot >= 0) ? fb : nullptr, kg0, kg1, c);
     load_sums<KPW>(v0, v1, s0, s1, kg0, kg1);
     if (!waited) {
       if (slot >= 0) ok = mbar_wait(bar, 0, A.status);
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
     const int pb = (g4 < nn) ? pairs[g4] : -1;
     // h fragments requested before the sums' round trip, so the two overlap
     uint4 b0[KPW], b1[KPW];
-    load_frags<KPW, 0>(b0, b1, (pb >= 0 && slot >= 0) ? A.hfrag + (long long)pb * G * 64 : nullptr,
+    load_frags<KPW>(b0, b1, (pb >= 0 && slot >= 0) ? A.hfrag + (long long)pb * G * 64 : nullptr,
                        kg0, kg1, c);
     // per-group sums of h for this pass's columns: 4 row-tile partials each
     for (int i = threadIdx.x; i < nn * G; i += EX_THREADS) {

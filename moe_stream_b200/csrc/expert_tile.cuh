@@ -44,11 +44,10 @@ __host__ __device__ constexpr int padded_stride(int row_bytes) {
   return s;
 }
 
-// Activation fragments (frag layout) of quantisation groups [kg0, kg1) for
-// lane quad position c. SRC 0: read-only path (written before the launch);
-// 1: through L2 (written by other CTAs of the same launch); 2: generic
-// loads (a shared-memory copy, or global memory).
-template <int KPW, int SRC>
+// Activation fragments (frag layout, written before the launch, so read by
+// the read-only path) of quantisation groups [kg0, kg1) for lane quad
+// position c; zeros past kg1 or without activations.
+template <int KPW>
 __device__ __forceinline__ void load_frags(uint4* b0, uint4* b1, const __half* frag_b, int kg0,
                                            int kg1, int c) {
 #pragma unroll
@@ -58,25 +57,12 @@ __device__ __forceinline__ void load_frags(uint4* b0, uint4* b1, const __half* f
     const int kg = kg0 + q;
     if (frag_b && kg < kg1) {
       const uint4* fb = reinterpret_cast<const uint4*>(frag_b + kg * 64);
-      if (SRC == 0) {
-        b0[q] = __ldg(fb + c);
-        b1[q] = __ldg(fb + 4 + c);
-      } else if (SRC == 1) {
-        b0[q] = __ldcg(fb + c);
-        b1[q] = __ldcg(fb + 4 + c);
-      } else {
-        b0[q] = fb[c];
-        b1[q] = fb[4 + c];
-      }
+      b0[q] = __ldg(fb + c);
+      b1[q] = __ldg(fb + 4 + c);
     }
   }
 }
 
-// Dot products of a 16-row tile held in shared memory (rows at `stride`
-// bytes) over quantisation groups [kg0, kg1), for the 8 activation columns of
-// this pass, from activation fragments b0/b1 (load_frags). Scales/biases:
-// sS/sB [16][G] relative to the tile; per-group activation sums of the two
-// columns of this lane at sum_c0 / sum_c1.
 // Per-group activation sums (X, X') of the two columns of this lane for
 // groups [kg0, kg1), into registers (zeros where a column is absent).
 template <int KPW>
@@ -118,6 +104,9 @@ __device__ __forceinline__ void tile_dot_regs(float* tot, const uint8_t* At, int
   }
 }
 
+// tile_dot_regs with each group's sums read from sum_c0 / sum_c1 (shared
+// memory) as the loop reaches it: fewer live registers than load_sums up
+// front, the same arithmetic in the same order.
 template <int KPW>
 __device__ __forceinline__ void tile_dot_frags(float* tot, const uint8_t* At, int stride, int G,
                                                int kg0, int kg1, int g4, int c, const uint16_t* sS,
@@ -141,18 +130,6 @@ __device__ __forceinline__ void tile_dot_frags(float* tot, const uint8_t* At, in
     tot[2] += s1 * (cc[2] - 1024.f * xp0) + q1 * xs0;
     tot[3] += s1 * (cc[3] - 1024.f * xp1) + q1 * xs1;
   }
-}
-
-// tile_dot_frags with the fragments read from global memory (frag layout)
-// by the read-only path.
-template <int KPW>
-__device__ __forceinline__ void tile_dot_smem(float* tot, const uint8_t* At, int stride, int G,
-                                              int kg0, int kg1, int g4, int c, const uint16_t* sS,
-                                              const uint16_t* sB, const __half* frag_b,
-                                              const float* sum_c0, const float* sum_c1) {
-  uint4 b0[KPW], b1[KPW];
-  load_frags<KPW, 0>(b0, b1, frag_b, kg0, kg1, c);
-  tile_dot_frags<KPW>(tot, At, stride, G, kg0, kg1, g4, c, sS, sB, b0, b1, sum_c0, sum_c1);
 }
 
 struct UpSmem {
