@@ -36,8 +36,10 @@ __device__ __forceinline__ float warp_sum(float v) {
 // top-k of vals[0..E) (bf16 bit patterns, one warp): descending, exact ties
 // to the lower index. A candidate is the 32-bit key (value << 16 | ~index),
 // so one redux.sync per round finds the winner. Writes out[0..k).
-__device__ void warp_topk(const uint16_t* vals, int E, int k, int* out, int lane) {
-  constexpr int PER = MAX_E / 32;
+// PER candidates per lane (E <= 32 * PER); every winner search takes a max
+// over them, so the decode-sized E <= 128 uses PER = 4.
+template <int PER>
+__device__ void warp_topk_n(const uint16_t* vals, int E, int k, int* out, int lane) {
   uint32_t key[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
@@ -55,6 +57,11 @@ __device__ void warp_topk(const uint16_t* vals, int E, int k, int* out, int lane
     if (lane == 0) out[r] = 0xffff - (int)(w & 0xffffu);
   }
   __syncwarp();
+}
+
+__device__ void warp_topk(const uint16_t* vals, int E, int k, int* out, int lane) {
+  if (E <= 128) warp_topk_n<4>(vals, E, k, out, lane);
+  else warp_topk_n<MAX_E / 32>(vals, E, k, out, lane);
 }
 
 // Routes one token from its fp32 logits lg[0..E) (one warp; vals/sel are the
