@@ -293,6 +293,14 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
     ms_pool_destroy(p);
     return code;
   };
+  // a failing CUDA call releases what creation had set up so far
+#define CKB(call)                                                                  \
+  do {                                                                             \
+    cudaError_t e_ = (call);                                                       \
+    if (e_ != cudaSuccess)                                                         \
+      return bail(fail(MS_E_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                       __FILE__, __LINE__));                                       \
+  } while (0)
 
   // arena: n_slots blobs, slot s at s*blob (16 KiB aligned: cudaMalloc is 256 B
   // aligned and blob is a multiple of 16 KiB, so every component keeps its
@@ -324,20 +332,20 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   if ((rc = palloc(p, &t.ctr, 1))) return bail(rc);
   if ((rc = palloc(p, &p->pf_ring, 2 * (size_t)t.max_fills))) return bail(rc);
   if ((rc = palloc(p, &p->pf_cnt, 3))) return bail(rc);
-  CK(cudaMemset(p->pf_cnt, 0, 3 * sizeof(int)));
-  CK(cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking));
-  CK(cudaEventCreateWithFlags(&p->ev_fork, cudaEventDisableTiming));
-  for (auto& e : p->ev_pf) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-  CK(cudaMemset(t.key_of, 0xff, sizeof(int) * t.n_slots));
-  CK(cudaMemset(t.slot_of, 0xff, sizeof(int) * t.n_keys));
-  CK(cudaMemset(t.freq, 0, sizeof(int) * t.n_keys));
-  CK(cudaMemset(t.born, 0, sizeof(long long) * t.n_keys));
-  CK(cudaMemset(t.last_use, 0, sizeof(long long) * t.n_keys));
-  CK(cudaMemset(t.kflags, 0, t.n_keys));
-  CK(cudaMemset(t.pinned, 0, t.n_slots));
+  CKB(cudaMemset(p->pf_cnt, 0, 3 * sizeof(int)));
+  CKB(cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking));
+  CKB(cudaEventCreateWithFlags(&p->ev_fork, cudaEventDisableTiming));
+  for (auto& e : p->ev_pf) CKB(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  CKB(cudaMemset(t.key_of, 0xff, sizeof(int) * t.n_slots));
+  CKB(cudaMemset(t.slot_of, 0xff, sizeof(int) * t.n_keys));
+  CKB(cudaMemset(t.freq, 0, sizeof(int) * t.n_keys));
+  CKB(cudaMemset(t.born, 0, sizeof(long long) * t.n_keys));
+  CKB(cudaMemset(t.last_use, 0, sizeof(long long) * t.n_keys));
+  CKB(cudaMemset(t.kflags, 0, t.n_keys));
+  CKB(cudaMemset(t.pinned, 0, t.n_slots));
   TableCtr c0{};
   c0.n_free = t.n_slots;
-  CK(cudaMemcpy(t.ctr, &c0, sizeof(c0), cudaMemcpyHostToDevice));
+  CKB(cudaMemcpy(t.ctr, &c0, sizeof(c0), cudaMemcpyHostToDevice));
 
   // scratch: routing results for up to max_tokens; the decode-path
   // intermediates for up to narrow_tokens (MS_MLP_MAX_PAIRS pairs)
@@ -347,7 +355,7 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   const long long Tn = p->narrow_tokens, Pn = Tn * geom->top_k;
   if ((rc = palloc(p, &p->logits, Tn * E * (1 + cfg->n_depths)))) return bail(rc);
   if ((rc = palloc(p, &p->ticket, 1))) return bail(rc);
-  CK(cudaMemset(p->ticket, 0, sizeof(unsigned)));
+  CKB(cudaMemset(p->ticket, 0, sizeof(unsigned)));
   if ((rc = palloc(p, &p->inds, P))) return bail(rc);
   if ((rc = palloc(p, &p->scores, P))) return bail(rc);
   if ((rc = palloc(p, &p->scores_f, P))) return bail(rc);
@@ -358,7 +366,7 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   if ((rc = palloc(p, &p->hpart, Pn * (F / 16) * 2))) return bail(rc);
   if ((rc = palloc(p, &p->ypart, Pn * D))) return bail(rc);
   if ((rc = palloc(p, &p->cnt, D / 16))) return bail(rc);
-  CK(cudaMemset(p->cnt, 0, sizeof(unsigned) * (D / 16)));
+  CKB(cudaMemset(p->cnt, 0, sizeof(unsigned) * (D / 16)));
   const long long key_range = std::max<long long>(E, cfg->n_slots + 1);
   if ((rc = palloc(p, &p->mlp_keys, std::min<long long>(P, MS_MLP_MAX_PAIRS)))) return bail(rc);
   if ((rc = palloc(p, &p->grp.n_groups, 1))) return bail(rc);
@@ -368,7 +376,7 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   if ((rc = palloc(p, &p->grp.grp_count, std::max<long long>(P, E)))) return bail(rc);
   if ((rc = palloc(p, &p->grp.grp_pairs, P))) return bail(rc);
   if ((rc = palloc(p, &p->grp.map, key_range))) return bail(rc);
-  CK(cudaMemset(p->grp.n_groups, 0, sizeof(int)));
+  CKB(cudaMemset(p->grp.n_groups, 0, sizeof(int)));
   if ((rc = palloc(p, &p->ep_scratch, 128))) return bail(rc);
   if ((rc = palloc(p, &p->d_slots, MS_MAX_REQ))) return bail(rc);
   if ((rc = palloc(p, &p->d_opstatus, 1))) return bail(rc);
@@ -378,9 +386,10 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   (void)kp;
   // the fill and route kernels run beside the expert kernels (the fills on
   // the side stream): keep every SM on its largest shared-memory split
-  CK(route_prefer_shared());
+  CKB(route_prefer_shared());
   if ((rc = setup_wide(p))) return bail(rc);
-  CK(cudaDeviceSynchronize());
+  CKB(cudaDeviceSynchronize());
+#undef CKB
   *out = p;
   return MS_OK;
 }
