@@ -15,7 +15,12 @@ machine:
   round trip sit between a table decision and its fill;
 * the LFU table (freq / born / last_use / pending / from_prefetch / pinned,
   clocks and counters) lives in device memory and is updated by one warp per
-  call, in exactly the reference's order.
+  call, in exactly the reference's order;
+* the prefetch fills of a block call run on a stream of the pool and are
+  joined into the caller's stream by the next call that reads the arena. A
+  caller that reads ``views`` itself right after block calls makes its
+  stream wait for them first (``join(stream)``, or a device-wide
+  synchronisation), as the reference's readers wait on ``pending`` reads.
 
 Everything here is a thin ctypes wrapper over libmoestream.so; there is no
 Python or CPU implementation of any of it.
