@@ -65,3 +65,21 @@ def test_errors_are_status_codes_not_exceptions(lib):
     rc = lib.ms_pool_create(ctypes.byref(g), ctypes.byref(cfg), 0, ctypes.byref(h))
     assert rc == _lib.MS_E_INVALID and "4-bit" in _lib.last_error()
     assert lib.ms_pool_destroy(None) == _lib.MS_OK
+
+
+def test_every_entry_point_rejects_a_null_handle(lib):
+    """Each exported call given a NULL pool (and NULL pointers) returns
+    MS_E_INVALID with a message, on a machine without a GPU."""
+    from moe_stream_b200 import _lib
+    ints = (ctypes.c_int, ctypes.c_int32, ctypes.c_long, ctypes.c_longlong, ctypes.c_size_t)
+    skip = {"ms_last_error", "ms_pool_create", "ms_pool_destroy"}
+    checked = 0
+    for name, argtypes in _lib.EXPORTS.items():
+        if name in skip:
+            continue
+        args = [0 if a in ints else None for a in argtypes]
+        rc = getattr(lib, name)(*args)
+        assert rc == _lib.MS_E_INVALID, (name, rc)
+        assert "NULL" in _lib.last_error(), (name, _lib.last_error())
+        checked += 1
+    assert checked >= 20
