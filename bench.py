@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark: moe-stream's MoE expert block on B200 (BASELINE metric
+"""Benchmark: moe-stream's MoE expert block on B200 (metric: MoE-block
 "MoE-block tok/s and expert-weight HBM GB/s vs peak").
 
 Default workload (N=1, the configuration the metric is quoted on): config 1,
@@ -94,7 +94,7 @@ def layer_case(args):
 
 
 def prefill_case(args):
-    """One MoE layer of BASELINE config 2 / 3 / 4 on one GPU: T tokens routed
+    """One MoE layer on a large batch on one GPU (Qwen3 T=4096, gpt-oss T=512 or 16384): T tokens routed
     over 128 resident experts (the pool holds the whole layer), grouped
     tcgen05 GEMMs. A step is one block call on T tokens."""
     import ctypes
@@ -194,7 +194,7 @@ def prefill_case(args):
 
 
 def ep_case(args):
-    """one gpt-oss layer on T tokens (default 16384), the
+    """Expert parallelism: one gpt-oss layer on T tokens (default 16384), the
     tokens split evenly over the ranks and the 128 experts sharded 128/G per
     GPU; a step is one expert-parallel block (route, pack, all-to-all out,
     local grouped GEMMs, all-to-all back, combine) on every rank. Timed on the

@@ -196,6 +196,11 @@ int ms_pool_join(ms_pool* pool, void* stream);
 int ms_expert_mlp(ms_pool* pool, const int32_t* slots, const float* scores,
                   const void* x, int T, int k, void* y, void* stream);
 
+/* Diagnostic with no reference counterpart: the SASS target the library's
+ * kernels carry for `device` (cudaFuncAttributes.binaryVersion of one of
+ * them; 100 for sm_100a). */
+int ms_kernel_arch(int device, int* binary_version);
+
 /* Device-side routing/slot buffers of the most recent ms_moe_block call
  * (valid until the next call): inds int32 [T,k], scores bf16 [T,k],
  * slots int32 [T,k]. For parity dumps. */
@@ -211,7 +216,7 @@ int ms_block_debug(ms_pool* pool, const int32_t** inds, const void** scores,
 int ms_pool_profile(ms_pool* pool, int enable);
 int ms_pool_timing(ms_pool* pool, int layer, float* out3);
 
-/* Expert parallelism, no counterpart in the reference,
+/* Expert parallelism (the gpt-oss layer on a 16384-token batch), no counterpart in the reference,
  * which runs on one device; the block it distributes is engine_120b.py:78-149.
  * Each rank holds its experts (and replicas) resident in its pool. The host
  * moves the buffers between ranks
@@ -252,8 +257,11 @@ int ms_ep_combine(ms_pool* pool, const void* back, const int32_t* pair_pos, int 
  * a fixed ~2 MB __device__ array inside the library, which every GPU that
  * loads the library keeps until the process exits.
  * Limits: T <= MS_STATIC_MAX_TOKENS, T*k <= MS_STATIC_MAX_PAIRS, d_model and
- * d_ff <= 4096, n_slots <= MS_STATIC_MAX_SLOTS; larger sizes return
- * MS_E_INVALID. The first call on each device looks up the array's device
+ * d_ff <= 4096 (<= 3072 for gpt-oss), n_slots <= MS_STATIC_MAX_SLOTS; larger
+ * sizes, and geometries whose components do not fit in blob_bytes, return
+ * MS_E_INVALID before anything is enqueued. A slot index outside
+ * [0, n_slots) gives zero rows for its token and is reported by
+ * ms_expert_mlp_static_status. The first call on each device looks up the array's device
  * address (cudaGetSymbolAddress); make that first call before any stream
  * capture. All calls share the array: calls that may overlap on the GPU
  * (other streams or host threads) race, so the caller must order them.
@@ -264,6 +272,13 @@ int ms_ep_combine(ms_pool* pool, const void* back, const int32_t* pair_pos, int 
 int ms_expert_mlp_static(const ms_geom* geom, const void* arena, int n_slots,
                          const int32_t* slots, const float* scores, const void* x,
                          int T, int k, void* y, void* stream);
+
+/* Device-side status of the most recent ms_expert_mlp_static call on the
+ * current device, which returns before its kernels run: MS_E_INVALID when a
+ * slot index was out of range, MS_E_TIMEOUT when a bounded wait for the
+ * weight copies ran out, else MS_OK. Waits for `stream`, then clears the
+ * status. Allocates nothing either. */
+int ms_expert_mlp_static_status(void* stream);
 
 #ifdef __cplusplus
 }

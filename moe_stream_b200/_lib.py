@@ -77,6 +77,8 @@ EXPORTS = {
     "ms_expert_mlp_static": [ctypes.POINTER(MsGeom), ctypes.c_void_p, ctypes.c_int,
                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                              ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p],
+    "ms_expert_mlp_static_status": [ctypes.c_void_p],
+    "ms_kernel_arch": [ctypes.c_int, ctypes.POINTER(ctypes.c_int)],
     "ms_block_debug": [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p),
                        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)],
     "ms_ep_pack": [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,

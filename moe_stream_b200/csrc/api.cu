@@ -50,6 +50,50 @@ int dalloc(T** p, size_t count) {
 
 namespace ms {
 void set_error_message(const char* msg) { g_err = msg; }
+
+static int __attribute__((format(printf, 3, 4))) geom_bad(char* msg, size_t n, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(msg, n, fmt, ap);
+  va_end(ap);
+  return MS_E_INVALID;
+}
+
+int validate_geom(const ms_geom* g, char* msg, size_t n) {
+#define bad(...) geom_bad(msg, n, __VA_ARGS__)
+  if (!g) return bad("geom is NULL");
+  if (g->model != MS_MODEL_QWEN3 && g->model != MS_MODEL_GPTOSS) return bad("unknown model %d", g->model);
+  if (g->bits != 4 || g->group_size != 64)
+    return bad("only 4-bit codes in groups of 64 are supported (got %d bits, group %d)", g->bits,
+               g->group_size);
+  if (g->d_model <= 0 || g->d_model % 64 || g->d_ff <= 0 || g->d_ff % 64)
+    return bad("d_model and d_ff must be positive multiples of 64");
+  if (g->d_ff > 4096 || g->d_model > 16384) return bad("d_ff must be <= 4096 and d_model <= 16384");
+  if (g->n_experts <= 0 || g->n_experts > 256) return bad("n_experts must be in [1, 256]");
+  if (g->top_k <= 0 || g->top_k > 32 || g->top_k > g->n_experts)
+    return bad("top_k must be in [1, min(32, n_experts)]");
+  if (g->n_layers <= 0) return bad("n_layers must be positive");
+  if (g->blob_bytes <= 0 || g->blob_bytes % 16384) return bad("blob_bytes must be a positive multiple of 16384");
+  if (g->proj_bias != 0 && g->proj_bias != 1) return bad("proj_bias must be 0 or 1");
+  // every component the kernels read lies inside the blob: its offset plus
+  // the size the shapes give it (weight U32 [out, in/8], scales and biases
+  // BF16 [out, in/64], the projection bias BF16 [out] when proj_bias is set)
+  for (int pr = 0; pr < 3; ++pr) {
+    const int n_out = pr == 2 ? g->d_model : g->d_ff;
+    const int n_in = pr == 2 ? g->d_ff : g->d_model;
+    const long long sz[4] = {(long long)n_out * n_in / 2, (long long)n_out * (n_in / 64) * 2,
+                             (long long)n_out * (n_in / 64) * 2, (long long)n_out * 2};
+    for (int pt = 0; pt < 4; ++pt) {
+      const long long off = g->comp_offset[pr][pt];
+      if (pt == 3 && !g->proj_bias) continue;
+      if (off < 0 || off + sz[pt] > g->blob_bytes)
+        return bad("component [%d][%d] at %lld (+%lld) lies outside the blob", pr, pt, off, sz[pt]);
+      if (off % 16) return bad("component [%d][%d] is not 16-byte aligned", pr, pt);
+    }
+  }
+#undef bad
+  return MS_OK;
+}
 }  // namespace ms
 
 struct ms_pool {
@@ -134,38 +178,9 @@ int palloc(ms_pool* p, T** out, size_t count) {
 }
 
 int check_geom(const ms_geom* g) {
-  if (!g) return fail(MS_E_INVALID, "geom is NULL");
-  if (g->model != MS_MODEL_QWEN3 && g->model != MS_MODEL_GPTOSS)
-    return fail(MS_E_INVALID, "unknown model %d", g->model);
-  if (g->bits != 4 || g->group_size != 64)
-    return fail(MS_E_INVALID, "only 4-bit codes in groups of 64 are supported (got %d bits, group %d)",
-                g->bits, g->group_size);
-  if (g->d_model <= 0 || g->d_model % 64 || g->d_ff <= 0 || g->d_ff % 64)
-    return fail(MS_E_INVALID, "d_model and d_ff must be positive multiples of 64");
-  if (g->d_ff > 4096 || g->d_model > 16384)
-    return fail(MS_E_INVALID, "d_ff must be <= 4096 and d_model <= 16384");
-  if (g->n_experts <= 0 || g->n_experts > 256)
-    return fail(MS_E_INVALID, "n_experts must be in [1, 256]");
-  if (g->top_k <= 0 || g->top_k > 32 || g->top_k > g->n_experts)
-    return fail(MS_E_INVALID, "top_k must be in [1, min(32, n_experts)]");
-  if (g->n_layers <= 0) return fail(MS_E_INVALID, "n_layers must be positive");
-  if (g->blob_bytes <= 0 || g->blob_bytes % 16384)
-    return fail(MS_E_INVALID, "blob_bytes must be a positive multiple of 16384");
-  for (int pr = 0; pr < 3; ++pr) {
-    const int n_out = pr == 2 ? g->d_model : g->d_ff;
-    const int n_in = pr == 2 ? g->d_ff : g->d_model;
-    const long long sz[4] = {(long long)n_out * n_in / 2, (long long)n_out * (n_in / 64) * 2,
-                             (long long)n_out * (n_in / 64) * 2, (long long)n_out * 2};
-    for (int pt = 0; pt < 4; ++pt) {
-      const long long off = g->comp_offset[pr][pt];
-      if (pt == 3 && !g->proj_bias) continue;
-      if (off < 0 || off + sz[pt] > g->blob_bytes)
-        return fail(MS_E_INVALID, "component [%d][%d] at %lld (+%lld) lies outside the blob",
-                    pr, pt, off, sz[pt]);
-      if (off % 16) return fail(MS_E_INVALID, "component [%d][%d] is not 16-byte aligned", pr, pt);
-    }
-  }
-  return MS_OK;
+  char msg[256];
+  const int rc = ms::validate_geom(g, msg, sizeof(msg));
+  return rc ? fail(rc, "%s", msg) : MS_OK;
 }
 
 Geo make_geo(const ms_geom& g) {
@@ -983,6 +998,18 @@ int ms_pool_timing(ms_pool* p, int layer, float* out3) {
   cudaEvent_t* ev = &p->prof_ev[(size_t)layer * 4];
   CK(cudaEventSynchronize(ev[3]));
   for (int i = 0; i < 3; ++i) CK(cudaEventElapsedTime(&out3[i], ev[i], ev[i + 1]));
+  return MS_OK;
+}
+
+int ms_kernel_arch(int device, int* binary_version) {
+  if (!binary_version) return fail(MS_E_INVALID, "binary_version is NULL");
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(MS_E_INVALID, "device %d out of range", device);
+  CK(cudaSetDevice(device));
+  cudaFuncAttributes attr{};
+  CK(route_step_attributes(&attr));
+  *binary_version = attr.binaryVersion;
   return MS_OK;
 }
 

@@ -306,8 +306,17 @@ static cudaError_t launch_pdl(Kern kern, dim3 grid, int smem, cudaStream_t s, co
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
+bool expert_shape_ok(int model, int d_model, int d_ff) {
+  if (d_model <= 0 || d_ff <= 0 || d_model % 64 || d_ff % 64) return false;
+  // gpt-oss: 6 quantisation groups per warp, at most 48 groups each way;
+  // Qwen3 and other shapes: at most 64 groups each way
+  const int G = d_model / 64, GF = d_ff / 64;
+  return model == 1 ? (G <= 48 && GF <= 48) : (G <= 64 && GF <= 64);
+}
+
 cudaError_t launch_expert(const ExpArgs& a, int max_groups, cudaStream_t s) {
   if (max_groups <= 0) return cudaSuccess;
+  if (!expert_shape_ok(a.geo.model, a.geo.d_model, a.geo.d_ff)) return cudaErrorInvalidValue;
   const int K = a.geo.d_model, F = a.geo.d_ff, G = K / 64, GF = F / 64;
   dim3 gu(F / 16, max_groups);
   cudaError_t e;

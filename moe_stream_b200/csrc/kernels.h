@@ -11,7 +11,18 @@
 #define MS_MAX_REQ 256
 #define MS_MLP_MAX_PAIRS 2048
 
+struct ms_geom;   // include/moestream.h
+
 namespace ms {
+
+// Checks a geometry for every entry point that takes one: model and
+// quantisation, shapes, and every component the kernels read inside the
+// blob (offset + size <= blob_bytes) and 16-byte aligned. Returns MS_OK or
+// MS_E_INVALID with the reason written to msg.
+int validate_geom(const ::ms_geom* g, char* msg, size_t n);
+
+// True when the decode expert kernels (launch_expert) handle this shape.
+bool expert_shape_ok(int model, int d_model, int d_ff);
 
 struct RouteArgs {
   Geo geo;
@@ -176,6 +187,8 @@ struct EpPackArgs {
 cudaError_t launch_mlp_wide_prep(const MlpWideArgs& a, int sms, cudaStream_t s);
 cudaError_t launch_ep_pack(const EpPackArgs& a, int sms, cudaStream_t s);
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s);
+// Attributes of the route-step kernel (its binaryVersion is the SASS target).
+cudaError_t route_step_attributes(cudaFuncAttributes* attr);
 cudaError_t route_prefer_shared();
 cudaError_t launch_route_wide(const RouteArgs& a, const WideArgs& w, cudaStream_t s);
 cudaError_t launch_scatter(const ScatterArgs& a, int grid, cudaStream_t s);

@@ -12,7 +12,7 @@
 // one file-scope __device__ array of fixed size, loaded with the library.
 //
 // Limits: T <= MS_STATIC_MAX_TOKENS tokens, T*k <= MS_STATIC_MAX_PAIRS,
-// d_model and d_ff <= 4096, n_slots <= MS_STATIC_MAX_SLOTS. Every GPU that
+// d_model and d_ff <= 4096 (3072 for gpt-oss), n_slots <= MS_STATIC_MAX_SLOTS. Every GPU that
 // loads the library keeps the array (about 2 MB) until the process exits.
 // All calls on a device share it, so two calls that can run at the same time
 // on the GPU (different streams, different host threads) race and corrupt
@@ -100,28 +100,28 @@ extern "C" int ms_expert_mlp_static(const ms_geom* geom, const void* arena, int 
   if (!geom || !arena || !slots || !scores || !x || !y)
     return sfail(MS_E_INVALID, "ms_expert_mlp_static: NULL argument");
   const ms_geom& g = *geom;
-  if (g.model != MS_MODEL_QWEN3 && g.model != MS_MODEL_GPTOSS)
-    return sfail(MS_E_INVALID, "ms_expert_mlp_static: unknown model");
-  if (g.bits != 4 || g.group_size != 64)
-    return sfail(MS_E_INVALID, "ms_expert_mlp_static: only 4-bit codes in groups of 64");
-  if (g.d_model <= 0 || g.d_model % 64 || g.d_model > MAX_D || g.d_ff <= 0 || g.d_ff % 64 ||
-      g.d_ff > MAX_D)
+  {
+    // the pool path's geometry checks: every component the kernels read
+    // (offset plus the size its shape gives) inside the blob
+    char msg[256], full[320];
+    if (validate_geom(geom, msg, sizeof(msg)) != MS_OK) {
+      snprintf(full, sizeof(full), "ms_expert_mlp_static: %s", msg);
+      return sfail(MS_E_INVALID, full);
+    }
+  }
+  if (g.d_model > MAX_D || g.d_ff > MAX_D)
+    return sfail(MS_E_INVALID, "ms_expert_mlp_static: d_model and d_ff must be <= 4096");
+  if (!expert_shape_ok(g.model, g.d_model, g.d_ff))
     return sfail(MS_E_INVALID,
-                 "ms_expert_mlp_static: d_model and d_ff must be multiples of 64 and <= 4096");
-  if (g.top_k <= 0 || k != g.top_k) return sfail(MS_E_INVALID, "ms_expert_mlp_static: k must equal top_k");
+                 "ms_expert_mlp_static: shape not handled by the decode kernels (gpt-oss: d_model "
+                 "and d_ff <= 3072)");
+  if (k != g.top_k) return sfail(MS_E_INVALID, "ms_expert_mlp_static: k must equal top_k");
   if (T <= 0 || T > MAX_T)
     return sfail(MS_E_INVALID, "ms_expert_mlp_static: T must be in [1, MS_STATIC_MAX_TOKENS]");
   if ((long long)T * k > MAX_P)
     return sfail(MS_E_INVALID, "ms_expert_mlp_static: T*k exceeds MS_STATIC_MAX_PAIRS");
   if (n_slots <= 0 || n_slots > MAX_SLOTS)
     return sfail(MS_E_INVALID, "ms_expert_mlp_static: n_slots must be in [1, MS_STATIC_MAX_SLOTS]");
-  if (g.blob_bytes <= 0 || g.blob_bytes % 16384)
-    return sfail(MS_E_INVALID, "ms_expert_mlp_static: blob_bytes must be a multiple of 16384");
-  for (int pr = 0; pr < 3; ++pr)
-    for (int pt = 0; pt < 3 + (g.proj_bias ? 1 : 0); ++pt)
-      if (g.comp_offset[pr][pt] < 0 || g.comp_offset[pr][pt] % 16 ||
-          g.comp_offset[pr][pt] >= g.blob_bytes)
-        return sfail(MS_E_INVALID, "ms_expert_mlp_static: bad component offset");
   if (!aligned16(x) || !aligned16(y) || !aligned16(arena))
     return sfail(MS_E_INVALID, "ms_expert_mlp_static: x, y and arena must be 16-byte aligned");
 
@@ -187,5 +187,31 @@ extern "C" int ms_expert_mlp_static(const ms_geom* geom, const void* arena, int 
   e.status = &ctr->status;
   if (launch_expert(e, std::min(T * k, n_slots), s) != cudaSuccess)
     return sfail(MS_E_CUDA, "ms_expert_mlp_static: expert kernel launch failed");
+  return MS_OK;
+}
+
+// Device status of the most recent ms_expert_mlp_static call on the current
+// device: an out-of-range slot (its rows come back as zeros) or a bounded
+// wait that ran out is recorded in the status word of the static array; this
+// reads it after `stream` has finished and clears it. Allocates nothing.
+extern "C" int ms_expert_mlp_static_status(void* stream) {
+  unsigned char* base = nullptr;
+  int rc = scratch_ptr(&base);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = 0;
+  TableCtr* ctr = reinterpret_cast<TableCtr*>(base + OFF_CTR);
+  if (cudaMemcpyAsync(&st, &ctr->status, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return sfail(MS_E_CUDA, "ms_expert_mlp_static_status: reading the status failed");
+  if (cudaMemsetAsync(&ctr->status, 0, sizeof(int), s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return sfail(MS_E_CUDA, "ms_expert_mlp_static_status: clearing the status failed");
+  if (st == MS_E_INVALID)
+    return sfail(MS_E_INVALID, "ms_expert_mlp_static: a slot index was outside [0, n_slots); "
+                               "its rows were returned as zeros");
+  if (st == MS_E_TIMEOUT)
+    return sfail(MS_E_TIMEOUT, "ms_expert_mlp_static: a bounded wait for the weight copies ran out");
+  if (st) return sfail(st, "ms_expert_mlp_static: device-side error");
   return MS_OK;
 }

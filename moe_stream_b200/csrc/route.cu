@@ -707,6 +707,10 @@ cudaError_t route_prefer_shared() {
   return cudaSuccess;
 }
 
+cudaError_t route_step_attributes(cudaFuncAttributes* attr) {
+  return cudaFuncGetAttributes(attr, k_route_step);
+}
+
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);

@@ -1,4 +1,4 @@
-"""Expert parallelism for wide batches: the 128 experts
+"""Expert parallelism for wide batches (the gpt-oss layer on 16384 tokens): the 128 experts
 of a layer are sharded over the ranks of one node, expert e living on rank
 e // e_local in slot e % e_local of that rank's pool, every rank holding its
 experts resident. The reference runs on one device (its MoE block is

@@ -1,6 +1,6 @@
 """GPU parity tests of the MoE block through the C ABI against the oracle.
 
-Tolerances: routing index sets bit-exact except at
+Tolerances (the parity bar of this path): routing index sets bit-exact except at
 exact bf16 ties; outputs within max-abs 2e-2 and mean-rel 1e-2 of the
 oracle's MLX-path restatement; and, as test_kernel.py:95-101 requires of the
 reference's own kernel, error against the fp32 dequantised reference no

@@ -2,7 +2,7 @@
 tiled router, the expert-order scatter, the two tcgen05 grouped GEMMs and
 the combine, against the oracle.
 
-Same bar as the decode tests: routing index sets
+Same bar as the decode tests (the parity bar of this path): routing index sets
 bit-exact except at exact bf16 ties (or one ulp, for fp32 accumulation
 order); outputs within max-abs 2e-2 and mean-rel 1e-2 of the oracle's
 MLX-path restatement; error against the fp32 dequantised reference no worse
