@@ -1,20 +1,28 @@
 #!/usr/bin/env python3
-"""Benchmark: moe-stream's MoE expert block on B200 (metric: MoE-block
-"MoE-block tok/s and expert-weight HBM GB/s vs peak").
+"""Benchmark: moe-stream's MoE expert block on B200 -- MoE-block tok/s and
+expert-weight HBM GB/s against the measured peak, at 1/2/4/8 GPUs.
 
-Default workload (N=1, the configuration the metric is quoted on): config 1,
-a Qwen3-30B-A3B-shape 48-layer expert stack at batch-1 decode -- 6144 experts
-in a pinned host store, a 3072-slot HBM pool with LFU eviction and
-next-layer router prefetch, Zipf(1.1)-skewed routers. One step = one decoded
-token = 48 MoE block calls (router, device slot-table step, fills, expert
-kernels), replayed from a CUDA graph with every input already in HBM.
+Default workload (N=1): a Qwen3-30B-A3B-shape 48-layer expert stack at
+batch-1 decode -- 6144 experts in a pinned host store, a 3072-slot HBM pool
+with LFU eviction and next-layer router prefetch, Zipf(1.1)-skewed routers.
+One step = one decoded token = 48 MoE block calls (router, device slot-table
+step, fills, expert kernels), replayed from a CUDA graph with every input
+already in HBM. Before the timed steps the pool is brought to its steady
+state (untimed tokens until the trailing cache-hit rate reaches 0.97). The
+e2e figure replays the same tokens from a checkpoint of the same pool state,
+with each token's inputs copied in from pinned host memory and its outputs
+copied back.
+
+Every run also measures the sharded configuration -- one gpt-oss layer on
+16384 tokens with its 128 experts spread over the N GPUs, NCCL all-to-all
+dispatch and combine -- and reports it under "expert_parallel".
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Under torchrun (N > 1) every rank runs its own replica (decode does not
-shard); value is the sum over replicas of tokens / the slowest rank's time.
-``--impl reference`` times the CPU restatement of the same path (the
-reference's MLX implementation is not installable here) on a bounded sample.
+Under torchrun (N > 1) every rank runs its own decode replica (decode does
+not shard); value is the sum over replicas of tokens / the slowest rank's
+time. ``--impl reference`` times the CPU port of the same decode path on the
+host cores (the reference's MLX implementation is not installable here).
 """
 import argparse
 import json
@@ -40,23 +48,29 @@ def parse():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=32)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-sample-layers", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="host time spent on the CPU baseline sample")
+    ap.add_argument("--hit-target", type=float, default=0.97,
+                    help="trailing cache-hit rate that ends the untimed pre-roll")
+    ap.add_argument("--preroll-max", type=int, default=1024,
+                    help="most untimed pre-roll tokens")
+    ap.add_argument("--no-ep", action="store_true",
+                    help="skip the expert-parallel measurement of the default run")
     ap.add_argument("--case", choices=["stack", "layer", "prefill", "ep"], default="stack",
                     help="layer: a 2-layer Qwen3 stack with every expert resident (a small "
                          "case for ncu section captures); prints per-call timings only. "
-                         "prefill: one MoE layer on a large token batch (config 2: qwen3, "
-                         "T=4096; config 3: gptoss, T=512; config 4 on one GPU: gptoss, "
-                         "T=16384), the grouped tcgen05 GEMM path. ep: config 4, the "
-                         "gpt-oss layer on T=16384 tokens with its 128 experts sharded over "
-                         "the ranks (run under torchrun), NCCL all-to-all dispatch/combine")
+                         "prefill: one MoE layer on a large token batch (qwen3 T=4096, "
+                         "gptoss T=512 or 16384), the grouped tcgen05 GEMM path. ep: only "
+                         "the expert-parallel measurement (gpt-oss layer, T=16384, experts "
+                         "sharded over the ranks under torchrun)")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--batch", type=int, default=1,
                     help="stack case: tokens per decode step (a multi-token verify batch); "
                          "each token its own hidden-state sequence")
     ap.add_argument("--model", choices=["qwen3", "gptoss"], default="qwen3")
     ap.add_argument("--no-replicas", action="store_true",
-                    help="ep: plain sharding, no replicas of hot experts")
+                    help="expert parallelism: plain sharding, no replicas of hot experts")
     return ap.parse_args()
 
 
@@ -193,146 +207,6 @@ def prefill_case(args):
     pool.close()
 
 
-def ep_case(args):
-    """Expert parallelism: one gpt-oss layer on T tokens (default 16384), the
-    tokens split evenly over the ranks and the 128 experts sharded 128/G per
-    GPU; a step is one expert-parallel block (route, pack, all-to-all out,
-    local grouped GEMMs, all-to-all back, combine) on every rank. Timed on the
-    device, max over ranks."""
-    import datetime
-    import torch
-    import torch.distributed as dist
-    from moe_stream_b200 import geometry, store as S
-    from moe_stream_b200.block import MoEBlock
-    from moe_stream_b200.ep import (DeviceOps, ep_forward, load_local_experts, plan_placement,
-                                    routed_counts)
-    from moe_stream_b200.pool import ExpertPool
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ.setdefault("MASTER_PORT", "29541")
-    torch.cuda.set_device(local)
-    dev = torch.device(f"cuda:{local}")
-    dist.init_process_group("nccl", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=300), device_id=dev)
-    geom = geometry.gptoss(1)
-    T = args.tokens or 16384
-    if T % world or geom.n_experts % world:
-        raise SystemExit(f"T={T} and {geom.n_experts} experts must split over {world} ranks")
-    Tr = T // world
-    base = geom.n_experts // world
-    spare = 0 if (world == 1 or args.no_replicas) else base // 2
-    pool = ExpertPool(geom, base + spare, depths=(), max_tokens=T)
-    st = torch.from_numpy(pool.alloc_store()).view(geom.n_keys, geom.blob_bytes)
-    st.copy_(S.make_layer_blobs(geom, SEED, 0, device=dev).cpu())
-    w, b = S.router_weights(geom, SEED, 0, zipf_s=1.1)
-    block = MoEBlock(pool, 0, w, b)
-    xs = [S.rms_norm_tokens(T, geom.d_model, seed=SEED + 200 + i)[rank * Tr:(rank + 1) * Tr]
-          .to(dev) for i in range(3)]
-    # placement from a calibration batch (not a timed one): hot experts
-    # replicated into the spare slots, replicas balanced over the ranks
-    counts = routed_counts(DeviceOps(block, world), xs[2])
-    table, slots = plan_placement(counts, world, base + spare)
-    load_local_experts(pool, 0, rank, world, slots[rank])
-    ops = DeviceOps(block, world, placement=table)
-    rank_load = [float(sum(counts[e] / table[e, 0] for e in r)) for r in slots]
-    xs = xs[:2]
-    W, K = max(3, args.warmup), args.steps
-    for i in range(W):
-        ep_forward(xs[i % 2], ops, world)
-    torch.cuda.synchronize()
-    pool.status()
-    clocks = ClockSampler(local)
-    clocks.start()
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(K):
-        ep_forward(xs[i % 2], ops, world)
-    e1.record()
-    torch.cuda.synchronize()
-    dist.barrier()
-    clk = clocks.stop()
-    pool.status()
-    ms = torch.tensor([e0.elapsed_time(e1) / K], device=dev)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
-    # e2e: pinned host tokens in, pinned host result out, every step
-    xh = xs[0].cpu().pin_memory()
-    yh = torch.empty_like(xh).pin_memory()
-    xd = torch.empty_like(xs[0])
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0.record()
-    for i in range(K):
-        xd.copy_(xh, non_blocking=True)
-        y = ep_forward(xd, ops, world)
-        yh.copy_(y, non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    dist.barrier()
-    ems = torch.tensor([e0.elapsed_time(e1) / K], device=dev)
-    dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-    ems = float(ems.item())
-    pool.status()
-    flops = 2.0 * T * geom.top_k * 3 * geom.d_model * geom.d_ff
-    peaks, peak_kind = measured_peaks()
-    achieved = flops / (ms * 1e-3) / 1e12
-    a2a_bytes = 2 * T * geom.top_k * geom.d_model * 2          # rows out and back, whole job
-    # phase breakdown of one more step (device events at the phase marks)
-    evs = []
-
-    def mark(name):
-        e = torch.cuda.Event(enable_timing=True)
-        e.record()
-        evs.append((name, e))
-
-    dist.barrier()
-    torch.cuda.synchronize()
-    mark("start")
-    ep_forward(xs[0], ops, world, mark=mark)
-    torch.cuda.synchronize()
-    phases = {evs[i][0]: evs[i - 1][1].elapsed_time(evs[i][1]) for i in range(1, len(evs))}
-    ph = torch.tensor([phases[n] for n in phases], device=dev)
-    dist.all_reduce(ph, op=dist.ReduceOp.MAX)
-    phases = dict(zip(phases, [round(float(v), 3) for v in ph.tolist()]))
-    if rank == 0:
-        line = {
-            "metric": "MoE-block expert-parallel prefill tok/s (gpt-oss layer, T=%d)" % T,
-            "value": T / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "u4 weights as exact fp16 hi+lo pairs x fp16 tokens, f32 accumulate",
-            "data": "synthetic (seeded N(0,0.02) weights, MLX affine 4-bit g64; N(0,1) RMS-normed tokens)",
-            "config": {"workload": "config4: gpt-oss layer, experts sharded %d per GPU, NCCL "
-                                   "all-to-all dispatch/combine" % (geom.n_experts // world),
-                       "placement": {"slots_per_gpu": base + spare, "replicas": int(table[:, 0].sum() - geom.n_experts),
-                                     "max_rank_share": max(rank_load) / max(1.0, sum(rank_load))},
-                       "tokens": T, "tokens_per_rank": Tr, "top_k": geom.top_k,
-                       "router_bias": "Zipf(1.1)", "parallelism": f"ep{world}",
-                       "l2": "inputs larger than L2: %.1f GB of expert weights per GPU"
-                             % (geom.n_experts // world * geom.payload_bytes / 1e9)},
-            "roofline": {"bound": "tensor", "achieved": achieved,
-                         "peak": peaks["bf16_tflops"] * world, "unit": "TFLOP/s",
-                         "frac": achieved / (peaks["bf16_tflops"] * world), "traffic": None,
-                         "peak_kind": peak_kind, "kernel": "whole expert-parallel step",
-                         "algorithmic_flops_per_step": flops,
-                         "a2a_bytes_per_step": a2a_bytes},
-            "cpu_baseline": None,
-            "e2e": {"value": T / (ems * 1e-3), "unit": "tok/s",
-                    "h2d_bytes_per_step": int(xh.numel() * 2 * world),
-                    "d2h_bytes_per_step": int(yh.numel() * 2 * world),
-                    "path": "ep.ep_forward on every rank, pinned host tokens in / result out"},
-            "gpu_launches": 12 * K,
-            "clocks": clk,
-            "phase_ms_max_over_ranks": phases,
-        }
-        print(json.dumps(line))
-    pool.close()
-    dist.destroy_process_group()
-
-
 def prefill_cpu_baseline(geom, st, w, b, x, model, n_tok):
     """The oracle on the first n_tok tokens of the batch (routing + every
     routed expert of those tokens), scaled to tok/s."""
@@ -349,7 +223,7 @@ def prefill_cpu_baseline(geom, st, w, b, x, model, n_tok):
     blobs = {int(e): st[int(e)].numpy() for e in np.unique(inds)}
     OM.expert_block(xn, inds, scores, blobs, comps, model)
     dt = time.perf_counter() - t0
-    return {"value": n_tok / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": n_tok / dt, "unit": "tok/s", "cores": len(os.sched_getaffinity(0)), "kind": "port",
             "sample": f"{n_tok} tokens of the batch ({dt:.1f} s): routing and every routed expert"}
 
 
@@ -407,96 +281,293 @@ def measured_peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
+# ---------------------------------------------------------- expert parallel
+EP_TOKENS = 16384
+EP_WORKLOAD = ("config4: gpt-oss layer (d=ff=2880, top-4 of 128, Zipf(1.1) router bias) on "
+               "T=16384 tokens, experts sharded over the ranks, NCCL all-to-all dispatch/combine")
+
+
+def ep_measure(args, world, rank, dev, steps, warmup):
+    """The gpt-oss layer on T tokens (default 16384) with its 128 experts
+    sharded over the ranks (one rank: the whole layer on one GPU, the same
+    block without the exchange). Every rank routes its T/world tokens; a
+    step is one expert-parallel block on every rank (route, pack, all-to-all
+    out, local grouped GEMMs, all-to-all back, combine), timed on the device
+    as the max over ranks. Returns the measurement dict (every rank)."""
+    import torch
+    import torch.distributed as dist
+    from moe_stream_b200 import geometry, store as S
+    from moe_stream_b200.block import MoEBlock
+    from moe_stream_b200.ep import (DeviceOps, ep_forward, load_local_experts, plan_placement,
+                                    routed_counts)
+    from moe_stream_b200.pool import ExpertPool
+    geom = geometry.gptoss(1)
+    T = args.tokens or EP_TOKENS
+    if T % world or geom.n_experts % world:
+        raise SystemExit(f"T={T} and {geom.n_experts} experts must split over {world} ranks")
+    Tr = T // world
+    base = geom.n_experts // world
+    spare = 0 if (world == 1 or args.no_replicas) else base // 2
+    pool = ExpertPool(geom, base + spare, depths=(), max_tokens=T if world == 1 else T)
+    st = torch.from_numpy(pool.alloc_store()).view(geom.n_keys, geom.blob_bytes)
+    st.copy_(S.make_layer_blobs(geom, SEED, 0, device=dev).cpu())
+    w, b = S.router_weights(geom, SEED, 0, zipf_s=1.1)
+    block = MoEBlock(pool, 0, w, b)
+    xs = [S.rms_norm_tokens(T, geom.d_model, seed=SEED + 200 + i)[rank * Tr:(rank + 1) * Tr]
+          .to(dev) for i in range(3)]
+    rank_share = 1.0
+    if world > 1:
+        # placement from a calibration batch (not a timed one): hot experts
+        # replicated into the spare slots, replicas balanced over the ranks
+        counts = routed_counts(DeviceOps(block, world), xs[2])
+        table, slots = plan_placement(counts, world, base + spare)
+        load_local_experts(pool, 0, rank, world, slots[rank])
+        ops = DeviceOps(block, world, placement=table)
+        loads = [float(sum(counts[e] / table[e, 0] for e in r)) for r in slots]
+        rank_share = max(loads) / max(1.0, sum(loads))
+        fwd = lambda x: ep_forward(x, ops, world)
+    else:
+        load_local_experts(pool, 0, 0, 1)
+        y1 = torch.empty_like(xs[0])
+        fwd = lambda x: block(x, out=y1)
+    xs = xs[:2]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    W, K = max(3, warmup), max(1, steps)
+    for i in range(W):
+        fwd(xs[i % 2])
+    torch.cuda.synchronize()
+    pool.status()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        fwd(xs[i % 2])
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    pool.status()
+    ms = max_over_ranks(e0.elapsed_time(e1) / K)
+    # e2e: pinned host tokens in, pinned host result out, every step
+    xh = xs[0].cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    xd = torch.empty_like(xs[0])
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(K):
+        xd.copy_(xh, non_blocking=True)
+        y = fwd(xd)
+        yh.copy_(y, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ems = max_over_ranks(e0.elapsed_time(e1) / K)
+    pool.status()
+    flops = 2.0 * T * geom.top_k * 3 * geom.d_model * geom.d_ff
+    peaks, peak_kind = measured_peaks()
+    achieved = flops / (ms * 1e-3) / 1e12
+    out = {"workload": EP_WORKLOAD, "n_gpus": world, "tokens": T, "tokens_per_rank": Tr,
+           "value": T / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms, "steps": K, "warmup": W,
+           "scaling": "strong",
+           "placement": {"slots_per_gpu": base + spare, "max_rank_share": rank_share},
+           "roofline": {"bound": "tensor", "achieved": achieved,
+                        "peak": peaks["bf16_tflops"] * world, "unit": "TFLOP/s",
+                        "frac": achieved / (peaks["bf16_tflops"] * world), "peak_kind": peak_kind,
+                        "algorithmic_flops_per_step": flops},
+           "e2e": {"value": T / (ems * 1e-3), "unit": "tok/s",
+                   "h2d_bytes_per_step": int(xh.numel() * 2 * world),
+                   "d2h_bytes_per_step": int(yh.numel() * 2 * world)},
+           "a2a_bytes_per_step": 2 * T * geom.top_k * geom.d_model * 2 if world > 1 else 0}
+    if world > 1:
+        # phase breakdown of one more step (device events at the phase marks)
+        evs = []
+
+        def mark(name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            evs.append((name, e))
+
+        barrier()
+        torch.cuda.synchronize()
+        mark("start")
+        ep_forward(xs[0], ops, world, mark=mark)
+        torch.cuda.synchronize()
+        phases = {evs[i][0]: evs[i - 1][1].elapsed_time(evs[i][1]) for i in range(1, len(evs))}
+        ph = torch.tensor([phases[n] for n in phases], device=dev)
+        dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+        out["phase_ms_max_over_ranks"] = dict(zip(phases, [round(float(v), 3) for v in ph.tolist()]))
+    pool.close()
+    del st
+    return out
+
+
+def ep_case(args):
+    """--case ep: only the expert-parallel measurement, as its own line."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=300), device_id=dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ep = ep_measure(args, world, rank, dev, args.steps, args.warmup)
+    clk = clocks.stop()
+    if rank == 0:
+        line = {"metric": "MoE-block expert-parallel prefill tok/s (gpt-oss layer, T=%d)" % ep["tokens"],
+                "value": ep["value"], "unit": "tok/s", "n_gpus": world, "steps": ep["steps"],
+                "warmup": ep["warmup"], "ms_per_step": ep["ms_per_step"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None,
+                "dtype": "u4 weights as exact fp16 hi+lo pairs x fp16 tokens, f32 accumulate",
+                "data": "synthetic (seeded N(0,0.02) weights, MLX affine 4-bit g64; N(0,1) RMS-normed tokens)",
+                "config": {"workload": EP_WORKLOAD, "parallelism": f"ep{world}"},
+                "roofline": dict(ep["roofline"], traffic=None), "cpu_baseline": None,
+                "e2e": ep["e2e"], "gpu_launches": 12 * ep["steps"], "clocks": clk,
+                "placement": ep["placement"]}
+        if "phase_ms_max_over_ranks" in ep:
+            line["phase_ms_max_over_ranks"] = ep["phase_ms_max_over_ranks"]
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------------ CPU baseline
-def cpu_baseline(geom, store, routers, X, n_layers_sample):
-    """The oracle (numpy restatement of the reference's block, MLX bf16
-    rounding points) on one token over `n_layers_sample` layers, scaled to
-    tokens/s of the 48-layer stack. Routing + expert math; the pool is
-    irrelevant to the CPU path's arithmetic."""
-    import numpy as np
-    from oracle import moe as OM
-    comps = [dict(c) for c in geom.components]
-    t0 = time.perf_counter()
-    for layer in range(n_layers_sample):
-        x = X[0, layer:layer + 1].float().numpy()
-        w, b = routers[layer]
-        inds, scores, _ = OM.route_qwen3(x, w.float().numpy(), geom.top_k, True,
-                                         b.float().numpy() if b is not None else None)
-        base = layer * geom.n_experts
-        blobs = {int(e): np.asarray(store[(base + int(e)) * geom.blob_bytes:
-                                          (base + int(e) + 1) * geom.blob_bytes])
-                 for e in inds[0]}
-        OM.expert_block(x, inds, scores, blobs, comps, "qwen3")
+def cpu_threads():
+    """Host threads the CPU legs use: every core this process may run on."""
+    import torch
+    n = len(os.sched_getaffinity(0))
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def decode_cpu_baseline(geom, blob_of, routers, X, seconds):
+    """The CPU port (oracle.torch_port: vectorised fp32 torch with MLX's bf16
+    rounding points, the pool simulator and blob fills) on whole 48-layer
+    tokens of the same workload, for about `seconds` (at least two tokens);
+    tokens/s."""
+    import torch
+    from oracle.torch_port import DecodeStackCPU
+    cores = cpu_threads()
+    cpu = DecodeStackCPU(geom, blob_of, routers, N_SLOTS)
+    cpu.step(X[0].float())                      # warm-up token
+    n, t0 = 0, time.perf_counter()
+    while n < 2 or (time.perf_counter() - t0 < seconds and n + 1 < X.shape[0]):
+        cpu.step(X[1 + n].float())
+        n += 1
     dt = time.perf_counter() - t0
-    per_layer = dt / n_layers_sample
-    return {"value": 1.0 / (per_layer * geom.n_layers), "unit": "tok/s",
-            "cores": os.cpu_count(), "kind": "port",
-            "sample": f"1 token x {n_layers_sample} of {geom.n_layers} layers "
-                      f"({dt:.1f} s), scaled to the 48-layer stack"}
+    return {"value": n / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} whole tokens x {geom.n_layers} layers after one warm-up token "
+                      f"({dt:.1f} s): router, speculation, pool simulator with blob fills, "
+                      f"8 experts per layer (oracle.torch_port, fp32 torch on the host)"}
+
+
+def _layer_store(geom):
+    """blob_of(key) over a store generated layer by layer on first touch:
+    the same blobs as the GPU arm (make_layer_blobs on a GPU) when one is
+    present; without one (the CPU-only contract test), random 4-bit codes
+    with N(0,0.02)-sized scales, which give the same amount of work."""
+    import numpy as np
+    import torch
+    from moe_stream_b200 import store as S
+    layers = {}
+    gpu = torch.cuda.is_available()
+
+    def cpu_blobs(n=32):
+        g = torch.Generator().manual_seed(SEED * 31 + 7)
+        out = torch.randint(0, 256, (n, geom.blob_bytes), dtype=torch.uint8, generator=g)
+        for c in geom.components:
+            if c["dtype"] == "BF16":
+                v = (torch.rand(n, c["nbytes"] // 2, generator=g) * 0.01 + 0.001).to(torch.bfloat16)
+                out[:, c["offset"]:c["offset"] + c["nbytes"]] = v.view(torch.uint8)
+        return out.numpy()
+
+    def blob_of(key):
+        layer, e = divmod(int(key), geom.n_experts)
+        if gpu:
+            if layer not in layers:
+                layers[layer] = S.make_layer_blobs(geom, SEED, layer, device="cuda").cpu().numpy()
+            return layers[layer][e]
+        if "cpu" not in layers:
+            layers["cpu"] = cpu_blobs()
+        return layers["cpu"][int(key) % layers["cpu"].shape[0]]
+
+    return blob_of, ("the GPU arm's blobs (generated layer by layer on the GPU)" if gpu else
+                     "32 random blobs of the same shapes reused for every key (no GPU here to "
+                     "generate the GPU arm's blobs; the same work per token)")
 
 
 def reference_arm(args):
-    """--impl reference: the CPU restatement of the reference's block (MLX is
-    not installable here). One step = one (token, layer) block call."""
+    """--impl reference: the CPU port of the reference's decode block (MLX,
+    the reference's own compute path, is not installable here). One step =
+    one decoded token through all 48 layers on the host cores."""
     import torch
     from moe_stream_b200 import geometry, store as S
-    from oracle import moe as OM
-    import numpy as np
-    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    from oracle.torch_port import DecodeStackCPU
+    cores = cpu_threads()
     geom = geometry.qwen3(N_LAYERS)
     routers = [S.router_weights(geom, SEED, l, zipf_s=1.1) for l in range(N_LAYERS)]
-    X = S.decode_inputs(1, N_LAYERS, geom.d_model, SEED)
-    comps = [dict(c) for c in geom.components]
-    cache = {}
-
-    def blob(layer, e):
-        key = (layer, e)
-        if key not in cache:
-            cache[key] = S.make_blob(geom, SEED, layer, e).numpy()
-        return cache[key]
-
-    def step(i):
-        layer = i % N_LAYERS
-        x = X[0, layer:layer + 1].float().numpy()
-        w, b = routers[layer]
-        inds, scores, _ = OM.route_qwen3(x, w.float().numpy(), geom.top_k, True, b.float().numpy())
-        blobs = {int(e): blob(layer, int(e)) for e in inds[0]}
-        OM.expert_block(x, inds, scores, blobs, comps, "qwen3")
-
-    # blobs are generated outside the timed region
-    for i in range(args.warmup + args.steps):
-        layer = i % N_LAYERS
-        x = X[0, layer:layer + 1].float().numpy()
-        w, b = routers[layer]
-        inds, _, _ = OM.route_qwen3(x, w.float().numpy(), geom.top_k, True, b.float().numpy())
-        for e in inds[0]:
-            blob(layer, int(e))
+    X = S.decode_inputs(args.warmup + args.steps, N_LAYERS, geom.d_model, SEED + 1)
+    blob_of, data = _layer_store(geom)
+    cpu = DecodeStackCPU(geom, blob_of, routers, N_SLOTS)
     for i in range(args.warmup):
-        step(i)
+        cpu.step(X[i].float())
     t0 = time.perf_counter()
     for i in range(args.steps):
-        step(args.warmup + i)
+        cpu.step(X[args.warmup + i].float())
     dt = time.perf_counter() - t0
-    tok_s = args.steps / (dt * N_LAYERS)
+    tok_s = args.steps / dt
     line = {"impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32/bf16-rounded",
-            "data": "synthetic", "config": {"workload": WORKLOAD, "step": "one (token, layer) block call"},
-            "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": torch.get_num_threads(),
-                             "kind": "port",
-                             "sample": "oracle (numpy, MLX bf16 rounding points) block calls; "
-                                       "MLX itself is not installable on this image"},
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 rounding points)",
+            "data": "synthetic: " + data,
+            "config": {"workload": WORKLOAD, "step": "one decoded token (48 block calls)"},
+            "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": f"{args.steps} whole tokens after {args.warmup} warm-up tokens "
+                                       f"(oracle.torch_port: router, speculation, pool simulator "
+                                       f"with blob fills, experts in fp32 torch); MLX itself is not "
+                                       f"installable on this image"},
             "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
 
+def profile_traffic():
+    """DRAM bytes (read + write) of one layer's expert kernels from the
+    committed ncu summary, or None."""
+    import re
+    path = os.path.join(ROOT, "profiles", "expert_kernels_layer_full.md")
+    try:
+        m = re.search(r"traffic per layer \(k_up \+ k_down[^)]*\):\s*([0-9]+)\s*bytes", open(path).read())
+    except OSError:
+        return None
+    return int(m.group(1)) if m else None
+
+
 # -------------------------------------------------------------- GPU arm
 def gpu_arm(args):
+    import ctypes
     import torch
     import torch.distributed as dist
-    from moe_stream_b200 import geometry, store as S
+    from moe_stream_b200 import _lib, geometry, store as S
     from moe_stream_b200.block import DecodeGraph, MoEBlock
     from moe_stream_b200.pool import ExpertPool
 
@@ -511,6 +582,17 @@ def gpu_arm(args):
     else:
         torch.cuda.set_device(0)
     dev = torch.device(f"cuda:{torch.cuda.current_device()}")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     geom = geometry.qwen3(N_LAYERS)
     TB = args.batch
@@ -528,10 +610,13 @@ def gpu_arm(args):
     blocks = [MoEBlock(pool, l, w, b) for l, (w, b) in enumerate(routers)]
 
     W, K = args.warmup, args.steps
-    # [steps, L, TB, d]: token i of a step follows its own sequence
-    X_cpu = torch.stack([S.decode_inputs(W + 2 * K + 64, N_LAYERS, geom.d_model, SEED + rank + 1000 * i)
-                         for i in range(TB)], dim=2)
-    X = X_cpu[:W + K].to(dev)
+    PR = args.preroll_max
+    n_prof = 16
+    # [tokens, L, TB, d]: token i of a step follows its own sequence; pre-roll
+    # tokens first, then warm-up, timed and profiling tokens
+    X_cpu = torch.stack([S.decode_inputs(PR + W + K + n_prof, N_LAYERS, geom.d_model,
+                                         SEED + rank + 1000 * i) for i in range(TB)], dim=2)
+    X = X_cpu.to(dev)
 
     # one eager token before capture, then the graph
     for layer, b in enumerate(blocks):
@@ -539,16 +624,37 @@ def gpu_arm(args):
     torch.cuda.synchronize()
     pool.status()
     g = DecodeGraph(blocks, T=TB)
-    for t in range(1, W):
+
+    # ---------------------------------------------- steady state pre-roll
+    # untimed tokens until the cache-hit rate over a trailing window of 32
+    # tokens reaches the target (the pool's steady state), at most PR
+    window, used = 32, 1
+    hist = [pool.stats()]
+    roll_hit = 0.0
+    while used < PR:
+        n = min(16, PR - used)
+        for t in range(used, used + n):
+            g.step(X[t])
+        used += n
+        hist.append(pool.stats())
+        back = hist[max(0, len(hist) - 1 - window // 16)]
+        tot = hist[-1]["total"] - back["total"]
+        roll_hit = (hist[-1]["cache"] - back["cache"]) / max(1, tot)
+        if used >= 2 * window and roll_hit >= args.hit_target:
+            break
+    torch.cuda.synchronize()
+    pool.status()
+    t0 = used
+    for t in range(t0, t0 + W):
         g.step(X[t])
     torch.cuda.synchronize()
     pool.status()
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    t0 += W
+    barrier()
 
     # ---------------------------------------------------------- timed
+    snap = pool.save_state(with_arena=True)       # e2e replays the same tokens from here
+    torch.cuda.synchronize()
     s0 = pool.stats()
     clocks = ClockSampler(local)
     clocks.start()
@@ -556,7 +662,7 @@ def gpu_arm(args):
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
-    for t in range(W, W + K):
+    for t in range(t0, t0 + K):
         g.step(X[t])
     ev1.record()
     torch.cuda.synchronize()
@@ -565,29 +671,53 @@ def gpu_arm(args):
     clk = clocks.stop()
     pool.status()
     s1 = pool.stats()
-    ms_max = ms
-    if world > 1:
-        tt = torch.tensor([ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms_max = float(tt.item())
+    y_value = g.y.clone()
+    table_value = pool.table()
+    ms_max = max_over_ranks(ms)
     tok_s = world * K * TB / (ms_max / 1e3)
     d = {k: s1[k] - s0[k] for k in ("total", "prefetch", "cache", "miss")}
     hit = {"cache": d["cache"] / max(1, d["total"]),
            "resident_at_acquire": (d["cache"] + d["prefetch"]) / max(1, d["total"]),
            "miss": d["miss"] / max(1, d["total"]),
-           "h2d_fill_bytes_per_token": (s1["gb"] - s0["gb"]) * 2 ** 30 / K}
+           "h2d_fill_bytes_per_token": (s1["gb"] - s0["gb"]) * 2 ** 30 / K,
+           "preroll_tokens": used, "preroll_window_cache_hit": roll_hit}
+
+    # ------------------------ e2e: the same tokens from the same pool state
+    pool.load_state(snap, with_arena=True)
+    torch.cuda.synchronize()
+    s2 = pool.stats()
+    Xh = X_cpu[t0:t0 + K].pin_memory()
+    Yh = torch.empty_like(Xh).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for t in range(K):
+        y = g.step(Xh[t])
+        Yh[t].copy_(y, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ems = max_over_ranks(e0.elapsed_time(e1))
+    pool.status()
+    s3 = pool.stats()
+    same = (torch.equal(Yh[K - 1].to(dev), y_value) and (pool.table() == table_value).all()
+            and all(s3[k] - s2[k] == d[k] for k in d))
+    del snap
+    e2e_tok_s = world * K * TB / (ems / 1e3)
+    e2e = {"value": e2e_tok_s, "unit": "tok/s",
+           "h2d_bytes_per_step": int(Xh[0].numel() * 2), "d2h_bytes_per_step": int(Yh[0].numel() * 2),
+           "path": "DecodeGraph over MoEBlock.__call__ (ms_moe_block), pinned host x in / y out",
+           "same_tokens_and_pool_state_as_value": bool(same),
+           "e2e_le_value": bool(e2e_tok_s <= tok_s)}
 
     # ------------------------------------- kernel timing (same kernels, events)
-    from moe_stream_b200 import _lib
-    import ctypes
     _lib.check(pool._lib.ms_pool_profile(pool._h, 1))
     gp = DecodeGraph(blocks, T=TB)
-    n_prof = 16
     acc = [[0.0, 0.0, 0.0] for _ in range(N_LAYERS)]
     buf = (ctypes.c_float * 3)()
-    Xp = X_cpu[W + K:W + K + n_prof].to(dev)
-    for t in range(n_prof):
-        gp.step(Xp[t])
+    for t in range(t0 + K, t0 + K + n_prof):
+        gp.step(X[t])
         torch.cuda.synchronize()
         for layer in range(N_LAYERS):
             _lib.check(pool._lib.ms_pool_timing(pool._h, layer, buf))
@@ -603,33 +733,19 @@ def gpu_arm(args):
     peaks, peak_kind = measured_peaks()
     achieved = bytes_per_layer / (expert_ms * 1e-3) / 1e9
     del gp
-
-    # ----------------------------------------------------------- e2e
-    Xh = X_cpu[W + K + n_prof:W + 2 * K + n_prof].pin_memory()
-    Yh = torch.empty_like(Xh).pin_memory()
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for t in range(K):
-        y = g.step(Xh[t])
-        Yh[t].copy_(y, non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    barrier()
-    ems = e0.elapsed_time(e1)
-    if world > 1:
-        tt = torch.tensor([ems], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ems = float(tt.item())
-    e2e = {"value": world * K * TB / (ems / 1e3), "unit": "tok/s",
-           "h2d_bytes_per_step": int(Xh[0].numel() * 2), "d2h_bytes_per_step": int(Yh[0].numel() * 2),
-           "path": "DecodeGraph over MoEBlock.__call__ (ms_moe_block), pinned host x in / y out"}
     pool.status()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and TB == 1:
-        cpu = cpu_baseline(geom, store, routers, X_cpu[:, :, 0], args.cpu_sample_layers)
+        blob_of = lambda key: store[int(key) * geom.blob_bytes:(int(key) + 1) * geom.blob_bytes]
+        cpu = decode_cpu_baseline(geom, blob_of, routers, X_cpu[:, :, 0], args.cpu_seconds)
+    pool.close()
+    del store, st_t, X
+    torch.cuda.empty_cache()
+
+    ep = None
+    if not args.no_ep and TB == 1:
+        ep = ep_measure(args, world, rank, dev, max(3, min(K, 10)), 3)
 
     if rank == 0:
         line = {
@@ -642,13 +758,16 @@ def gpu_arm(args):
             "config": {"workload": WORKLOAD, "n_layers": N_LAYERS, "n_slots": N_SLOTS,
                        "n_experts_total": geom.n_keys, "top_k": geom.top_k, "batch": TB,
                        "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                       "steady_state": f"untimed pre-roll until the cache-hit rate over the last "
+                                       f"{window} tokens >= {args.hit_target} (at most {PR} tokens)",
                        "l2": "inputs larger than L2: 1.02 GB of expert weights per step"},
             "hit_rate": hit,
             "expert_hbm_gbs": achieved,
             "per_layer_us": {"router_table": per_layer[0] * 1e3, "fill": per_layer[1] * 1e3,
                              "experts": expert_ms * 1e3},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
-                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                         "traffic": profile_traffic() if TB == 1 else None,
                          "peak_kind": peak_kind,
                          "kernel": "k_up + k_down (expert MLP of one layer)",
                          "algorithmic_bytes_per_launch": bytes_per_layer,
@@ -661,8 +780,9 @@ def gpu_arm(args):
             "clocks": clk,
             "setup_s": {"store_generation": t_gen},
         }
+        if ep is not None:
+            line["expert_parallel"] = ep
         print(json.dumps(line))
-    pool.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -196,6 +196,18 @@ int ms_pool_join(ms_pool* pool, void* stream);
 int ms_expert_mlp(ms_pool* pool, const int32_t* slots, const float* scores,
                   const void* x, int T, int k, void* y, void* stream);
 
+/* Checkpoint of a pool, no reference counterpart (the reference's pool lives
+ * and dies with its process). The state is the slot table with its clocks,
+ * counters and statistics and, when with_arena is set, the slot arena
+ * itself; a pool restored from a snapshot continues exactly as the saved one
+ * did (same slots, same fills, same outputs). ms_pool_state_bytes gives the
+ * size of the caller-owned device buffer (256-byte aligned); save and load
+ * join the pending prefetch fills into `stream` and enqueue device-to-device
+ * copies on it. */
+int ms_pool_state_bytes(ms_pool* pool, int with_arena, size_t* bytes);
+int ms_pool_save_state(ms_pool* pool, void* dev_buf, int with_arena, void* stream);
+int ms_pool_load_state(ms_pool* pool, const void* dev_buf, int with_arena, void* stream);
+
 /* Diagnostic with no reference counterpart: the SASS target the library's
  * kernels carry for `device` (cudaFuncAttributes.binaryVersion of one of
  * them; 100 for sm_100a). */

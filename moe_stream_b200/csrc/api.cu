@@ -7,6 +7,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/moestream.h"
@@ -999,6 +1000,57 @@ int ms_pool_timing(ms_pool* p, int layer, float* out3) {
   CK(cudaEventSynchronize(ev[3]));
   for (int i = 0; i < 3; ++i) CK(cudaEventElapsedTime(&out3[i], ev[i], ev[i + 1]));
   return MS_OK;
+}
+
+// The pool's persistent state as (device pointer, bytes) segments: the slot
+// table and its counters, then (with_arena) the slot arena. Per-call scratch
+// (fill lists, groups, arrival counters, which are zero between calls) is not
+// part of it.
+static std::vector<std::pair<void*, size_t>> state_segments(ms_pool* p, int with_arena) {
+  const DevTable& t = p->tab;
+  const size_t ns = (size_t)t.n_slots, nk = (size_t)t.n_keys;
+  std::vector<std::pair<void*, size_t>> seg = {
+      {t.key_of, 4 * ns},      {t.slot_of, 4 * nk},  {t.freq, 4 * nk},     {t.born, 8 * nk},
+      {t.last_use, 8 * nk},    {t.kflags, nk},       {t.pinned, ns},       {t.pin_list, 4 * ns},
+      {t.pend_list, 4 * ns},   {t.ctr, sizeof(TableCtr)}};
+  if (with_arena) seg.push_back({p->arena, p->arena_bytes});
+  return seg;
+}
+
+static size_t seg_round(size_t b) { return (b + 255) & ~size_t(255); }
+
+int ms_pool_state_bytes(ms_pool* p, int with_arena, size_t* bytes) {
+  if (!p || !bytes) return fail(MS_E_INVALID, "NULL argument");
+  size_t n = 0;
+  for (const auto& sg : state_segments(p, with_arena)) n += seg_round(sg.second);
+  *bytes = n;
+  return MS_OK;
+}
+
+static int copy_state(ms_pool* p, void* buf, int with_arena, cudaStream_t s, bool save) {
+  if (!buf || (reinterpret_cast<uintptr_t>(buf) & 255u))
+    return fail(MS_E_INVALID, "the state buffer must be a 256-byte aligned device pointer");
+  CK(cudaSetDevice(p->device));
+  // no prefetch fill may still be writing the arena or the table's slots
+  if (int rc = join_side(p, s)) return rc;
+  uint8_t* b = static_cast<uint8_t*>(buf);
+  for (const auto& sg : state_segments(p, with_arena)) {
+    if (save) CK(cudaMemcpyAsync(b, sg.first, sg.second, cudaMemcpyDeviceToDevice, s));
+    else CK(cudaMemcpyAsync(sg.first, b, sg.second, cudaMemcpyDeviceToDevice, s));
+    b += seg_round(sg.second);
+  }
+  return MS_OK;
+}
+
+int ms_pool_save_state(ms_pool* p, void* dev_buf, int with_arena, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  return copy_state(p, dev_buf, with_arena, static_cast<cudaStream_t>(stream), true);
+}
+
+int ms_pool_load_state(ms_pool* p, const void* dev_buf, int with_arena, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  return copy_state(p, const_cast<void*>(dev_buf), with_arena, static_cast<cudaStream_t>(stream),
+                    false);
 }
 
 int ms_kernel_arch(int device, int* binary_version) {

@@ -102,6 +102,7 @@ struct ExpArgs {
   unsigned* cnt;              // [d_model/16]
   uint16_t* y;                // bf16 [T, d_model]
   int* status;                // sticky pool status (bounded waits report here)
+  int stages_up, stages_dn;   // ring depths of k_up / k_down (set by launch_expert)
 };
 
 // ------------------------------------------------ wide batches (prefill)

@@ -228,6 +228,22 @@ class ExpertPool:
         pool's side stream (needed before ending a graph capture)."""
         _lib.check(self._lib.ms_pool_join(self._h, _stream_ptr(stream)))
 
+    # ------------------------------------------------------- checkpoints
+    def save_state(self, with_arena=True, stream=None):
+        """Snapshot of the pool (slot table, clocks, counters and, with_arena,
+        the slot contents) as a device uint8 tensor; ``load_state`` puts it
+        back, after which the pool continues exactly as it did from here."""
+        n = ctypes.c_size_t()
+        _lib.check(self._lib.ms_pool_state_bytes(self._h, int(with_arena), ctypes.byref(n)))
+        buf = torch.empty(n.value, dtype=torch.uint8, device=f"cuda:{self.device}")
+        _lib.check(self._lib.ms_pool_save_state(self._h, ctypes.c_void_p(buf.data_ptr()),
+                                                int(with_arena), _stream_ptr(stream)))
+        return buf
+
+    def load_state(self, buf, with_arena=True, stream=None):
+        _lib.check(self._lib.ms_pool_load_state(self._h, ctypes.c_void_p(buf.data_ptr()),
+                                                int(with_arena), _stream_ptr(stream)))
+
     def close(self):
         if getattr(self, "_h", None) is not None and self._h.value:
             self.views = {}

@@ -19,6 +19,9 @@ It is a plain numpy restatement of the reference's algorithm:
 * ``pool_sim`` -- ``ExpertPool``'s slot bookkeeping (engine_v3.py:303-464)
                   made deterministic: reads complete at the end of each
                   ``acquire``.
+* ``torch_port`` -- the whole decode step (routers, speculation, pool
+                  simulator with blob fills, expert math) vectorised in
+                  float32 torch on the host: the timed CPU baseline.
 
 Parity status. The slot-pool restatement is PINNED: it is checked against
 fixtures produced by running the reference's own ``ExpertPool`` code
