@@ -150,6 +150,10 @@ struct ms_pool {
   uint16_t* hbuf = nullptr;
   uint16_t* ybuf = nullptr;
   CUtensorMap tm_x{}, tm_h{}, tm_wg{}, tm_wu{}, tm_wd{};
+  // decode expert kernels: gate, up and down weight rows as whole-row tiles
+  // (encode_rows_map), when the row widths allow it
+  CUtensorMap dec_maps[3] = {};
+  bool dec_maps_ok = false;
   int* mlp_cnt = nullptr;       // [n_slots + 1] pairs per slot (wide ms_expert_mlp)
   int* mlp_wkeys = nullptr;     // [max_pairs] sanitised slot keys (wide ms_expert_mlp)
   int* ep_scratch = nullptr;    // [128]: counts and cursors of ms_ep_pack
@@ -400,6 +404,14 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
       cudaSuccess)
     return bail(fail(MS_E_NOMEM, "cudaMallocHost failed"));
   (void)kp;
+  {
+    const int64_t* o = &p->geom.comp_offset[0][0];
+    const int dr = expert_down_rows(geom->model, D, F);
+    p->dec_maps_ok =
+        encode_rows_map(&p->dec_maps[0], p->arena + o[0], D / 2, F, cfg->n_slots, geom->blob_bytes, 16) == 0 &&
+        encode_rows_map(&p->dec_maps[1], p->arena + o[4], D / 2, F, cfg->n_slots, geom->blob_bytes, 16) == 0 &&
+        encode_rows_map(&p->dec_maps[2], p->arena + o[8], F / 2, D, cfg->n_slots, geom->blob_bytes, dr) == 0;
+  }
   // the fill and route kernels run beside the expert kernels (the fills on
   // the side stream): keep every SM on its largest shared-memory split
   CKB(route_prefer_shared());
@@ -849,7 +861,8 @@ int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* str
     if ((rc = wide_experts(p, x, T, k, p->inds, p->scores_f, p->pair_slot, y, s))) return rc;
   } else {
     const int max_groups = std::min(T * k, p->geom.n_experts);
-    CK(launch_expert(exp_args(p, x, T, y, p->scores_f), max_groups, s));
+    CK(launch_expert(exp_args(p, x, T, y, p->scores_f), max_groups, s,
+                     p->dec_maps_ok ? p->dec_maps : nullptr));
   }
   if (ev) CK(cudaEventRecordWithFlags(ev[3], s, rec_flags));
   return MS_OK;
@@ -918,7 +931,8 @@ int ms_expert_mlp(ms_pool* p, const int32_t* slots, const float* scores, const v
   a.xsum = p->xsum;
   a.grp = p->grp;
   CK(launch_mlp_prep(a, s));
-  CK(launch_expert(exp_args(p, x, T, y, scores), std::min(T * k, p->cfg.n_slots), s));
+  CK(launch_expert(exp_args(p, x, T, y, scores), std::min(T * k, p->cfg.n_slots), s,
+                   p->dec_maps_ok ? p->dec_maps : nullptr));
   return MS_OK;
 }
 

@@ -29,9 +29,14 @@ namespace ms {
 
 // Qwen3 shapes (KPW 4): three CTAs per SM, so a batch-1 layer's 384 tiles
 // fit one wave; the wider rows of the other shapes keep two.
-template <int MODEL, int KPW>
-__global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2) k_up(ExpArgs A) {
-  extern __shared__ __align__(128) uint8_t smem[];
+// TMA: the gate and up rows of the tile come as two tensor-map boxes
+// (128-byte swizzled, see encode_rows_map) instead of 32 row copies.
+template <int MODEL, int KPW, bool TMA>
+__global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2)
+    k_up(ExpArgs A, const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmU) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // swizzled boxes need a 1 KB aligned destination
+  uint8_t* smem = smem_raw + (TMA ? ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) : 0u);
   pdl_wait();                                   // slots and groups come from the route step
   pdl_trigger();
   const int g = blockIdx.y;
@@ -45,30 +50,39 @@ __global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2) 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g4 = lane >> 2, c = lane & 3;
   const int K = A.geo.d_model, G = K / 64, F = A.geo.d_ff, GF = F / 64;
   const int k = A.geo.top_k;
-  const int row_bytes = K / 2, stride = UpSmem::stride(K);
+  const int row_bytes = K / 2;
+  const int stride = TMA ? 16 * 128 : UpSmem::stride(K);   // chunk stride when swizzled
+  const int a_bytes = TMA ? 16 * row_bytes : UpSmem::a_bytes(K);
   const int kg0 = min(G, warp * KPW), kg1 = min(G, kg0 + KPW);
 
-  uint8_t* sA[2] = {smem, smem + UpSmem::a_bytes(K)};
-  uint16_t* sSB = reinterpret_cast<uint16_t*>(smem + 2 * UpSmem::a_bytes(K));
+  uint8_t* sA[2] = {smem, smem + a_bytes};
+  uint16_t* sSB = reinterpret_cast<uint16_t*>(smem + 2 * a_bytes);
   const int sbn = 16 * G;                       // elements per staged [16][G] block
-  float* red = reinterpret_cast<float*>(smem + 2 * UpSmem::a_bytes(K) + 4 * UpSmem::sb_bytes(G));
+  float* red = reinterpret_cast<float*>(smem + 2 * a_bytes + 4 * UpSmem::sb_bytes(G));
   uint64_t* bar = reinterpret_cast<uint64_t*>(red + EX_WARPS * 2 * 4 * 32);
 
   const uint8_t* blob = A.arena + (long long)(slot < 0 ? 0 : slot) * A.geo.blob;
-  if (threadIdx.x == 0 && slot >= 0) {
-    mbar_init(bar, 1);
-    fence_barrier_init();
-    const uint64_t pol = l2_evict_first();     // the weights stream through L2
-    const unsigned bytes = 2u * 16u * row_bytes + 4u * UpSmem::sb_bytes(G);
-    mbar_expect_tx(bar, bytes);
-    for (int p = 0; p < 2; ++p) {
-      const uint8_t* W = blob + A.geo.off[p][0] + (long long)rt * 16 * row_bytes;
-      for (int r = 0; r < 16; ++r) bulk_g2s_hint(sA[p] + r * stride, W + r * row_bytes, row_bytes, bar, pol);
-      bulk_g2s_hint(sSB + (2 * p) * sbn, blob + A.geo.off[p][1] + (long long)rt * 16 * G * 2,
-                    UpSmem::sb_bytes(G), bar, pol);
-      bulk_g2s_hint(sSB + (2 * p + 1) * sbn, blob + A.geo.off[p][2] + (long long)rt * 16 * G * 2,
-                    UpSmem::sb_bytes(G), bar, pol);
+  if (warp == 0 && slot >= 0) {
+    // warp 0 issues the tile's 36 copies, one or two per lane: gate rows
+    // 0..15 and up rows 0..15, then the gate and up scales and biases
+    if (lane == 0) {
+      mbar_init(bar, 1);
+      fence_barrier_init();
+      mbar_expect_tx(bar, 2u * 16u * row_bytes + 4u * UpSmem::sb_bytes(G));
     }
+    __syncwarp();
+    const uint64_t pol = l2_evict_first();     // the weights stream through L2
+    if (TMA) {
+      if (lane == 0) tma_load_4d_hint(sA[0], &tmG, 0, rt * 16, 0, slot, bar, pol);
+      if (lane == 1) tma_load_4d_hint(sA[1], &tmU, 0, rt * 16, 0, slot, bar, pol);
+    } else {
+      const int p = lane >> 4, r = lane & 15;
+      bulk_g2s_hint(sA[p] + r * stride, blob + A.geo.off[p][0] + (long long)(rt * 16 + r) * row_bytes,
+                    row_bytes, bar, pol);
+    }
+    if (lane < 4)
+      bulk_g2s_hint(sSB + lane * sbn, blob + A.geo.off[lane >> 1][1 + (lane & 1)] + (long long)rt * 16 * G * 2,
+                    UpSmem::sb_bytes(G), bar, pol);
   }
   __syncthreads();
   bool ok = true, waited = false;
@@ -93,9 +107,9 @@ __global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2) 
     }
     float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f};
     if (slot >= 0 && ok && kg0 < kg1) {
-      tile_dot_regs<KPW>(tg, sA[0], stride, G, kg0, kg1, g4, c, sSB, sSB + sbn, b0, b1, v0, v1);
-      tile_dot_regs<KPW>(tu, sA[1], stride, G, kg0, kg1, g4, c, sSB + 2 * sbn, sSB + 3 * sbn, b0, b1,
-                         v0, v1);
+      tile_dot_regs<KPW, TMA>(tg, sA[0], stride, G, kg0, kg1, g4, c, sSB, sSB + sbn, b0, b1, v0, v1);
+      tile_dot_regs<KPW, TMA>(tu, sA[1], stride, G, kg0, kg1, g4, c, sSB + 2 * sbn, sSB + 3 * sbn, b0,
+                              b1, v0, v1);
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -103,23 +117,25 @@ __global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2) 
       red[((warp * 2 + 1) * 4 + i) * 32 + lane] = tu[i];
     }
     __syncthreads();
-    if (warp == 0) {
-      float hs[2] = {0.f, 0.f}, hp[2] = {0.f, 0.f};
+    // epilogue: thread t < 128 owns (row r, column col) of the tile
+    if (threadIdx.x < 128) {
+      const int r = threadIdx.x & 15, col = threadIdx.x >> 4;
+      const int src = (r & 7) * 4 + (col >> 1), e = ((r >> 3) << 1) | (col & 1);
+      const int row = rt * 16 + r;
+      float hh_f = 0.f, hsc_f = 0.f;
+      const int pc = col < nn ? pairs[col] : -1;
+      if (col < nn) {
+        __half hsc = __float2half(0.f);
+        if (slot >= 0 && ok) {
+          float gv = 0.f, uv = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float gv = 0.f, uv = 0.f;
-#pragma unroll
-        for (int w = 0; w < EX_WARPS; ++w) {
-          gv += red[((w * 2 + 0) * 4 + i) * 32 + lane];
-          uv += red[((w * 2 + 1) * 4 + i) * 32 + lane];
-        }
-        const int row = rt * 16 + g4 + ((i < 2) ? 0 : 8);
-        const int col = 2 * c + (i & 1);
-        const int pc = (i & 1) ? pc1 : pc0;
-        if (col < nn && slot >= 0 && ok) {
-          float h;
+          for (int w = 0; w < EX_WARPS; ++w) {
+            gv += red[((w * 2 + 0) * 4 + e) * 32 + src];
+            uv += red[((w * 2 + 1) * 4 + e) * 32 + src];
+          }
           gv = bfr(gv);                          // gather_qmm outputs are bf16
           uv = bfr(uv);
+          float h;
           if (MODEL == 1) {
             const uint16_t* bgp = reinterpret_cast<const uint16_t*>(blob + A.geo.off[0][3]);
             const uint16_t* bup = reinterpret_cast<const uint16_t*>(blob + A.geo.off[1][3]);
@@ -128,39 +144,32 @@ __global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2) 
             h = silu_mul(gv, uv);
           }
           const __half hh = __float2half_rn(h);
-          const __half hsc = (row & 1) ? __hmul(hh, __float2half(0.0625f)) : hh;
-          A.hfrag[frag_off(pc, GF, row)] = hsc;
-          hs[i & 1] += __half2float(hh);
-          hp[i & 1] += __half2float(hsc);
-        } else if (col < nn) {
-          A.hfrag[frag_off(pc, GF, row)] = __float2half(0.f);
+          hsc = (row & 1) ? __hmul(hh, __float2half(0.0625f)) : hh;
+          hh_f = __half2float(hh);
+          hsc_f = __half2float(hsc);
         }
+        A.hfrag[frag_off(pc, GF, row)] = hsc;
       }
-      // sums over the 16 rows of the tile, per column
+      // sums over the 16 rows of the tile, per column (16 consecutive threads)
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-          hs[q] += __shfl_xor_sync(MS_FULL, hs[q], o);
-          hp[q] += __shfl_xor_sync(MS_FULL, hp[q], o);
-        }
+      for (int o = 1; o < 16; o <<= 1) {
+        hh_f += __shfl_xor_sync(MS_FULL, hh_f, o);
+        hsc_f += __shfl_xor_sync(MS_FULL, hsc_f, o);
       }
-      if (g4 == 0) {
-        const int nt = F / 16;
-        if (2 * c < nn)
-          *reinterpret_cast<float2*>(A.hpart + ((long long)pc0 * nt + rt) * 2) = make_float2(hs[0], hp[0]);
-        if (2 * c + 1 < nn)
-          *reinterpret_cast<float2*>(A.hpart + ((long long)pc1 * nt + rt) * 2) = make_float2(hs[1], hp[1]);
-      }
+      if (r == 0 && col < nn)
+        *reinterpret_cast<float2*>(A.hpart + ((long long)pc * (F / 16) + rt) * 2) =
+            make_float2(hh_f, hsc_f);
     }
     __syncthreads();
   }
 }
 
 
-template <int MODEL, int KPW, int RT>
-__global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
-  extern __shared__ __align__(128) uint8_t smem[];
+// TMA: the RT*16 down rows of the unit come as one tensor-map box.
+template <int MODEL, int KPW, int RT, bool TMA>
+__global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A, const __grid_constant__ CUtensorMap tmD) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + (TMA ? ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) : 0u);
   // the route step finished before k_up started, so the groups and the
   // filled slots can be read now; only h (k_up's output) needs pdl_wait
   const int g = blockIdx.y;
@@ -177,30 +186,41 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
   const int rt = blockIdx.x * RT + sub;
   const int K = A.geo.d_ff, G = K / 64, D = A.geo.d_model;
   const int k = A.geo.top_k;
-  const int row_bytes = K / 2, stride = DownSmem::stride(K);
+  const int row_bytes = K / 2;
+  const int stride = TMA ? RT * 16 * 128 : DownSmem::stride(K);   // chunk stride when swizzled
+  const int a_bytes = TMA ? RT * 16 * row_bytes : DownSmem::a_bytes(K, RT);
   const int kg0 = min(G, wk * KPW), kg1 = min(G, kg0 + KPW);
   const int nt_ff = K / 16;
 
   uint8_t* sA = smem;
-  uint16_t* sS = reinterpret_cast<uint16_t*>(smem + DownSmem::a_bytes(K, RT));
+  uint16_t* sS = reinterpret_cast<uint16_t*>(smem + a_bytes);
   uint16_t* sB = sS + RT * 16 * G;
-  float* red = reinterpret_cast<float*>(smem + DownSmem::a_bytes(K, RT) + 2 * DownSmem::sb_bytes(G, RT));
+  float* red = reinterpret_cast<float*>(smem + a_bytes + 2 * DownSmem::sb_bytes(G, RT));
   float* s_sums = red + EX_WARPS * 4 * 32;      // [8][G][2]
   uint64_t* bar = reinterpret_cast<uint64_t*>(s_sums + 8 * G * 2);
   __shared__ int s_last[RT];
 
   const uint8_t* blob = A.arena + (long long)(slot < 0 ? 0 : slot) * A.geo.blob;
-  if (threadIdx.x == 0 && slot >= 0) {
-    mbar_init(bar, 1);
-    fence_barrier_init();
+  if (warp == 0 && slot >= 0) {
+    // warp 0 issues the tile's copies, about one per lane: the RT*16 rows,
+    // then the scales and biases
+    if (lane == 0) {
+      mbar_init(bar, 1);
+      fence_barrier_init();
+      mbar_expect_tx(bar, (unsigned)(RT * 16 * row_bytes + 2 * DownSmem::sb_bytes(G, RT)));
+    }
+    __syncwarp();
     const uint64_t pol = l2_evict_first();     // the weights stream through L2
-    mbar_expect_tx(bar, (unsigned)(RT * 16 * row_bytes + 2 * DownSmem::sb_bytes(G, RT)));
-    const uint8_t* W = blob + A.geo.off[2][0] + (long long)blockIdx.x * RT * 16 * row_bytes;
-    for (int r = 0; r < RT * 16; ++r) bulk_g2s_hint(sA + r * stride, W + r * row_bytes, row_bytes, bar, pol);
-    bulk_g2s_hint(sS, blob + A.geo.off[2][1] + (long long)blockIdx.x * RT * 16 * G * 2,
-                  DownSmem::sb_bytes(G, RT), bar, pol);
-    bulk_g2s_hint(sB, blob + A.geo.off[2][2] + (long long)blockIdx.x * RT * 16 * G * 2,
-                  DownSmem::sb_bytes(G, RT), bar, pol);
+    if (TMA) {
+      if (lane == 0) tma_load_4d_hint(sA, &tmD, 0, blockIdx.x * RT * 16, 0, slot, bar, pol);
+    } else {
+      const uint8_t* W = blob + A.geo.off[2][0] + (long long)blockIdx.x * RT * 16 * row_bytes;
+      for (int r = lane; r < RT * 16; r += 32)
+        bulk_g2s_hint(sA + r * stride, W + (long long)r * row_bytes, row_bytes, bar, pol);
+    }
+    if (lane < 2)
+      bulk_g2s_hint(lane ? sB : sS, blob + A.geo.off[2][1 + lane] + (long long)blockIdx.x * RT * 16 * G * 2,
+                    DownSmem::sb_bytes(G, RT), bar, pol);
   }
   pdl_wait();                                   // h and its sums come from k_up
   __syncthreads();
@@ -227,7 +247,7 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
     __syncthreads();
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
     if (slot >= 0 && ok && kg0 < kg1) {
-      tile_dot_frags<KPW>(tot, sA + sub * 16 * stride, stride, G, kg0, kg1, g4, c,
+      tile_dot_frags<KPW, TMA>(tot, sA + sub * 16 * (TMA ? 128 : stride), stride, G, kg0, kg1, g4, c,
                          sS + sub * 16 * G, sB + sub * 16 * G, b0, b1,
                          (2 * c < nn) ? s_sums + (2 * c) * G * 2 : nullptr,
                          (2 * c + 1 < nn) ? s_sums + (2 * c + 1) * G * 2 : nullptr);
@@ -288,9 +308,8 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A) {
   }
 }
 
-template <typename Kern>
-static cudaError_t launch_pdl(Kern kern, dim3 grid, int smem, cudaStream_t s, const ExpArgs& a,
-                              bool pdl) {
+template <typename Kern, typename... Args>
+static cudaError_t launch_pdl(Kern kern, dim3 grid, int smem, cudaStream_t s, const Args&... args) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
@@ -302,8 +321,8 @@ static cudaError_t launch_pdl(Kern kern, dim3 grid, int smem, cudaStream_t s, co
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, a);
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 bool expert_shape_ok(int model, int d_model, int d_ff) {
@@ -314,31 +333,46 @@ bool expert_shape_ok(int model, int d_model, int d_ff) {
   return model == 1 ? (G <= 48 && GF <= 48) : (G <= 64 && GF <= 64);
 }
 
-cudaError_t launch_expert(const ExpArgs& a, int max_groups, cudaStream_t s) {
+// The Qwen3 kernels: 2048/768 (up 32 groups, 4 per warp; down 12 groups, 2
+// row tiles per CTA with 4 warps x 3 groups each).
+static bool qwen3_shape(int model, int d_model, int d_ff) {
+  return model == 0 && d_model / 64 <= 32 && d_ff / 64 <= 12 && (d_model / 16) % 2 == 0;
+}
+
+int expert_down_rows(int model, int d_model, int d_ff) {
+  return qwen3_shape(model, d_model, d_ff) ? 32 : 16;
+}
+
+template <int MODEL, int KPW_UP, int KPW_DN, int RT>
+static cudaError_t launch_pair(const ExpArgs& a, int max_groups, cudaStream_t s, const CUtensorMap* maps) {
+  const int K = a.geo.d_model, F = a.geo.d_ff;
+  const dim3 gu(F / 16, max_groups), gd(K / (16 * RT), max_groups);
+  const int su = UpSmem::total(K, maps != nullptr), sd = DownSmem::total(F, RT, maps != nullptr);
+  cudaError_t e;
+  if (maps) {
+    e = launch_pdl(k_up<MODEL, KPW_UP, true>, gu, su, s, a, maps[0], maps[1]);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_down<MODEL, KPW_DN, RT, true>, gd, sd, s, a, maps[2]);
+  }
+  CUtensorMap none{};
+  e = launch_pdl(k_up<MODEL, KPW_UP, false>, gu, su, s, a, none, none);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(k_down<MODEL, KPW_DN, RT, false>, gd, sd, s, a, none);
+}
+
+cudaError_t launch_expert(const ExpArgs& a, int max_groups, cudaStream_t s, const CUtensorMap* maps) {
   if (max_groups <= 0) return cudaSuccess;
   if (!expert_shape_ok(a.geo.model, a.geo.d_model, a.geo.d_ff)) return cudaErrorInvalidValue;
-  const int K = a.geo.d_model, F = a.geo.d_ff, G = K / 64, GF = F / 64;
-  dim3 gu(F / 16, max_groups);
   cudaError_t e;
-  const int su = UpSmem::total(K);
   if (a.geo.model == 1) {
-    // gpt-oss 2880/2880: 45 groups both ways, 6 per warp
-    if (G > 48 || GF > 48) return cudaErrorInvalidValue;
-    e = launch_pdl(k_up<1, 6>, gu, su, s, a, true);
-    if (e != cudaSuccess) return e;
-    e = launch_pdl(k_down<1, 6, 1>, dim3(K / 16, max_groups), DownSmem::total(F, 1), s, a, true);
-  } else if (G <= 32 && GF <= 12 && (K / 16) % 2 == 0) {
-    // Qwen3 2048/768: up 32 groups, 4 per warp; down 12 groups, 2 row tiles
-    // per CTA with 4 warps x 3 groups each
-    e = launch_pdl(k_up<0, 4>, gu, su, s, a, true);
-    if (e != cudaSuccess) return e;
-    e = launch_pdl(k_down<0, 3, 2>, dim3(K / 32, max_groups), DownSmem::total(F, 2), s, a, true);
+    // gpt-oss 2880/2880: 45 groups both ways, 6 per warp (rows of 1440 B
+    // are not whole 128-byte chunks: row copies)
+    e = launch_pair<1, 6, 6, 1>(a, max_groups, s, nullptr);
+  } else if (qwen3_shape(a.geo.model, a.geo.d_model, a.geo.d_ff)) {
+    e = launch_pair<0, 4, 3, 2>(a, max_groups, s, maps);
   } else {
     // other shapes: up to 64 groups, 8 per warp
-    if (G > 64 || GF > 64) return cudaErrorInvalidValue;
-    e = launch_pdl(k_up<0, 8>, gu, su, s, a, true);
-    if (e != cudaSuccess) return e;
-    e = launch_pdl(k_down<0, 8, 1>, dim3(K / 16, max_groups), DownSmem::total(F, 1), s, a, true);
+    e = launch_pair<0, 8, 8, 1>(a, max_groups, s, maps);
   }
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

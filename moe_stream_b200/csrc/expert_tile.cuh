@@ -80,8 +80,21 @@ __device__ __forceinline__ void load_sums(float2* v0, float2* v1, const float* s
   }
 }
 
+// Offset of lane (g4, c)'s 8 weight bytes of quantisation group kg in a
+// 16-row tile at At, rows g4 (hi = 0) or g4 + 8 (hi = 1). Padded layout:
+// rows `stride` bytes apart. Swizzled layout (a 128-byte-swizzled tensor
+// map box of whole rows, [chunk][row][128 B]): `stride` is the chunk stride
+// and the 16-byte unit u of row r sits at u ^ (r mod 8); At is the tile's
+// first row, a multiple of 8 rows into the box.
+template <bool SWZ>
+__device__ __forceinline__ const uint8_t* wrow(const uint8_t* At, int stride, int g4, int hi, int kg, int c) {
+  if (!SWZ) return At + (g4 + 8 * hi) * stride + kg * 32 + 8 * c;
+  return At + (kg >> 2) * stride + (g4 + 8 * hi) * 128 + (((((kg & 3) << 1) | (c >> 1)) ^ g4) << 4) +
+         ((c & 1) << 3);
+}
+
 // The dot product with fragments and sums already in registers.
-template <int KPW>
+template <int KPW, bool SWZ = false>
 __device__ __forceinline__ void tile_dot_regs(float* tot, const uint8_t* At, int stride, int G,
                                               int kg0, int kg1, int g4, int c, const uint16_t* sS,
                                               const uint16_t* sB, const uint4* b0, const uint4* b1,
@@ -89,9 +102,9 @@ __device__ __forceinline__ void tile_dot_regs(float* tot, const uint8_t* At, int
 #pragma unroll
   for (int q = 0; q < KPW; ++q) {
     const int kg = kg0 + q;
-    if (kg >= kg1) break;
-    const uint2 ra = *reinterpret_cast<const uint2*>(At + g4 * stride + kg * 32 + 8 * c);
-    const uint2 rb = *reinterpret_cast<const uint2*>(At + (g4 + 8) * stride + kg * 32 + 8 * c);
+    if (kg >= kg1) continue;
+    const uint2 ra = *reinterpret_cast<const uint2*>(wrow<SWZ>(At, stride, g4, 0, kg, c));
+    const uint2 rb = *reinterpret_cast<const uint2*>(wrow<SWZ>(At, stride, g4, 1, kg, c));
     float cc[4] = {0.f, 0.f, 0.f, 0.f};
     mma_group(cc, ra, rb, b0[q], b1[q]);
     const float xs0 = v0[q].x, xp0 = v0[q].y, xs1 = v1[q].x, xp1 = v1[q].y;
@@ -107,7 +120,7 @@ __device__ __forceinline__ void tile_dot_regs(float* tot, const uint8_t* At, int
 // tile_dot_regs with each group's sums read from sum_c0 / sum_c1 (shared
 // memory) as the loop reaches it: fewer live registers than load_sums up
 // front, the same arithmetic in the same order.
-template <int KPW>
+template <int KPW, bool SWZ = false>
 __device__ __forceinline__ void tile_dot_frags(float* tot, const uint8_t* At, int stride, int G,
                                                int kg0, int kg1, int g4, int c, const uint16_t* sS,
                                                const uint16_t* sB, const uint4* b0, const uint4* b1,
@@ -115,9 +128,9 @@ __device__ __forceinline__ void tile_dot_frags(float* tot, const uint8_t* At, in
 #pragma unroll
   for (int q = 0; q < KPW; ++q) {
     const int kg = kg0 + q;
-    if (kg >= kg1) break;
-    const uint2 ra = *reinterpret_cast<const uint2*>(At + g4 * stride + kg * 32 + 8 * c);
-    const uint2 rb = *reinterpret_cast<const uint2*>(At + (g4 + 8) * stride + kg * 32 + 8 * c);
+    if (kg >= kg1) continue;
+    const uint2 ra = *reinterpret_cast<const uint2*>(wrow<SWZ>(At, stride, g4, 0, kg, c));
+    const uint2 rb = *reinterpret_cast<const uint2*>(wrow<SWZ>(At, stride, g4, 1, kg, c));
     float cc[4] = {0.f, 0.f, 0.f, 0.f};
     mma_group(cc, ra, rb, b0[q], b1[q]);
     float xs0 = 0.f, xp0 = 0.f, xs1 = 0.f, xp1 = 0.f;
@@ -136,9 +149,11 @@ struct UpSmem {
   static __host__ __device__ int stride(int K) { return padded_stride(K / 2); }
   static __host__ __device__ int a_bytes(int K) { return 16 * stride(K); }
   static __host__ __device__ int sb_bytes(int G) { return 16 * G * 2; }
-  static __host__ __device__ int total(int K) {
+  // tma: dense rows in 128-byte-swizzled boxes, 1 KB of alignment slack
+  static __host__ __device__ int total(int K, bool tma) {
     const int G = K / 64;
-    return 2 * a_bytes(K) + 4 * sb_bytes(G) + EX_WARPS * 2 * 4 * 32 * 4 + 16;
+    const int a = tma ? 16 * (K / 2) : a_bytes(K);
+    return 2 * a + 4 * sb_bytes(G) + EX_WARPS * 2 * 4 * 32 * 4 + 16 + (tma ? 1024 : 0);
   }
 };
 
@@ -146,9 +161,10 @@ struct DownSmem {
   static __host__ __device__ int stride(int F) { return padded_stride(F / 2); }
   static __host__ __device__ int a_bytes(int F, int RT) { return RT * 16 * stride(F); }
   static __host__ __device__ int sb_bytes(int GF, int RT) { return RT * 16 * GF * 2; }
-  static __host__ __device__ int total(int F, int RT) {
+  static __host__ __device__ int total(int F, int RT, bool tma) {
     const int GF = F / 64;
-    return a_bytes(F, RT) + 2 * sb_bytes(GF, RT) + EX_WARPS * 4 * 32 * 4 + 8 * GF * 2 * 4 + 16;
+    const int a = tma ? RT * 16 * (F / 2) : a_bytes(F, RT);
+    return a + 2 * sb_bytes(GF, RT) + EX_WARPS * 4 * 32 * 4 + 8 * GF * 2 * 4 + 16 + (tma ? 1024 : 0);
   }
 };
 

@@ -33,9 +33,11 @@ __device__ __forceinline__ uint32_t lop_or(uint32_t u, uint32_t mask) {
   return r;
 }
 
+// Not volatile: the MMA is a pure function of its operands, so the compiler
+// may interleave the independent accumulation chains of different groups.
 __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])

@@ -772,6 +772,27 @@ int encode_weight_map(CUtensorMap* m, const void* base, int K, int rows_out, int
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS ? 0 : -2;
 }
 
+// 4-bit weight rows of one projection across all slots, for the decode
+// kernels: dims (innermost first) 128 bytes, rows_out rows (stride
+// row_bytes), row_bytes / 128 chunks (stride 128 B), n_slots slots (stride
+// blob); boxes of box_rows whole rows, 128-byte swizzled, so a tile lands in
+// shared memory as [chunk][row][128 B] with the 16-byte units of row r XORed
+// with r mod 8 (bank-conflict-free fragment reads).
+int encode_rows_map(CUtensorMap* m, const void* base, int row_bytes, int rows_out, int n_slots,
+                    long long blob, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return -1;
+  if (row_bytes % 128 || row_bytes / 128 > 256 || box_rows > 256 || rows_out % box_rows) return -3;
+  const cuuint64_t dims[4] = {128, (cuuint64_t)rows_out, (cuuint64_t)(row_bytes / 128),
+                              (cuuint64_t)n_slots};
+  const cuuint64_t strides[3] = {(cuuint64_t)row_bytes, 128, (cuuint64_t)blob};
+  const cuuint32_t box[4] = {128, (cuuint32_t)box_rows, (cuuint32_t)(row_bytes / 128), 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS ? 0 : -2;
+}
+
 // ---------------------------------------------------------------- launchers
 cudaError_t launch_scatter(const ScatterArgs& a, int grid, cudaStream_t s) {
   k_scatter<<<grid, 256, 0, s>>>(a);

@@ -209,7 +209,15 @@ cudaError_t launch_pool_op(const DevTable& t, const PoolReq& r, int* slots_out, 
                            cudaStream_t s);
 cudaError_t launch_fill(const FillArgs& f, int grid, cudaStream_t s);
 cudaError_t launch_mlp_prep(const MlpPrepArgs& a, cudaStream_t s);
-cudaError_t launch_expert(const ExpArgs& a, int max_groups, cudaStream_t s);
+// The decode expert kernels. maps: null, or the tensor maps of the gate, up
+// and down weight rows over the arena (encode_rows_map with 16, 16 and the
+// down kernel's rows per tile), which replace the per-row copies.
+cudaError_t launch_expert(const ExpArgs& a, int max_groups, cudaStream_t s,
+                          const CUtensorMap* maps = nullptr);
+// Rows per tensor-map box of the down kernel for this shape (0: no map path).
+int expert_down_rows(int model, int d_model, int d_ff);
+int encode_rows_map(CUtensorMap* m, const void* base, int row_bytes, int rows_out, int n_slots,
+                    long long blob, int box_rows);
 
 // Message returned by the next ms_last_error() on this thread.
 void set_error_message(const char* msg);

@@ -52,6 +52,18 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, unsign
       : "memory");
 }
 
+// Tiled 4-D tensor copy global -> this CTA's shared memory (no multicast),
+// completing on `bar`, with an L2 cache policy.
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const void* tmap, int x, int y, int z, int w,
+                                                 uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar)),
+      "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned phase) {
   uint32_t ok;
   asm volatile(
