@@ -208,6 +208,14 @@ int ms_pool_state_bytes(ms_pool* pool, int with_arena, size_t* bytes);
 int ms_pool_save_state(ms_pool* pool, void* dev_buf, int with_arena, void* stream);
 int ms_pool_load_state(ms_pool* pool, const void* dev_buf, int with_arena, void* stream);
 
+/* Failure-detection self-test, no reference counterpart: enqueues on
+ * `stream` one CTA that waits, with the same bounded wait every kernel of the
+ * library uses but a limit of limit_ns (at most 2 s), on an mbarrier that
+ * never completes. The wait gives up and records MS_E_TIMEOUT in the pool's
+ * sticky status, which the next ms_pool_status reports and clears; nothing
+ * else changes and the pool stays usable. */
+int ms_pool_selftest_wait(ms_pool* pool, long long limit_ns, void* stream);
+
 /* Diagnostic with no reference counterpart: the SASS target the library's
  * kernels carry for `device` (cudaFuncAttributes.binaryVersion of one of
  * them; 100 for sm_100a). */

@@ -1067,6 +1067,16 @@ int ms_pool_load_state(ms_pool* p, const void* dev_buf, int with_arena, void* st
                     false);
 }
 
+int ms_pool_selftest_wait(ms_pool* p, long long limit_ns, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (limit_ns <= 0 || limit_ns > 2000000000LL)
+    return fail(MS_E_INVALID, "limit_ns must be in (0, 2e9]");
+  CK(cudaSetDevice(p->device));
+  CK(launch_wait_selftest((unsigned long long)limit_ns, &p->tab.ctr->status,
+                          static_cast<cudaStream_t>(stream)));
+  return MS_OK;
+}
+
 int ms_kernel_arch(int device, int* binary_version) {
   if (!binary_version) return fail(MS_E_INVALID, "binary_version is NULL");
   int ndev = 0;

@@ -188,6 +188,9 @@ struct EpPackArgs {
 cudaError_t launch_mlp_wide_prep(const MlpWideArgs& a, int sms, cudaStream_t s);
 cudaError_t launch_ep_pack(const EpPackArgs& a, int sms, cudaStream_t s);
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s);
+// One CTA waits (bounded, limit_ns) on an mbarrier whose phase never
+// completes and records MS_E_TIMEOUT in *status.
+cudaError_t launch_wait_selftest(unsigned long long limit_ns, int* status, cudaStream_t s);
 // Attributes of the route-step kernel (its binaryVersion is the SASS target).
 cudaError_t route_step_attributes(cudaFuncAttributes* attr);
 cudaError_t route_prefer_shared();

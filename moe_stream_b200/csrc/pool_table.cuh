@@ -454,6 +454,125 @@ __device__ __forceinline__ bool warp_acquire_resident(const DevTable& T, OpCtx* 
   return true;
 }
 
+// The whole table step of a block call -- prefetch of `np_` keys (one
+// prefetch depth), then acquire of `na` keys, both sorted and distinct -- in
+// the common case where no key needs a slot: every predicted key is resident
+// or pending and every acquired key too. Then no slot changes hands and the
+// reference's loops (prefetch engine_v3.py:383-396, acquire :398-454, the
+// completion of the earlier prefetches at the end of the acquire) reduce to
+// independent per-key updates: one round of loads (key states, counters, the
+// previous pin list, the pending list), then stores. The use clock is
+// reproduced by rank, as in warp_acquire_resident. Returns false, having
+// written nothing, when some key needs a slot (or a list is longer than a
+// warp): the caller then runs the sequential walk.
+__device__ __forceinline__ bool warp_table_fast(const DevTable& T, const int* pkeys, int np_,
+                                                const int* akeys, int na, int* slots_out,
+                                                int lane) {
+  if (np_ > 32 || na > 32) return false;
+  // ---- one round of independent loads
+  int ps = 0, as = -1, afr = 0, pin = -1, pend = -1;
+  uint8_t pf = 0, af = 0;
+  const int pk = lane < np_ ? pkeys[lane] : -1;
+  const int ak = lane < na ? akeys[lane] : -1;
+  if (pk >= 0) {
+    ps = T.slot_of[pk];
+    pf = T.kflags[pk];
+  }
+  if (ak >= 0) {
+    as = T.slot_of[ak];
+    af = T.kflags[ak];
+    afr = T.freq[ak];
+  }
+  if (lane < T.n_slots) {
+    pin = T.pin_list[lane];
+    pend = T.pend_list[lane];
+  }
+  long long uc0 = 0;
+  int n_pin = 0, n_pend = 0;
+  if (lane == 0) {
+    uc0 = T.ctr->use_clock;
+    n_pin = T.ctr->n_pin;
+    n_pend = T.ctr->n_pend;
+  }
+  uc0 = __shfl_sync(MS_FULL, uc0, 0);
+  n_pin = __shfl_sync(MS_FULL, n_pin, 0);
+  n_pend = __shfl_sync(MS_FULL, n_pend, 0);
+  // ---- the common case?
+  const bool p_need = pk >= 0 && ps < 0 && !(pf & KF_PENDING);
+  const bool a_pend = ak >= 0 && (af & KF_PENDING) != 0;
+  const bool a_need = ak >= 0 && !a_pend && as < 0;
+  if (__any_sync(MS_FULL, p_need || a_need) || n_pin > 32 || n_pend > 32) return false;
+  // ---- acquire: every item touched in item order, then each waited-on
+  // pending item once more, in item order (engine_v3.py:412-446)
+  const unsigned lt = (1u << lane) - 1u;
+  const unsigned pb = __ballot_sync(MS_FULL, a_pend);
+  const int n_wait = __popc(pb);
+  int n_pf = 0, n_cache = 0, n_reads = 0;
+  if (ak >= 0) {
+    long long uc = uc0 + lane + 1;
+    uint8_t f = af;
+    int uses = 1;
+    if (!a_pend) {
+      if (f & KF_FROMPF) {                     // first use of a prefetched key (:431-435)
+        f = (uint8_t)(f & ~KF_FROMPF);
+        ++n_pf;
+      } else {
+        ++n_cache;
+      }
+    } else {                                   // waited on, touched again (:438-446)
+      uc = uc0 + na + __popc(pb & lt) + 1;
+      uses = 2;
+      f = (uint8_t)(f & ~(KF_PENDING | KF_FROMPF));
+      ++n_reads;
+      ++n_pf;
+    }
+    if (f != af) T.kflags[ak] = f;
+    T.last_use[ak] = uc;                       // _touch (:376-380)
+    T.freq[ak] = afr + uses;
+    slots_out[lane] = as;
+  }
+  // ---- pinned = set(slots) (:452-453): the previous pins go, this call's
+  // slots come (distinct keys, distinct slots)
+  if (lane < n_pin) T.pinned[pin] = 0;
+  __syncwarp();
+  if (ak >= 0) {
+    T.pinned[as] = 1;
+    T.pin_list[lane] = as;
+  }
+  // ---- the earlier prefetches that were not waited on complete now:
+  // pending -> from_prefetch (a pending key's flags are exactly PENDING)
+  bool waited = false;
+  for (int i = 0; i < na; ++i) {
+    const int ki = __shfl_sync(MS_FULL, ak, i);
+    waited |= (ki == pend) && ((pb >> i) & 1u);
+  }
+  int n_done = 0;
+  if (lane < n_pend && !waited) {
+    T.kflags[pend] = KF_FROMPF;
+    n_done = 1;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    n_pf += __shfl_xor_sync(MS_FULL, n_pf, o);
+    n_cache += __shfl_xor_sync(MS_FULL, n_cache, o);
+    n_reads += __shfl_xor_sync(MS_FULL, n_reads, o);
+    n_done += __shfl_xor_sync(MS_FULL, n_done, o);
+  }
+  if (lane == 0) {
+    TableCtr* c = T.ctr;
+    c->use_clock = uc0 + na + n_wait;
+    c->n_pend = 0;
+    c->n_pin = na;
+    c->n_fill = 0;
+    c->n_fill_pf = 0;
+    c->st[ST_PREFETCH] += n_pf;
+    c->st[ST_CACHE] += n_cache;
+    c->st[ST_READS] += n_reads + n_done;
+  }
+  __syncwarp();
+  return true;
+}
+
 // acquire (engine_v3.py:398-454) of request r. slots_out[i] receives the
 // slot of item i (-1 if exhausted before it was placed). waits: scratch of
 // r.n ints. Returns 0 or MS_E_EXHAUSTED (-3).

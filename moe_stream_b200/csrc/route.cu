@@ -14,6 +14,7 @@
 #include "pool_table.cuh"
 #include "groups.cuh"
 #include "frag.cuh"
+#include "tma.cuh"
 #include "kernels.h"
 
 namespace ms {
@@ -121,6 +122,19 @@ __device__ __forceinline__ void warp_pool_step(const RouteArgs& A, int (*s_pred)
                                                int* s_slots, int* s_waits, OpCtx* s_op, KeyCache* s_kc,
                                                int (*s_ci)[MAX_E], int lane) {
   const DevTable& Tb = A.tab;
+  if (A.n_pred <= 1) {
+    // the common case (no key needs a slot) in one round of loads
+    int* keys = s_ci[0];                       // [0, np): predicted keys, [32, 32 + na): acquired
+    const int np_ = A.n_pred ? s_n_pred[0] : 0;
+    for (int i = lane; i < np_ && i < 32; i += 32) keys[i] = A.pred_layer[0] * Tb.n_experts + s_pred[0][i];
+    for (int i = lane; i < n_acq && i < 32; i += 32) keys[32 + i] = A.layer * Tb.n_experts + s_acq[i];
+    __syncwarp();
+    if (warp_table_fast(Tb, keys, np_, keys + 32, n_acq, s_slots, lane)) {
+      if (A.pf_ring && lane == 0) *A.pf_cnt = 0;
+      __syncwarp();
+      return;
+    }
+  }
   op_load(Tb, s_op, lane);
   if (lane == 0) s_kc->n = 0;
   __syncwarp();
@@ -705,6 +719,28 @@ cudaError_t route_prefer_shared() {
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+// Self-test of the bounded waits: an mbarrier that expects two arrivals gets
+// one, so its phase never completes; every thread waits on it with the
+// bounded wait the kernels use (a limit of limit_ns), which must give up,
+// record MS_E_TIMEOUT in *status and return. No copy is in flight, so
+// nothing is left pending when the CTA exits.
+__global__ void k_wait_selftest(unsigned long long limit_ns, int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 2);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&bar)) : "memory");
+  mbar_wait_ns(&bar, 0, status, limit_ns);
+}
+
+cudaError_t launch_wait_selftest(unsigned long long limit_ns, int* status, cudaStream_t s) {
+  k_wait_selftest<<<1, 32, 0, s>>>(limit_ns, status);
+  return cudaGetLastError();
 }
 
 cudaError_t route_step_attributes(cudaFuncAttributes* attr) {

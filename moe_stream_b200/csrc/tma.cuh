@@ -100,15 +100,20 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, unsigned phas
 // Bounded wait for phase `phase` of `bar`: suspending polls, at most
 // MBAR_SPIN_LIMIT of them and MBAR_WAIT_NS of wall time. Returns false (and
 // sets *status to MS_E_TIMEOUT once) if either limit ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, int* status) {
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, unsigned phase, int* status,
+                                             unsigned long long limit_ns) {
   if (mbar_try_wait(bar, phase)) return true;
   const unsigned long long t0 = global_ns();
   for (unsigned i = 0; i < MBAR_SPIN_LIMIT; ++i) {
     if (mbar_try_wait_sleep(bar, phase, 100000u)) return true;
-    if (global_ns() - t0 > MBAR_WAIT_NS) break;
+    if (global_ns() - t0 > limit_ns) break;
   }
   if (status) atomicCAS(status, 0, -4);
   return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, int* status) {
+  return mbar_wait_ns(bar, phase, status, MBAR_WAIT_NS);
 }
 
 // True once any wait of this call chain has timed out: later CTAs then skip

@@ -172,3 +172,46 @@ def test_plan_placement_balances_and_covers():
             assert slots[table[e, 1 + 2 * j]][table[e, 2 + 2 * j]] == e
     load = [sum(counts[e] / table[e, 0] for e in r) for r in slots]
     assert max(load) <= 1.1 * counts.sum() / 4
+
+
+def _withholding_rank(rank, world, port, out_dir):
+    """Rank 1 never sends its pair counts (it stops before the first
+    exchange, as a failed rank would); rank 0 must get an error from the
+    process group's timeout instead of waiting forever."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    geom = _geom()
+    w, b, x, blobs = _inputs(geom, 8)
+    result = os.path.join(out_dir, "rank0.txt")
+    if rank == 0:
+        from moe_stream_b200.ep import ep_forward
+        ops = OracleOps(geom, rank, world, w, b, blobs)
+        t0 = time.monotonic()
+        try:
+            ep_forward(x[:4], ops, world)
+            msg = "completed"
+        except RuntimeError as e:
+            msg = f"error after {time.monotonic() - t0:.1f} s: {type(e).__name__}: {e}"
+        with open(result + ".tmp", "w") as f:
+            f.write(msg)
+        os.replace(result + ".tmp", result)
+    else:
+        # the failed rank: no collective at all; it leaves once rank 0 has
+        # recorded what it saw (at most 60 s)
+        t0 = time.monotonic()
+        while not os.path.exists(result) and time.monotonic() - t0 < 60:
+            time.sleep(0.1)
+    # no destroy_process_group: its barrier would wait on the broken group
+
+
+def test_ep_rank_that_withholds_its_counts_times_out(tmp_path):
+    mp.start_processes(_withholding_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       start_method="spawn")
+    msg = (tmp_path / "rank0.txt").read_text()
+    assert msg.startswith("error after"), msg
+    secs = float(msg.split()[2])
+    assert 2.0 <= secs <= 30.0, msg

@@ -143,3 +143,41 @@ def test_bad_arguments_raise(lib, cuda):
             pool._read(8, 0, 0)                  # slot out of range
     finally:
         pool.close()
+
+
+def test_bounded_wait_reports_timeout_and_pool_recovers(lib, cuda):
+    """Failure detection without a GPU fault: a CTA waits, with the bounded
+    wait every kernel uses, on an mbarrier that never completes. The wait
+    gives up after its limit, ms_pool_status reports MS_E_TIMEOUT once, and
+    the pool then serves a block call as before."""
+    import ctypes
+    import time
+    from moe_stream_b200 import _lib, store as S
+    from moe_stream_b200.block import MoEBlock
+    from moe_stream_b200.pool import ExpertPool
+    geom = geometry.qwen3(1)
+    pool = ExpertPool(geom, geom.n_experts, depths=(), max_tokens=1)
+    try:
+        st = pool.alloc_store()
+        torch.from_numpy(st).view(geom.n_keys, geom.blob_bytes).copy_(
+            S.make_layer_blobs(geom, 2, 0, device="cuda").cpu())
+        blk = MoEBlock(pool, 0, *S.router_weights(geom, 2, 0))
+        x = S.rms_norm_tokens(1, geom.d_model, seed=3, device="cuda")
+        y0 = blk(x).clone()
+        pool.status()
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        t0 = time.monotonic()
+        assert lib.ms_pool_selftest_wait(pool._h, 50_000_000, stream) == _lib.MS_OK
+        with pytest.raises(_lib.MoeStreamError) as err:
+            pool.status()
+        waited = time.monotonic() - t0
+        assert err.value.code == _lib.MS_E_TIMEOUT
+        assert 0.04 <= waited < 5.0
+        pool.status()                             # reported once, then cleared
+        torch.cuda.synchronize()
+        # the same call again: same result (the block is deterministic)
+        y1 = blk(x)
+        pool.status()
+        assert torch.equal(y0, y1)
+    finally:
+        pool.close()
