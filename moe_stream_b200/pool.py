@@ -122,18 +122,26 @@ class ExpertPool:
         return arr
 
     @classmethod
-    def open(cls, model_dir, model, d_model, d_ff, n_slots, **kw):
+    def open(cls, model_dir, model, d_model, d_ff, n_slots, cold=False, **kw):
         """Pool over an on-disk store (experts_index.json + experts.bin,
-        repack.py:137-146): the whole file is read once into pinned memory."""
+        repack.py:137-146): the whole file is read once into the pinned,
+        device-mapped store with preadv (engine_v3.py:255-290). cold=True
+        reads with O_DIRECT, past the OS page cache -- the Linux form of the
+        reference's F_NOCACHE cold-cache mode (engine_v3.py:138-142); the
+        pinned store is page aligned and blobs are whole 16 KiB pages, as
+        O_DIRECT requires. A filesystem without O_DIRECT raises OSError."""
         idx = json.load(open(os.path.join(model_dir, "experts_index.json")))
         geom = from_index(idx, model, d_model, d_ff)
-        pool = cls(geom, n_slots, **kw)
         path = os.path.join(model_dir, "experts.bin")
         size = os.path.getsize(path)
+        if size % geom.blob_bytes:
+            raise IOError(f"{path}: {size} bytes is not a whole number of {geom.blob_bytes}-byte blobs")
         n_blobs = size // geom.blob_bytes
-        store = pool.alloc_store(n_blobs)
-        fd = os.open(path, os.O_RDONLY)
+        flags = os.O_RDONLY | (os.O_DIRECT if cold else 0)
+        fd = os.open(path, flags)
         try:
+            pool = cls(geom, n_slots, **kw)
+            store = pool.alloc_store(n_blobs)
             mv = memoryview(store)
             off, step = 0, 1 << 28
             while off < n_blobs * geom.blob_bytes:
@@ -144,6 +152,15 @@ class ExpertPool:
         finally:
             os.close(fd)
         return pool
+
+    def write_store(self, model_dir):
+        """Write the attached store as experts.bin + experts_index.json in the
+        reference's on-disk format (repack.py:137-146), readable by open()."""
+        os.makedirs(model_dir, exist_ok=True)
+        with open(os.path.join(model_dir, "experts_index.json"), "w") as f:
+            json.dump(self.geom.index(), f, indent=2)
+        with open(os.path.join(model_dir, "experts.bin"), "wb") as f:
+            f.write(memoryview(self.store))
 
     # ------------------------------------------------------------- views
     def _make_views(self):

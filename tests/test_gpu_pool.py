@@ -181,3 +181,39 @@ def test_bounded_wait_reports_timeout_and_pool_recovers(lib, cuda):
         assert torch.equal(y0, y1)
     finally:
         pool.close()
+
+
+@pytest.mark.parametrize("cold", [False, True])
+def test_open_reads_a_store_in_the_reference_format(cold, lib, cuda, tmp_path):
+    """ExpertPool.open on experts.bin + experts_index.json as repack.py
+    writes them (repack.py:137-146): the store holds the file byte for byte,
+    and acquired slots hold their blobs (verify_pool.py:64-76). cold=True
+    reads with O_DIRECT."""
+    from moe_stream_b200.pool import ExpertPool
+    geom = geometry.make("qwen3", 128, 64, 8, 2, 2)
+    src = ExpertPool(geom, 2, max_tokens=1)
+    try:
+        pattern_store(src)
+        src.write_store(str(tmp_path))
+    finally:
+        src.close()
+    raw = np.fromfile(tmp_path / "experts.bin", dtype=np.uint8)
+    idx = json.load(open(tmp_path / "experts_index.json"))
+    assert idx["offset_formula"] == "(layer * n_experts + expert) * blob_bytes"
+    try:
+        pool = ExpertPool.open(str(tmp_path), "qwen3", geom.d_model, geom.d_ff, 6,
+                               cold=cold, max_tokens=1)
+    except OSError as e:
+        if cold:
+            pytest.skip(f"no O_DIRECT on this filesystem: {e}")
+        raise
+    try:
+        assert pool.geom.blob_bytes == geom.blob_bytes and pool.geom.n_keys == geom.n_keys
+        assert np.array_equal(pool.store, raw)
+        slots = pool.acquire(1, [3, 5, 7])
+        torch.cuda.synchronize()
+        for e, s in zip((3, 5, 7), slots):
+            key = 1 * geom.n_experts + e
+            assert np.array_equal(arena_bytes(pool, s), raw[key * pool.blob:(key + 1) * pool.blob])
+    finally:
+        pool.close()
