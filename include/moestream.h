@@ -33,6 +33,10 @@ extern "C" {
 #define MS_E_STATE       -6   /* call not valid in the handle's current state      */
 #define MS_E_IO          -7   /* store read out of range / short (IOError,
                                  engine_v3.py:283-284)                             */
+#define MS_E_RANGE       -8   /* an activation (x, or the SwiGLU output h) beyond
+                                 the fp16 range (|v| > 65504) reached the fp16
+                                 tensor-core operands; that call's output is
+                                 not valid                                         */
 
 /* ------------------------------------------------------------- enumerations */
 #define MS_MODEL_QWEN3    0   /* engine_v3.py: softmax over E, top-k, renormalise  */

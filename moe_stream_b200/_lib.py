@@ -17,6 +17,7 @@ MS_E_TIMEOUT = -4
 MS_E_NOMEM = -5
 MS_E_STATE = -6
 MS_E_IO = -7
+MS_E_RANGE = -8
 
 MODEL_QWEN3, MODEL_GPTOSS = 0, 1
 EVICT = {"lfu": 0, "lru": 1, "asis": 2}

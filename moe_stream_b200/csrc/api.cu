@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "../../include/moestream.h"
+#include "host_wait.h"
 #include "kernels.h"
 
 using namespace ms;
@@ -32,6 +33,19 @@ int fail(int code, const char* fmt, ...) {
 #define CK(call)                                                                       \
   do {                                                                                 \
     cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      return fail(MS_E_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                  __FILE__, __LINE__);                                                 \
+  } while (0)
+
+// A host wait on the device (stream_wait_bounded / event_wait_bounded):
+// MS_E_TIMEOUT when it ran past the host limit, MS_E_CUDA for a CUDA error.
+#define HWAIT(call)                                                                    \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ == cudaErrorTimeout)                                                        \
+      return fail(MS_E_TIMEOUT, "%s: the device did not finish within %.0f s "         \
+                  "(MS_HOST_WAIT_S)", #call, host_wait_limit_s());                     \
     if (e_ != cudaSuccess)                                                             \
       return fail(MS_E_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
                   __FILE__, __LINE__);                                                 \
@@ -502,7 +516,7 @@ static int join_side(ms_pool* p, cudaStream_t s) {
   if (cap == p->pf_captured && (!cap || id == p->pf_capture_id)) {
     CK(cudaStreamWaitEvent(s, p->ev_pf[p->pf_slot], 0));
   } else if (!p->pf_captured) {
-    CK(cudaEventSynchronize(p->ev_pf[p->pf_slot]));
+    HWAIT(event_wait_bounded(p->ev_pf[p->pf_slot]));
   } else {
     // a capture that ended without joining its fork cannot be waited for
     // from here; report it once and forget the fork
@@ -575,7 +589,7 @@ int ms_pool_acquire(ms_pool* p, int layer, const int32_t* experts, int n, int32_
   if (rc) return rc;
   if (n > 0) CK(cudaMemcpyAsync(p->h_pinned, p->d_slots, sizeof(int) * n, cudaMemcpyDeviceToHost, s));
   CK(cudaMemcpyAsync(p->h_pinned + MS_MAX_REQ, p->d_opstatus, sizeof(int), cudaMemcpyDeviceToHost, s));
-  CK(cudaStreamSynchronize(s));
+  HWAIT(stream_wait_bounded(s));
   if (p->h_pinned[MS_MAX_REQ] == MS_E_EXHAUSTED)
     return fail(MS_E_EXHAUSTED, "pool exhausted: every slot pinned or pending");
   for (int i = 0; i < n; ++i) slots_out[i] = p->h_pinned[i];
@@ -755,6 +769,7 @@ static int wide_experts(ms_pool* p, const void* x, int T, int k, const int* keys
   sa.perm_score = p->perm_score;
   sa.inv = p->inv;
   sa.pair_slot = pair_slot;
+  sa.status = &p->tab.ctr->status;
   CK(launch_scatter(sa, std::min((P + 7) / 8, p->sm_count * 8), s));
   GemmArgs g{};
   g.model = p->geo.model;
@@ -873,7 +888,7 @@ int ms_pool_status(ms_pool* p, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CK(cudaSetDevice(p->device));
   if (int rc = join_side(p, s)) return rc;
-  CK(cudaStreamSynchronize(s));
+  HWAIT(stream_wait_bounded(s));
   int st = 0, st_pf = 0;
   CK(cudaMemcpy(&st, &p->tab.ctr->status, sizeof(int), cudaMemcpyDeviceToHost));
   CK(cudaMemcpy(&st_pf, p->pf_cnt + 2, sizeof(int), cudaMemcpyDeviceToHost));
@@ -882,6 +897,9 @@ int ms_pool_status(ms_pool* p, void* stream) {
   CK(cudaMemcpy(p->pf_cnt + 2, &zero, sizeof(int), cudaMemcpyHostToDevice));
   if (!st) st = st_pf;
   if (st == MS_E_EXHAUSTED) return fail(st, "pool exhausted: every slot pinned or pending");
+  if (st == MS_E_RANGE)
+    return fail(st, "an activation beyond the fp16 range (|v| > 65504) reached the expert "
+                    "kernels in an earlier block call; its output is not valid");
   if (st) return fail(st, "device-side error %d in an earlier block call", st);
   return MS_OK;
 }
@@ -1011,7 +1029,7 @@ int ms_pool_timing(ms_pool* p, int layer, float* out3) {
   if (p->prof_ev.empty()) return fail(MS_E_STATE, "profiling was never enabled");
   if (layer < 0 || layer >= p->geom.n_layers) return fail(MS_E_INVALID, "layer out of range");
   cudaEvent_t* ev = &p->prof_ev[(size_t)layer * 4];
-  CK(cudaEventSynchronize(ev[3]));
+  HWAIT(event_wait_bounded(ev[3]));
   for (int i = 0; i < 3; ++i) CK(cudaEventElapsedTime(&out3[i], ev[i], ev[i + 1]));
   return MS_OK;
 }

@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2)
           } else {
             h = silu_mul(gv, uv);
           }
+          if (fabsf(h) > F16_MAX) atomicCAS(A.status, 0, ST_E_RANGE);
           const __half hh = __float2half_rn(h);
           hsc = (row & 1) ? __hmul(hh, __float2half(0.0625f)) : hh;
           hh_f = __half2float(hh);

@@ -73,9 +73,14 @@ __device__ __forceinline__ long long frag_off(long long r, int G, int k) {
 // 16-byte B-operand block of lane w>>1, pass w&1, so one thread writes one
 // uint4. The group's sums (X, X') are reduced over the 8 lanes that handle
 // words 0..7 (aligned octet of the warp, all active) and written by word 0.
-__device__ __forceinline__ void frag_write_word(const uint16_t* src8, __half* frag, float* sums,
+// Returns true when one of the 8 values lies beyond the fp16 range. (Values
+// below fp16's normal range, 2^-14, or 2^-10 at the odd positions, keep an
+// absolute precision of 2^-24 (2^-20 before the division by 16): far below
+// a bf16 output ulp, so they are not flagged.)
+__device__ __forceinline__ bool frag_write_word(const uint16_t* src8, __half* frag, float* sums,
                                                 long long r, int G, int kg, int w, bool valid) {
   float xs = 0.f, xp = 0.f;
+  bool over = false;
   if (valid) {
     const uint4 v = *reinterpret_cast<const uint4*>(src8);
     const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
@@ -83,7 +88,9 @@ __device__ __forceinline__ void frag_write_word(const uint16_t* src8, __half* fr
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const uint16_t b = (uint16_t)((w4[i >> 1] >> ((i & 1) * 16)) & 0xffffu);
-      const __half x = __float2half_rn(bf2f(b));
+      const float xf = bf2f(b);
+      over |= fabsf(xf) > F16_MAX;
+      const __half x = __float2half_rn(xf);
       const __half xs_ = (i & 1) ? __hmul(x, __float2half(0.0625f)) : x;
       xs += __half2float(x);
       xp += __half2float(xs_);
@@ -105,21 +112,26 @@ __device__ __forceinline__ void frag_write_word(const uint16_t* src8, __half* fr
     sums[(r * G + kg) * 2] = xs;
     sums[(r * G + kg) * 2 + 1] = xp;
   }
+  return over;
 }
 
 // Frag layout of rows [0, T) of x (bf16 [T, d]) by the calling threads:
 // thread index `tid` of `nthreads` (a multiple of 32), grid-stride.
+// Records ST_E_RANGE in *status (first error wins) when a value of x lies
+// beyond the fp16 range.
 __device__ __forceinline__ void frag_write_rows(const uint16_t* x, int T, int d, __half* frag,
-                                                float* sums, int tid, int nthreads) {
+                                                float* sums, int tid, int nthreads, int* status) {
   const int G = d / 64;
   const int tasks = T * G * 8;
   const int rounded = (tasks + 31) & ~31;
+  bool over = false;
   for (int i = tid; i < rounded; i += nthreads) {
     const bool valid = i < tasks;
     const int grp = valid ? (i >> 3) : 0, w = i & 7;
     const int t = grp / G, kg = grp % G;
-    frag_write_word(x + (long long)t * d + kg * 64 + w * 8, frag, sums, t, G, kg, w, valid);
+    over |= frag_write_word(x + (long long)t * d + kg * 64 + w * 8, frag, sums, t, G, kg, w, valid);
   }
+  if (over) atomicCAS(status, 0, ST_E_RANGE);
 }
 
 }  // namespace ms

@@ -203,6 +203,13 @@ __device__ __forceinline__ uint32_t h2_bits(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// Either bf16 of a pair beyond the fp16 range: |v| > 65504 <=> magnitude
+// bits above 0x477f (65280, the largest bf16 below 65504), inf and NaN
+// included.
+__device__ __forceinline__ bool bf16x2_beyond_f16(uint32_t v) {
+  return (v & 0x7fffu) > 0x477fu || ((v >> 16) & 0x7fffu) > 0x477fu;
+}
+
 // 8 consecutive bf16 (natural order) -> 8 fp16 in the (0,4,1,5,2,6,3,7)
 // order; exact for |x| in [2^-17, 65504] (and x = 0).
 __device__ __forceinline__ uint4 kperm8_f16(uint4 v) {
@@ -235,7 +242,14 @@ __global__ void __launch_bounds__(256) k_scatter(ScatterArgs a) {
     pos = __shfl_sync(MS_FULL, pos, 0);
     const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)(p / a.k) * a.d);
     uint4* dst = reinterpret_cast<uint4*>(a.xperm + (long long)pos * a.d);
-    for (int c = lane; c < chunks; c += 32) dst[c] = kperm8_f16(__ldg(src + c));
+    bool over = false;
+    for (int c = lane; c < chunks; c += 32) {
+      const uint4 v = __ldg(src + c);
+      over |= bf16x2_beyond_f16(v.x) | bf16x2_beyond_f16(v.y) | bf16x2_beyond_f16(v.z) |
+              bf16x2_beyond_f16(v.w);
+      dst[c] = kperm8_f16(v);
+    }
+    if (__any_sync(MS_FULL, over) && lane == 0) atomicCAS(a.status, 0, ST_E_RANGE);
   }
 }
 
@@ -495,7 +509,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             const float u = is_up ? vf[8 + j] : other;
             const int m = c0 + (is_up ? 8 : 0) + j;
             const float h = t.slot >= 0 ? g_swiglu(a.model, g, u) : 0.f;
-            if (m < t.rows) hrow[(long long)m * a.ld_out] = __half_as_ushort(__float2half_rn(h));
+            if (m < t.rows) {
+              if (fabsf(h) > F16_MAX) atomicCAS(a.status, 0, ST_E_RANGE);
+              hrow[(long long)m * a.ld_out] = __half_as_ushort(__float2half_rn(h));
+            }
           }
         }
       } else {
@@ -572,7 +589,7 @@ __global__ void __launch_bounds__(256) k_mlp_count(MlpWideArgs a) {
     int s = a.slots[p];
     if (s < 0 || s >= a.n_slots) {             // its group reads nothing and yields zeros
       s = a.n_slots;
-      atomicCAS(a.status, 0, -1);
+      atomicCAS(a.status, 0, ST_E_INVALID);
     }
     a.keys[p] = s;
     atomicAdd(&a.cnt[s], 1);

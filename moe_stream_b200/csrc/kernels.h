@@ -133,6 +133,7 @@ struct ScatterArgs {
   float* perm_score;          // [P_pad]
   int* inv;                   // [T, k] pair -> row of xperm
   int* pair_slot;             // [T, k] or null
+  int* status;                // sticky pool status (ST_E_RANGE for x beyond fp16)
 };
 
 struct GemmArgs {

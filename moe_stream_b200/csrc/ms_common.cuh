@@ -19,6 +19,13 @@ constexpr int SAMPLE = 24;                    // engine_v3.py:322
 constexpr long long STRIDE = 7919;            // engine_v3.py:336
 constexpr long long YOUNG = 1LL << 30;        // engine_v3.py:349
 
+// Device-side status codes (the same values as MS_E_* of the C ABI).
+constexpr int ST_E_INVALID = -1, ST_E_TIMEOUT = -4, ST_E_RANGE = -8;
+// Largest finite fp16. An activation beyond it would enter the fp16
+// tensor-core operands as inf; its writer records ST_E_RANGE instead of
+// passing the overflow on silently.
+constexpr float F16_MAX = 65504.f;
+
 // stats slots (ms_stats order minus totals)
 enum { ST_PREFETCH = 0, ST_CACHE, ST_MISS, ST_BAIL, ST_ISSUED, ST_READS, ST_EXPOSED, ST_N };
 

@@ -22,6 +22,7 @@
 #include <mutex>
 
 #include "../../include/moestream.h"
+#include "host_wait.h"
 #include "kernels.h"
 
 using namespace ms;
@@ -201,17 +202,25 @@ extern "C" int ms_expert_mlp_static_status(void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int st = 0;
   TableCtr* ctr = reinterpret_cast<TableCtr*>(base + OFF_CTR);
-  if (cudaMemcpyAsync(&st, &ctr->status, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
-      cudaStreamSynchronize(s) != cudaSuccess)
+  if (cudaMemcpyAsync(&st, &ctr->status, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return sfail(MS_E_CUDA, "ms_expert_mlp_static_status: reading the status failed");
+  const cudaError_t we = stream_wait_bounded(s);
+  if (we == cudaErrorTimeout)
+    return sfail(MS_E_TIMEOUT, "ms_expert_mlp_static_status: the stream did not finish within "
+                               "the host wait limit (MS_HOST_WAIT_S)");
+  if (we != cudaSuccess)
     return sfail(MS_E_CUDA, "ms_expert_mlp_static_status: reading the status failed");
   if (cudaMemsetAsync(&ctr->status, 0, sizeof(int), s) != cudaSuccess ||
-      cudaStreamSynchronize(s) != cudaSuccess)
+      stream_wait_bounded(s) != cudaSuccess)
     return sfail(MS_E_CUDA, "ms_expert_mlp_static_status: clearing the status failed");
   if (st == MS_E_INVALID)
     return sfail(MS_E_INVALID, "ms_expert_mlp_static: a slot index was outside [0, n_slots); "
                                "its rows were returned as zeros");
   if (st == MS_E_TIMEOUT)
     return sfail(MS_E_TIMEOUT, "ms_expert_mlp_static: a bounded wait for the weight copies ran out");
+  if (st == MS_E_RANGE)
+    return sfail(MS_E_RANGE, "ms_expert_mlp_static: an activation beyond the fp16 range "
+                             "(|v| > 65504) reached the expert kernels; the output is not valid");
   if (st) return sfail(st, "ms_expert_mlp_static: device-side error");
   return MS_OK;
 }

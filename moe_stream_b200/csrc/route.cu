@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
   }
   if (A.xfrag)
     frag_write_rows(A.x, T, d, A.xfrag, A.xsum, blockIdx.x * RT_THREADS + threadIdx.x,
-                    gridDim.x * RT_THREADS);
+                    gridDim.x * RT_THREADS, &A.tab.ctr->status);
 
   // ----------------------------------------------------- arrival: last CTA
   __shared__ int s_last;
@@ -676,7 +676,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_mlp_prep(MlpPrepArgs A) {
   __shared__ int s_uniq[MS_MLP_MAX_PAIRS];
   __shared__ int s_cnt[MS_MLP_MAX_PAIRS], s_run[MS_MLP_MAX_PAIRS];
   extern __shared__ unsigned s_mask[];
-  frag_write_rows(A.x, A.T, A.d_model, A.xfrag, A.xsum, threadIdx.x, RT_THREADS);
+  frag_write_rows(A.x, A.T, A.d_model, A.xfrag, A.xsum, threadIdx.x, RT_THREADS, &A.ctr->status);
   // key n_slots collects out-of-range slots: its group reads nothing and
   // yields zeros, and the pool status records MS_E_INVALID
   const int nw = (A.n_slots + 1 + 31) / 32;
@@ -687,7 +687,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_mlp_prep(MlpPrepArgs A) {
     int s = A.slots[p];
     if (s < 0 || s >= A.n_slots) {
       s = A.n_slots;
-      atomicCAS(&A.ctr->status, 0, -1);
+      atomicCAS(&A.ctr->status, 0, ST_E_INVALID);
     }
     A.keys[p] = s;
     atomicOr(&s_mask[s >> 5], 1u << (s & 31));
