@@ -43,6 +43,11 @@ extern "C" {
 #define MS_MODEL_GPTOSS   1   /* engine_120b.py: top-k logits, softmax over k,
                                  per-projection bias, clamped SwiGLU               */
 
+#define MS_SCALE_BF16     0   /* scales and biases: bf16 [out, in/64] (mx.quantize) */
+#define MS_SCALE_FP8      1   /* scales and biases: OCP FP8 E4M3 [out, in/64] times
+                                 a per-row 2^(E-127), E one byte per row           */
+#define MS_MAX_CLASSES    8
+
 #define MS_EVICT_LFU      0   /* MOE_EVICT=lfu  (engine_v3.py:103, 347-348)        */
 #define MS_EVICT_LRU      1   /* MOE_EVICT=lru  (engine_v3.py:345-346)             */
 #define MS_EVICT_ASIS     2   /* MOE_EVICT=asis (engine_v3.py:343-344)             */
@@ -74,6 +79,19 @@ typedef struct ms_geom {
     int64_t blob_bytes;       /* padded blob size, a multiple of 16 KiB            */
     int64_t comp_offset[3][4];/* byte offset of [proj][part] in a blob, -1 if none */
 } ms_geom;
+
+/* One precision class of expert blobs (ms_pool_set_precision): the codes
+ * of a row are a little-endian bit stream of `bits`-bit codes (code j at
+ * bit bits*j), rows padded to 16 bytes; scales and biases per group of 64
+ * as bf16 or fp8. comp_offset[proj][part], parts: 0 weight, 1 scales,
+ * 2 biases, 3 bias (gpt-oss), 4 scales_exp, 5 biases_exp (fp8: one byte per
+ * row); -1 where absent. */
+typedef struct ms_prec {
+    int32_t bits;             /* 2, 3, 4 or 8                                      */
+    int32_t scale_fmt;        /* MS_SCALE_*                                        */
+    int64_t payload_bytes;    /* bytes of a blob of this class (<= blob_bytes)     */
+    int64_t comp_offset[3][6];
+} ms_prec;
 
 /* Pool configuration: PF_SLOTS, MOE_EVICT, PF_DEPTH, PF_WIDEN
  * (engine_v3.py:59-62, 84, 103). */
@@ -211,6 +229,17 @@ int ms_expert_mlp(ms_pool* pool, const int32_t* slots, const float* scores,
 int ms_pool_state_bytes(ms_pool* pool, int with_arena, size_t* bytes);
 int ms_pool_save_state(ms_pool* pool, void* dev_buf, int with_arena, void* stream);
 int ms_pool_load_state(ms_pool* pool, const void* dev_buf, int with_arena, void* stream);
+
+/* Per-expert precision (the reference's purpose for owning its kernel,
+ * kernels.py:25-29, which gather_qmm's single `bits` cannot express): the
+ * blob of key (layer, expert) is of class class_of_key[key] (host array of
+ * n_layers*n_experts entries) among n_classes classes. The slot and store
+ * stride stays geom.blob_bytes (the largest class); a fill copies only its
+ * class's payload, and every kernel reads each slot with its class's code
+ * width and scale format. Call before any slot is filled (MS_E_STATE
+ * after). One class equal to the geometry's own blob restores the default. */
+int ms_pool_set_precision(ms_pool* pool, int n_classes, const ms_prec* classes,
+                          const uint8_t* class_of_key);
 
 /* Failure-detection self-test, no reference counterpart: enqueues on
  * `stream` one CTA that waits, with the same bounded wait every kernel of the

@@ -20,6 +20,8 @@ MS_E_IO = -7
 MS_E_RANGE = -8
 
 MODEL_QWEN3, MODEL_GPTOSS = 0, 1
+SCALE_BF16, SCALE_FP8 = 0, 1
+MAX_CLASSES = 8
 EVICT = {"lfu": 0, "lru": 1, "asis": 2}
 MAX_DEPTHS = 4
 
@@ -32,6 +34,12 @@ class MsGeom(ctypes.Structure):
                 ("norm_topk_prob", ctypes.c_int32), ("proj_bias", ctypes.c_int32),
                 ("blob_bytes", ctypes.c_int64),
                 ("comp_offset", (ctypes.c_int64 * 4) * 3)]
+
+
+class MsPrec(ctypes.Structure):
+    _fields_ = [("bits", ctypes.c_int32), ("scale_fmt", ctypes.c_int32),
+                ("payload_bytes", ctypes.c_int64),
+                ("comp_offset", (ctypes.c_int64 * 6) * 3)]
 
 
 class MsPoolConfig(ctypes.Structure):
@@ -83,6 +91,7 @@ EXPORTS = {
     "ms_pool_save_state": [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p],
     "ms_pool_load_state": [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p],
     "ms_pool_selftest_wait": [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p],
+    "ms_pool_set_precision": [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p],
     "ms_kernel_arch": [ctypes.c_int, ctypes.POINTER(ctypes.c_int)],
     "ms_block_debug": [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p),
                        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)],

@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmoestream.so")
-SOURCES = ["api.cu", "route.cu", "expert.cu", "gemm.cu", "noalloc.cu"]
+SOURCES = ["api.cu", "route.cu", "expert.cu", "expert_mx.cu", "gemm.cu", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -163,7 +163,8 @@ struct ms_pool {
   int* inv = nullptr;
   uint16_t* hbuf = nullptr;
   uint16_t* ybuf = nullptr;
-  CUtensorMap tm_x{}, tm_h{}, tm_wg{}, tm_wu{}, tm_wd{};
+  CUtensorMap tm_x{}, tm_h{};
+  GemmMaps gm_up{}, gm_dn{};    // code tiles per precision class (gate/up, down)
   // decode expert kernels: gate, up and down weight rows as whole-row tiles
   // (encode_rows_map), when the row widths allow it
   CUtensorMap dec_maps[3] = {};
@@ -185,6 +186,15 @@ struct ms_pool {
   int pf_slot = 0;
   bool pf_captured = false;     // that fork was recorded inside a stream capture
   unsigned long long pf_capture_id = 0;
+  // precision classes (ms_pool_set_precision); by default one class, the
+  // geometry's 4-bit bf16 blob, served by the tuned uniform kernels
+  bool mixed = false;
+  bool used = false;            // a slot was filled: the classes are fixed from here on
+  ClassTab ctab{};
+  long long cls_bytes[MS_MAX_CLASSES] = {};   // bytes a fill of the class copies
+  uint8_t* class_of_key = nullptr;            // [n_keys]
+  uint8_t* slot_class = nullptr;              // [n_slots]
+  std::vector<uint8_t> h_class_of_key;
 };
 
 namespace {
@@ -267,12 +277,43 @@ int setup_wide(ms_pool* p) {
   const int ns = p->cfg.n_slots;
   const long long blob = p->geom.blob_bytes;
   if (encode_act_map(&p->tm_x, p->xperm, D, p->p_pad) || encode_act_map(&p->tm_h, p->hbuf, F, p->p_pad) ||
-      encode_weight_map(&p->tm_wg, p->arena + o[0 * 4 + 0], D, F, ns, blob, 64) ||
-      encode_weight_map(&p->tm_wu, p->arena + o[1 * 4 + 0], D, F, ns, blob, 64) ||
-      encode_weight_map(&p->tm_wd, p->arena + o[2 * 4 + 0], F, D, ns, blob, 128))
+      encode_codes_map(&p->gm_up.w[0][0], p->arena + o[0 * 4 + 0], D / 2, F, ns, blob, 32, 64) ||
+      encode_codes_map(&p->gm_up.w[1][0], p->arena + o[1 * 4 + 0], D / 2, F, ns, blob, 32, 64) ||
+      encode_codes_map(&p->gm_dn.w[0][0], p->arena + o[2 * 4 + 0], F / 2, D, ns, blob, 32, 128))
     return fail(MS_E_CUDA, "cuTensorMapEncodeTiled failed for the grouped-GEMM operands");
   p->wide = true;
   return MS_OK;
+}
+
+// Code-tile maps of the grouped GEMM for every precision class.
+int encode_class_maps(ms_pool* p, const ClassTab& t) {
+  const int D = p->geom.d_model, F = p->geom.d_ff, ns = p->cfg.n_slots;
+  const long long blob = p->geom.blob_bytes;
+  for (int i = 0; i < t.n; ++i) {
+    const PrecDev& c = t.c[i];
+    const int cb = gemm_tile_row_bytes(c.bits);
+    if (encode_codes_map(&p->gm_up.w[0][i], p->arena + c.off[0][P_W], code_row_bytes(D, c.bits), F, ns,
+                         blob, cb, 64) ||
+        encode_codes_map(&p->gm_up.w[1][i], p->arena + c.off[1][P_W], code_row_bytes(D, c.bits), F, ns,
+                         blob, cb, 64) ||
+        encode_codes_map(&p->gm_dn.w[0][i], p->arena + c.off[2][P_W], code_row_bytes(F, c.bits), D, ns,
+                         blob, cb, 128))
+      return fail(MS_E_CUDA, "cuTensorMapEncodeTiled failed for the code tiles of class %d", i);
+  }
+  return MS_OK;
+}
+
+// The geometry's own blob as precision class 0.
+void default_classes(ms_pool* p) {
+  ClassTab t{};
+  t.n = 1;
+  t.c[0].bits = 4;
+  t.c[0].fmt = SF_BF16;
+  for (int a = 0; a < 3; ++a)
+    for (int b = 0; b < 4; ++b) t.c[0].off[a][b] = std::max<long long>(0, p->geom.comp_offset[a][b]);
+  p->ctab = t;
+  p->cls_bytes[0] = p->geom.blob_bytes;
+  p->mixed = false;
 }
 
 }  // namespace
@@ -364,6 +405,11 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   if ((rc = palloc(p, &t.pend_list, t.n_slots))) return bail(rc);
   if ((rc = palloc(p, &t.fills, t.max_fills))) return bail(rc);
   if ((rc = palloc(p, &t.ctr, 1))) return bail(rc);
+  if ((rc = palloc(p, &p->class_of_key, t.n_keys))) return bail(rc);
+  if ((rc = palloc(p, &p->slot_class, t.n_slots))) return bail(rc);
+  CKB(cudaMemset(p->class_of_key, 0, t.n_keys));
+  CKB(cudaMemset(p->slot_class, 0, t.n_slots));
+  default_classes(p);
   if ((rc = palloc(p, &p->pf_ring, 2 * (size_t)t.max_fills))) return bail(rc);
   if ((rc = palloc(p, &p->pf_cnt, 3))) return bail(rc);
   CKB(cudaMemset(p->pf_cnt, 0, 3 * sizeof(int)));
@@ -543,6 +589,7 @@ int ms_pool_join(ms_pool* p, void* stream) {
 constexpr int FILL_CTAS = 32;
 
 static FillArgs fill_args(ms_pool* p) {
+  p->used = true;                       // fills may run from here on
   FillArgs f{};
   f.store = p->store_dev;
   f.arena = p->arena;
@@ -551,6 +598,11 @@ static FillArgs fill_args(ms_pool* p) {
   f.fills = p->tab.fills;
   f.max_fills = p->tab.max_fills;
   f.ctr = p->tab.ctr;
+  f.slot_class = p->slot_class;
+  if (p->mixed) {
+    f.class_of_key = p->class_of_key;
+    for (int i = 0; i < p->ctab.n; ++i) f.cls_chunks[i] = (int)((p->cls_bytes[i] + 16383) / 16384);
+  }
   return f;
 }
 
@@ -608,8 +660,12 @@ int ms_pool_read(ms_pool* p, int slot, int layer, int expert, void* stream) {
     return fail(MS_E_IO, "short read: blob (%d, %d) lies past the end of the store", layer, expert);
   CK(cudaSetDevice(p->device));
   if (int rc = join_side(p, static_cast<cudaStream_t>(stream))) return rc;
-  CK(cudaMemcpyAsync(p->arena + (size_t)slot * blob, p->store_host + off, blob,
+  p->used = true;
+  const int cls = p->mixed ? p->h_class_of_key[(size_t)layer * p->geom.n_experts + expert] : 0;
+  const size_t bytes = p->mixed ? (size_t)p->cls_bytes[cls] : blob;
+  CK(cudaMemcpyAsync(p->arena + (size_t)slot * blob, p->store_host + off, bytes,
                      cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream)));
+  CK(cudaMemsetAsync(p->slot_class + slot, cls, 1, static_cast<cudaStream_t>(stream)));
   return MS_OK;
 }
 
@@ -746,7 +802,15 @@ static ExpArgs exp_args(ms_pool* p, const void* x, int T, void* y, const float* 
   e.cnt = p->cnt;
   e.y = static_cast<uint16_t*>(y);
   e.status = &p->tab.ctr->status;
+  e.slot_class = p->slot_class;
   return e;
+}
+
+// The decode expert kernels of the pool: the tuned uniform ones, or the
+// per-class ones of a pool with precision classes.
+static cudaError_t run_experts(ms_pool* p, const ExpArgs& e, int max_groups, cudaStream_t s) {
+  if (p->mixed) return launch_expert_mx(e, p->ctab, max_groups, s);
+  return launch_expert(e, max_groups, s, p->dec_maps_ok ? p->dec_maps : nullptr);
 }
 
 // Expert MLPs of a routed wide batch: pairs scattered into expert order,
@@ -788,11 +852,13 @@ static int wide_experts(ms_pool* p, const void* x, int T, int k, const int* keys
   g.K = p->geom.d_model;
   g.n_out = p->geom.d_ff;
   g.ld_out = p->geom.d_ff;
-  CK(launch_gemm(0, p->tm_x, p->tm_wg, p->tm_wu, g, tiles * (p->geom.d_ff / 64), p->sm_count, s));
+  g.slot_class = p->slot_class;
+  g.C = p->ctab;
+  CK(launch_gemm(0, p->tm_x, p->gm_up, g, p->mixed, tiles * (p->geom.d_ff / 64), p->sm_count, s));
   g.K = p->geom.d_ff;
   g.n_out = p->geom.d_model;
   g.ld_out = p->geom.d_model;
-  CK(launch_gemm(1, p->tm_h, p->tm_wd, p->tm_wd, g, tiles * ((p->geom.d_model + 127) / 128),
+  CK(launch_gemm(1, p->tm_h, p->gm_dn, g, p->mixed, tiles * ((p->geom.d_model + 127) / 128),
                  p->sm_count, s));
   CombineArgs c{};
   c.Y = p->ybuf;
@@ -876,8 +942,7 @@ int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* str
     if ((rc = wide_experts(p, x, T, k, p->inds, p->scores_f, p->pair_slot, y, s))) return rc;
   } else {
     const int max_groups = std::min(T * k, p->geom.n_experts);
-    CK(launch_expert(exp_args(p, x, T, y, p->scores_f), max_groups, s,
-                     p->dec_maps_ok ? p->dec_maps : nullptr));
+    CK(run_experts(p, exp_args(p, x, T, y, p->scores_f), max_groups, s));
   }
   if (ev) CK(cudaEventRecordWithFlags(ev[3], s, rec_flags));
   return MS_OK;
@@ -949,8 +1014,7 @@ int ms_expert_mlp(ms_pool* p, const int32_t* slots, const float* scores, const v
   a.xsum = p->xsum;
   a.grp = p->grp;
   CK(launch_mlp_prep(a, s));
-  CK(launch_expert(exp_args(p, x, T, y, scores), std::min(T * k, p->cfg.n_slots), s,
-                   p->dec_maps_ok ? p->dec_maps : nullptr));
+  CK(run_experts(p, exp_args(p, x, T, y, scores), std::min(T * k, p->cfg.n_slots), s));
   return MS_OK;
 }
 
@@ -1044,7 +1108,7 @@ static std::vector<std::pair<void*, size_t>> state_segments(ms_pool* p, int with
   std::vector<std::pair<void*, size_t>> seg = {
       {t.key_of, 4 * ns},      {t.slot_of, 4 * nk},  {t.freq, 4 * nk},     {t.born, 8 * nk},
       {t.last_use, 8 * nk},    {t.kflags, nk},       {t.pinned, ns},       {t.pin_list, 4 * ns},
-      {t.pend_list, 4 * ns},   {t.ctr, sizeof(TableCtr)}};
+      {t.pend_list, 4 * ns},   {t.ctr, sizeof(TableCtr)}, {p->slot_class, ns}};
   if (with_arena) seg.push_back({p->arena, p->arena_bytes});
   return seg;
 }
@@ -1081,8 +1145,69 @@ int ms_pool_save_state(ms_pool* p, void* dev_buf, int with_arena, void* stream) 
 
 int ms_pool_load_state(ms_pool* p, const void* dev_buf, int with_arena, void* stream) {
   if (!p) return fail(MS_E_INVALID, "NULL pool");
+  p->used = true;
   return copy_state(p, const_cast<void*>(dev_buf), with_arena, static_cast<cudaStream_t>(stream),
                     false);
+}
+
+int ms_pool_set_precision(ms_pool* p, int n_classes, const ms_prec* classes,
+                          const uint8_t* class_of_key) {
+  if (!p || !classes || !class_of_key) return fail(MS_E_INVALID, "NULL argument");
+  if (n_classes < 1 || n_classes > MS_MAX_CLASSES)
+    return fail(MS_E_INVALID, "n_classes must be in [1, %d]", MS_MAX_CLASSES);
+  if (p->used)
+    return fail(MS_E_STATE, "precision classes must be set before the first slot fill");
+  const ms_geom& g = p->geom;
+  const int D = g.d_model, F = g.d_ff;
+  ClassTab t{};
+  t.n = n_classes;
+  for (int i = 0; i < n_classes; ++i) {
+    const ms_prec& c = classes[i];
+    if (c.bits != 2 && c.bits != 3 && c.bits != 4 && c.bits != 8)
+      return fail(MS_E_INVALID, "class %d: bits must be 2, 3, 4 or 8 (got %d)", i, c.bits);
+    if (c.scale_fmt != MS_SCALE_BF16 && c.scale_fmt != MS_SCALE_FP8)
+      return fail(MS_E_INVALID, "class %d: unknown scale format %d", i, c.scale_fmt);
+    if (c.payload_bytes <= 0 || c.payload_bytes > g.blob_bytes)
+      return fail(MS_E_INVALID, "class %d: payload_bytes must be in (0, blob_bytes]", i);
+    const int esz = c.scale_fmt == MS_SCALE_FP8 ? 1 : 2;
+    for (int pr = 0; pr < 3; ++pr) {
+      const int n_out = pr < 2 ? F : D, n_in = pr < 2 ? D : F, G = n_in / 64;
+      const long long sz[6] = {(long long)n_out * code_row_bytes(n_in, c.bits), (long long)n_out * G * esz,
+                               (long long)n_out * G * esz, (long long)n_out * 2, n_out, n_out};
+      const bool need[6] = {true, true, true, g.proj_bias != 0, esz == 1, esz == 1};
+      for (int pt = 0; pt < 6; ++pt) {
+        const long long off = c.comp_offset[pr][pt];
+        if (!need[pt]) continue;
+        if (off < 0 || off % 16 || off + sz[pt] > c.payload_bytes)
+          return fail(MS_E_INVALID, "class %d: component [%d][%d] at %lld (+%lld) is not a 16-byte "
+                      "aligned range inside the payload", i, pr, pt, off, sz[pt]);
+        t.c[i].off[pr][pt] = off;
+      }
+    }
+    t.c[i].bits = c.bits;
+    t.c[i].fmt = c.scale_fmt;
+  }
+  for (long long k = 0; k < p->n_keys; ++k)
+    if (class_of_key[k] >= n_classes)
+      return fail(MS_E_INVALID, "class_of_key[%lld] = %d is not a class", k, (int)class_of_key[k]);
+  CK(cudaSetDevice(p->device));
+  // one class that is the geometry's own blob keeps the uniform kernels
+  bool same = n_classes == 1 && classes[0].bits == 4 && classes[0].scale_fmt == MS_SCALE_BF16;
+  for (int pr = 0; pr < 3 && same; ++pr)
+    for (int pt = 0; pt < 4 && same; ++pt)
+      if (g.comp_offset[pr][pt] >= 0 && classes[0].comp_offset[pr][pt] != g.comp_offset[pr][pt]) same = false;
+  if (same) {
+    default_classes(p);
+    return MS_OK;
+  }
+  if (p->wide)
+    if (int rc = encode_class_maps(p, t)) return rc;
+  CK(cudaMemcpy(p->class_of_key, class_of_key, (size_t)p->n_keys, cudaMemcpyHostToDevice));
+  p->h_class_of_key.assign(class_of_key, class_of_key + p->n_keys);
+  p->ctab = t;
+  for (int i = 0; i < n_classes; ++i) p->cls_bytes[i] = classes[i].payload_bytes;
+  p->mixed = true;
+  return MS_OK;
 }
 
 int ms_pool_selftest_wait(ms_pool* p, long long limit_ns, void* stream) {

@@ -61,9 +61,9 @@ constexpr int GM_STAGES = 8;                  // token + code tiles
 constexpr int GM_A_STAGES = 4;                // weight tiles in TMEM
 constexpr int GM_TOK = GEMM_TILE_ROWS;        // tokens per tile (MMA N, at most)
 constexpr int GM_X_BYTES = GM_TOK * 128;      // 128 tokens x 64 fp16
-constexpr int GM_P_BYTES = 128 * 32;          // 128 weight rows x 64 nibbles
+constexpr int GM_P_BYTES = 128 * 64;          // 128 weight rows x 64 codes of up to 8 bits
 constexpr int GM_OFF_P = GM_STAGES * GM_X_BYTES;                   // 128 KB
-constexpr int GM_OFF_BAR = GM_OFF_P + GM_STAGES * GM_P_BYTES;      // 160 KB (> half an SM:
+constexpr int GM_OFF_BAR = GM_OFF_P + GM_STAGES * GM_P_BYTES;      // 192 KB (> half an SM:
 constexpr int GM_SMEM = GM_OFF_BAR + 256 + 1024;                   //  one CTA per SM)
 // TMEM columns: accumulators [0, 128) and [128, 256); weight stage s at
 // 256 + 64 s (hi, then lo)
@@ -258,10 +258,58 @@ __global__ void __launch_bounds__(256) k_scatter(ScatterArgs a) {
 // tiles are 64 features of d_ff (gate and up rows), PHASE 1 tiles 128
 // features of d_model (down rows). Items whose group has no slot (pool
 // exhausted) run with zero weights and write zeros.
-template <int PHASE>
+// The class of an item's slot (MIXED pools; 0 for a missing slot, whose
+// codes read as zeros through class 0's maps).
+template <bool MIXED>
+__device__ __forceinline__ int item_class(const GemmArgs& a, int slot) {
+  if (!MIXED || slot < 0) return 0;
+  return min((int)a.slot_class[slot], a.C.n - 1);
+}
+
+// Codes j and j + 4 (j in 0..3) of 8-code block b of the 16 codes a
+// dequantising lane takes from a staged K tile, as exact floats. r: the raw
+// bits (see load_codes).
+template <int BITS>
+__device__ __forceinline__ float2 code_pair(const uint32_t* r, int b, int j) {
+  uint32_t q0, q1;
+  if (BITS == 2) {
+    q0 = (r[0] >> (16 * b + 2 * j)) & 3u;
+    q1 = (r[0] >> (16 * b + 2 * j + 8)) & 3u;
+  } else if (BITS == 8) {
+    q0 = (r[2 * b] >> (8 * j)) & 0xFFu;
+    q1 = (r[2 * b + 1] >> (8 * j)) & 0xFFu;
+  } else {                                     // 3: r[b] holds codes 8b..8b+7 at bits 3i
+    q0 = (r[b] >> (3 * j)) & 7u;
+    q1 = (r[b] >> (3 * j + 12)) & 7u;
+  }
+  return make_float2(__uint_as_float(q0 | 0x4B000000u) - 8388608.f,
+                     __uint_as_float(q1 | 0x4B000000u) - 8388608.f);
+}
+
+// The raw bits of a lane's 16 codes (part `part` of a 64-code K tile) from
+// its staged row: 2 bits one word, 8 bits four, 3 bits two words of codes
+// 0-7 and 8-15 (the tile starts o3 bytes into the staged row).
+template <int BITS>
+__device__ __forceinline__ void load_codes(const uint8_t* row, int part, int o3, uint32_t* r) {
+  if (BITS == 2) {
+    r[0] = *reinterpret_cast<const uint32_t*>(row + 4 * part);
+  } else if (BITS == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + 16 * part);
+    r[0] = u.x; r[1] = u.y; r[2] = u.z; r[3] = u.w;
+  } else {
+    const int b0 = o3 + 6 * part, base = b0 & ~3, sh = (b0 & 3) * 8;
+    const uint32_t lo = *reinterpret_cast<const uint32_t*>(row + base);
+    const uint32_t hi = *reinterpret_cast<const uint32_t*>(row + base + 4);
+    const uint32_t aa = __funnelshift_r(lo, hi, sh);
+    const uint32_t bb = hi >> sh;
+    r[0] = aa;
+    r[1] = __funnelshift_r(aa, bb, 24);
+  }
+}
+
+template <int PHASE, bool MIXED>
 __global__ void __launch_bounds__(GM_THREADS, 1)
-    k_gemm(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW0,
-           const __grid_constant__ CUtensorMap tmW1, GemmArgs a) {
+    k_gemm(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ GemmMaps mm, GemmArgs a) {
   constexpr int FT = PHASE == 0 ? 64 : 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -314,20 +362,26 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         const GemmTile t = tn;
         if (w + step < total) tn = a.tiles[(w + step) / n_ft];
         const int f0 = (w % n_ft) * FT;
+        const int cls = item_class<MIXED>(a, t.slot);
+        const int bits = MIXED ? a.C.c[cls].bits : 4;
+        const int cb = gemm_tile_row_bytes(bits);   // staged bytes per row of a K tile
         for (int kt = 0; kt < KT; ++kt, ++it) {
           const int s = it % GM_STAGES;
           if (it >= GM_STAGES && !mbar_wait(&empty_x[s], ((it / GM_STAGES) - 1) & 1, a.status)) {
             ok = false;
             break;
           }
-          mbar_expect_tx(&full[s], GM_X_BYTES + GM_P_BYTES);
+          // the K tile's codes start 8*bits*kt bytes into the row (3 bits:
+          // from the 16-byte boundary below, the rest is read past it)
+          const int xc = bits == 3 ? ((24 * kt) & ~15) : 8 * bits * kt;
+          mbar_expect_tx(&full[s], GM_X_BYTES + 128 * cb);
           tma_load_2d(sX(s), &tmX, kt * 64, t.row0, &full[s]);
           // a slot of -1 reads outside the tensor: the codes arrive as zeros
           if (PHASE == 0) {
-            tma_load_3d(sP(s), &tmW0, kt * 32, f0, t.slot, &full[s]);
-            tma_load_3d(sP(s) + 64 * 32, &tmW1, kt * 32, f0, t.slot, &full[s]);
+            tma_load_3d(sP(s), &mm.w[0][cls], xc, f0, t.slot, &full[s]);
+            tma_load_3d(sP(s) + 64 * cb, &mm.w[1][cls], xc, f0, t.slot, &full[s]);
           } else {
-            tma_load_3d(sP(s), &tmW0, kt * 32, f0, t.slot, &full[s]);
+            tma_load_3d(sP(s), &mm.w[0][cls], xc, f0, t.slot, &full[s]);
           }
         }
       }
@@ -377,25 +431,51 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     // scale/bias prefetch cursor: item pw, K tile pkt, SCALE_AHEAD K tiles
     // ahead of the work and running across item boundaries. Every load
     // address is valid (rows without weights read row 0 of slot 0 and are
-    // masked when consumed), so no load is ever waited on early.
+    // masked when consumed), so no load is ever waited on early: a ring
+    // entry keeps the raw scale and bias (bf16 bits, or fp8 codes) in the
+    // registers the loads write, untouched until the entry is consumed, and
+    // a word with whether the row is active plus (MIXED) the item's code
+    // width and fp8 row exponents, so the consumer needs no per-item lookups
+    // of its own.
     int pw = blockIdx.x, pkt = 0;
-    const uint16_t *psc = nullptr, *pbi = nullptr;
-    bool pact = false;
+    const uint8_t *psc = nullptr, *pbi = nullptr;
+    uint32_t pmeta = 0;                        // active | fp8 << 1 | bits << 2 | es << 8 | eb << 16
+    int pesz = 2;
     GemmTile pnext = a.tiles[pw / n_ft];
     auto enter = [&](int w) {                  // the cursor enters item w (pnext = its tile)
       const GemmTile tt = pnext;
       if (w + step < total) pnext = a.tiles[(w + step) / n_ft];
       const int orow = (w % n_ft) * FT + (PHASE == 0 ? 16 * quarter + (lane & 15) : L);
-      pact = tt.slot >= 0 && orow < n_out;
-      const uint8_t* blob = a.arena + (long long)(pact ? tt.slot : 0) * a.blob;
-      const long long ro = pact ? (long long)orow * G : 0;
-      psc = reinterpret_cast<const uint16_t*>(blob + a.off[proj][1]) + ro;
-      pbi = reinterpret_cast<const uint16_t*>(blob + a.off[proj][2]) + ro;
+      const bool act = tt.slot >= 0 && orow < n_out;
+      const uint8_t* blob = a.arena + (long long)(act ? tt.slot : 0) * a.blob;
+      const long long ro = act ? orow : 0;
+      if (!MIXED) {
+        psc = blob + a.off[proj][1] + ro * G * 2;
+        pbi = blob + a.off[proj][2] + ro * G * 2;
+        pmeta = (act ? 1u : 0u) | (4u << 2);
+      } else {
+        const PrecDev& pc = a.C.c[item_class<MIXED>(a, tt.slot)];
+        pesz = pc.fmt == SF_FP8 ? 1 : 2;
+        psc = blob + pc.off[proj][P_S] + ro * G * pesz;
+        pbi = blob + pc.off[proj][P_B] + ro * G * pesz;
+        uint32_t es = 0, eb = 0;
+        if (pc.fmt == SF_FP8) {
+          es = blob[pc.off[proj][P_SE] + ro];
+          eb = blob[pc.off[proj][P_BE] + ro];
+        }
+        pmeta = (act ? 1u : 0u) | ((pc.fmt == SF_FP8 ? 1u : 0u) << 1) | ((uint32_t)pc.bits << 2) |
+                (es << 8) | (eb << 16);
+      }
     };
-    auto fetch = [&](uint16_t& sv, uint16_t& bv, bool& av) {
-      av = pact && pw < total;
-      sv = psc[pkt];
-      bv = pbi[pkt];
+    auto fetch = [&](uint32_t& sv, uint32_t& bv, uint32_t& meta) {
+      meta = pw < total ? pmeta : 0u;
+      if (!MIXED || pesz == 2) {
+        sv = reinterpret_cast<const uint16_t*>(psc)[pkt];
+        bv = reinterpret_cast<const uint16_t*>(pbi)[pkt];
+      } else {
+        sv = psc[pkt];
+        bv = pbi[pkt];
+      }
       if (++pkt == KT) {
         pkt = 0;
         pw += step;
@@ -403,10 +483,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       }
     };
     enter(pw);
-    uint16_t rs[SCALE_AHEAD], rb[SCALE_AHEAD];
-    bool ra[SCALE_AHEAD];
+    uint32_t rs[SCALE_AHEAD], rb[SCALE_AHEAD], rmeta[SCALE_AHEAD];
 #pragma unroll
-    for (int i = 0; i < SCALE_AHEAD; ++i) fetch(rs[i], rb[i], ra[i]);
+    for (int i = 0; i < SCALE_AHEAD; ++i) fetch(rs[i], rb[i], rmeta[i]);
     const float2 magic_off = make_float2(-8388608.f, -8388608.f);
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const int n_it = ((total - (int)blockIdx.x + step - 1) / step) * KT;   // K tiles of this CTA
@@ -418,8 +497,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       for (int j = 0; j < SCALE_AHEAD; ++j) {
         const int it = it0 + j;
         if (it >= n_it || !ok) continue;
-        const float sc = ra[j] ? bf2f(rs[j]) : 0.f, bi = ra[j] ? bf2f(rb[j]) : 0.f;
-        fetch(rs[j], rb[j], ra[j]);
+        const uint32_t meta = rmeta[j];
+        float sc = 0.f, bi = 0.f;
+        if (meta & 1u) {
+          if (MIXED && (meta & 2u)) {
+            sc = e4m3_to_f((uint8_t)rs[j]) * exp_factor((uint8_t)((meta >> 8) & 0xFFu));
+            bi = e4m3_to_f((uint8_t)rb[j]) * exp_factor((uint8_t)((meta >> 16) & 0xFFu));
+          } else {
+            sc = bf2f((uint16_t)rs[j]);
+            bi = bf2f((uint16_t)rb[j]);
+          }
+        }
+        const int bits = MIXED ? (int)((meta >> 2) & 0xFu) : 4;
+        fetch(rs[j], rb[j], rmeta[j]);
         const int sx = it % GM_STAGES, sa = it % GM_A_STAGES;
         // every lane waits; the warp goes on only if all of them saw the stage
         bool got = mbar_wait(&full[sx], (it / GM_STAGES) & 1, a.status);
@@ -431,25 +521,53 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         }
         tc_fence_after();
         uint32_t wh[8], wl[8];
-        const uint2 pw2 = *reinterpret_cast<const uint2*>(sP(sx) + prow * 32 + part * 8);
-        const uint32_t words[2] = {pw2.x, pw2.y};
         const float2 s2 = make_float2(sc, sc), b2 = make_float2(bi, bi);
+        // the weight pair (q, q') -> hi and lo halves: exact s*q + b split
+        auto put = [&](int idx, float2 q) {
+          const float2 wv = __ffma2_rn(q, s2, b2);            // exact: s*q + b
+          const __half2 hi = __floats2half2_rn(wv.x, wv.y);
+          const float2 hf = __half22float2(hi);
+          const float2 lo = __fadd2_rn(wv, make_float2(-hf.x, -hf.y));
+          wh[idx] = *reinterpret_cast<const uint32_t*>(&hi);
+          wl[idx] = h2_bits(lo.x, lo.y);
+        };
+        if (!MIXED || bits == 4) {
+          const uint2 pw2 = *reinterpret_cast<const uint2*>(sP(sx) + prow * 32 + part * 8);
+          const uint32_t words[2] = {pw2.x, pw2.y};
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const uint32_t u = words[i];
+          for (int i = 0; i < 2; ++i) {
+            const uint32_t u = words[i];
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            // q and q+4 of this word as exact floats (2^23 + q, minus 2^23)
-            const uint32_t m = (u >> (4 * q4)) & 0x000F000Fu;
-            const float2 q = __fadd2_rn(make_float2(__uint_as_float((m & 0xFu) | 0x4B000000u),
-                                                    __uint_as_float((m >> 16) | 0x4B000000u)),
-                                        magic_off);
-            const float2 wv = __ffma2_rn(q, s2, b2);            // exact: s*q + b
-            const __half2 hi = __floats2half2_rn(wv.x, wv.y);
-            const float2 hf = __half22float2(hi);
-            const float2 lo = __fadd2_rn(wv, make_float2(-hf.x, -hf.y));
-            wh[i * 4 + q4] = *reinterpret_cast<const uint32_t*>(&hi);
-            wl[i * 4 + q4] = h2_bits(lo.x, lo.y);
+            for (int q4 = 0; q4 < 4; ++q4) {
+              // q and q+4 of this word as exact floats (2^23 + q, minus 2^23)
+              const uint32_t m = (u >> (4 * q4)) & 0x000F000Fu;
+              put(i * 4 + q4, __fadd2_rn(make_float2(__uint_as_float((m & 0xFu) | 0x4B000000u),
+                                                     __uint_as_float((m >> 16) | 0x4B000000u)),
+                                         magic_off));
+            }
+          }
+        } else {
+          const uint8_t* row = sP(sx) + prow * gemm_tile_row_bytes(bits);
+          const int kt = it % KT;
+          uint32_t r[4];
+          if (bits == 2) {
+            load_codes<2>(row, part, 0, r);
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) put(i * 4 + q4, code_pair<2>(r, i, q4));
+          } else if (bits == 8) {
+            load_codes<8>(row, part, 0, r);
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) put(i * 4 + q4, code_pair<8>(r, i, q4));
+          } else {
+            load_codes<3>(row, part, (24 * kt) & 15, r);
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) put(i * 4 + q4, code_pair<3>(r, i, q4));
           }
         }
         const uint32_t col = TM_A + sa * 64 + part * 8;
@@ -486,8 +604,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         const bool is_up = lane >= 16;
         const int fg = f0 + 16 * quarter + (lane & 15);     // feature index in d_ff
         const int pos = (fg & ~7) | kperm_pos(fg & 7);      // its k-permuted h column
+        const long long boff = MIXED ? a.C.c[item_class<MIXED>(a, t.slot)].off[is_up ? 1 : 0][P_BIAS]
+                                     : a.off[is_up ? 1 : 0][3];
         const float bias = (a.model == 1 && t.slot >= 0)
-                               ? bf2f(reinterpret_cast<const uint16_t*>(blob + a.off[is_up ? 1 : 0][3])[fg])
+                               ? bf2f(reinterpret_cast<const uint16_t*>(blob + boff)[fg])
                                : 0.f;
         uint16_t* hrow = a.H + (long long)t.row0 * a.ld_out + pos;
         for (int c0 = 0; c0 < ntok; c0 += 16) {
@@ -518,8 +638,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       } else {
         const int fo = f0 + L;                 // output feature
         const bool f_ok = fo < n_out;
+        const long long boff = MIXED ? a.C.c[item_class<MIXED>(a, t.slot)].off[2][P_BIAS] : a.off[2][3];
         const float bias = (a.model == 1 && f_ok && t.slot >= 0)
-                               ? bf2f(reinterpret_cast<const uint16_t*>(blob + a.off[2][3])[fo]) : 0.f;
+                               ? bf2f(reinterpret_cast<const uint16_t*>(blob + boff)[fo]) : 0.f;
 #pragma unroll
         for (int c0 = 0; c0 < GM_TOK; c0 += 16) {
           if (c0 >= ntok) continue;
@@ -773,16 +894,16 @@ int encode_act_map(CUtensorMap* m, const void* base, int K, long long rows) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS ? 0 : -2;
 }
 
-// 4-bit weight codes of one projection across all slots, as bytes
-// [n_slots][rows_out][K/2]: boxes of 32 bytes (one group of 64 codes) x
-// box_rows rows x 1 slot, unswizzled.
-int encode_weight_map(CUtensorMap* m, const void* base, int K, int rows_out, int n_slots,
-                      long long blob, int box_rows) {
+// Weight codes of one projection across all slots, as bytes
+// [n_slots][rows_out][row_bytes]: boxes of box_bytes (one K tile of codes)
+// x box_rows rows x 1 slot, unswizzled.
+int encode_codes_map(CUtensorMap* m, const void* base, int row_bytes, int rows_out, int n_slots,
+                     long long blob, int box_bytes, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return -1;
-  const cuuint64_t dims[3] = {(cuuint64_t)(K / 2), (cuuint64_t)rows_out, (cuuint64_t)n_slots};
-  const cuuint64_t strides[2] = {(cuuint64_t)(K / 2), (cuuint64_t)blob};
-  const cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
+  const cuuint64_t dims[3] = {(cuuint64_t)row_bytes, (cuuint64_t)rows_out, (cuuint64_t)n_slots};
+  const cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)blob};
+  const cuuint32_t box[3] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -821,23 +942,22 @@ cudaError_t launch_combine(const CombineArgs& a, int grid, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-template <int PHASE>
-static cudaError_t launch_gemm_t(const CUtensorMap& tX, const CUtensorMap& tW0,
-                                 const CUtensorMap& tW1, const GemmArgs& a, int grid,
-                                 cudaStream_t s) {
-  auto kern = k_gemm<PHASE>;
+template <int PHASE, bool MIXED>
+static cudaError_t launch_gemm_t(const CUtensorMap& tX, const GemmMaps& maps, const GemmArgs& a,
+                                 int grid, cudaStream_t s) {
+  auto kern = k_gemm<PHASE, MIXED>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<grid, GM_THREADS, GM_SMEM, s>>>(tX, tW0, tW1, a);
+  kern<<<grid, GM_THREADS, GM_SMEM, s>>>(tX, maps, a);
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm(int phase, const CUtensorMap& tX, const CUtensorMap& tW0,
-                        const CUtensorMap& tW1, const GemmArgs& a, int max_items, int sms,
-                        cudaStream_t s) {
+cudaError_t launch_gemm(int phase, const CUtensorMap& tX, const GemmMaps& maps, const GemmArgs& a,
+                        bool mixed, int max_items, int sms, cudaStream_t s) {
   const int grid = std::max(1, std::min(max_items, sms));
-  if (phase == 0) return launch_gemm_t<0>(tX, tW0, tW1, a, grid, s);
-  return launch_gemm_t<1>(tX, tW0, tW1, a, grid, s);
+  if (phase == 0)
+    return mixed ? launch_gemm_t<0, true>(tX, maps, a, grid, s) : launch_gemm_t<0, false>(tX, maps, a, grid, s);
+  return mixed ? launch_gemm_t<1, true>(tX, maps, a, grid, s) : launch_gemm_t<1, false>(tX, maps, a, grid, s);
 }
 
 }  // namespace ms

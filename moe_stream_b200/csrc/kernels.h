@@ -4,6 +4,7 @@
 #include <cuda.h>   // CUtensorMap
 
 #include "ms_common.cuh"
+#include "prec.cuh"
 
 #ifndef MS_MAX_DEPTHS
 #define MS_MAX_DEPTHS 4
@@ -75,6 +76,10 @@ struct FillArgs {
   int pdl;                    // launched as a programmatic dependent of the route step
   const void* l2_next;        // bytes the next block call's route step will read first
   unsigned l2_next_bytes;     // (a multiple of 16), prefetched into L2; 0 for none
+  // precision classes (null class_of_key: one class, whole blobs)
+  const uint8_t* class_of_key;  // [n_keys]
+  uint8_t* slot_class;          // [n_slots]: written with each fill
+  int cls_chunks[MS_MAX_CLASSES];   // 16 KiB chunks a fill of the class copies
 };
 
 struct MlpPrepArgs {
@@ -102,7 +107,7 @@ struct ExpArgs {
   unsigned* cnt;              // [d_model/16]
   uint16_t* y;                // bf16 [T, d_model]
   int* status;                // sticky pool status (bounded waits report here)
-  int stages_up, stages_dn;   // ring depths of k_up / k_down (set by launch_expert)
+  const uint8_t* slot_class;  // [n_slots] precision class of each slot's blob (mixed pools)
 };
 
 // ------------------------------------------------ wide batches (prefill)
@@ -150,6 +155,14 @@ struct GemmArgs {
   int ld_out;
   const float* perm_score;
   int* status;
+  const uint8_t* slot_class;  // mixed pools: class of each slot, and the classes
+  ClassTab C;
+};
+
+// Code-tile tensor maps of the grouped GEMM, per precision class: phase 0
+// w[0] gate, w[1] up; phase 1 w[0] down.
+struct GemmMaps {
+  CUtensorMap w[2][MS_MAX_CLASSES];
 };
 
 struct CombineArgs {
@@ -199,14 +212,21 @@ cudaError_t launch_route_wide(const RouteArgs& a, const WideArgs& w, cudaStream_
 cudaError_t launch_scatter(const ScatterArgs& a, int grid, cudaStream_t s);
 // Persistent grouped GEMM over at most max_items (token tile, feature tile)
 // items, one CTA per SM (sms).
-cudaError_t launch_gemm(int phase, const CUtensorMap& tX, const CUtensorMap& tW0,
-                        const CUtensorMap& tW1, const GemmArgs& a, int max_items, int sms,
-                        cudaStream_t s);
+// mixed: the pool has precision classes (a.C, a.slot_class; maps.w per class),
+// else every slot is the geometry's 4-bit bf16 blob (maps.w[.][0]).
+cudaError_t launch_gemm(int phase, const CUtensorMap& tX, const GemmMaps& maps, const GemmArgs& a,
+                        bool mixed, int max_items, int sms, cudaStream_t s);
 cudaError_t launch_combine(const CombineArgs& a, int grid, cudaStream_t s);
 // Tensor maps of the grouped GEMM. 0 on success.
 int encode_act_map(CUtensorMap* m, const void* base, int K, long long rows);
-int encode_weight_map(CUtensorMap* m, const void* base, int K, int rows_out, int n_slots,
-                      long long blob, int box_rows);
+// Weight codes of one projection across all slots, as bytes [n_slots]
+// [rows_out][row_bytes], in boxes of box_bytes x box_rows x 1 slot.
+int encode_codes_map(CUtensorMap* m, const void* base, int row_bytes, int rows_out, int n_slots,
+                     long long blob, int box_bytes, int box_rows);
+// Bytes per staged row of a GEMM K tile (64 codes) of a class: 8*bits,
+// except 3 bits, whose 24-byte tile is read as the 32 bytes from the
+// 16-byte boundary at or below it.
+__host__ __device__ inline int gemm_tile_row_bytes(int bits) { return bits == 3 ? 32 : 8 * bits; }
 // Token rows per GEMM tile.
 constexpr int GEMM_TILE_ROWS = 128;
 cudaError_t launch_pool_op(const DevTable& t, const PoolReq& r, int* slots_out, int* st,
@@ -218,6 +238,8 @@ cudaError_t launch_mlp_prep(const MlpPrepArgs& a, cudaStream_t s);
 // down kernel's rows per tile), which replace the per-row copies.
 cudaError_t launch_expert(const ExpArgs& a, int max_groups, cudaStream_t s,
                           const CUtensorMap* maps = nullptr);
+// The decode expert kernels of a pool with precision classes (expert_mx.cu).
+cudaError_t launch_expert_mx(const ExpArgs& a, const ClassTab& C, int max_groups, cudaStream_t s);
 // Rows per tensor-map box of the down kernel for this shape (0: no map path).
 int expert_down_rows(int model, int d_model, int d_ff);
 int encode_rows_map(CUtensorMap* m, const void* base, int row_bytes, int rows_out, int n_slots,

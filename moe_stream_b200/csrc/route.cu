@@ -661,6 +661,11 @@ __global__ void __launch_bounds__(256) k_fill(FillArgs F) {
       if (threadIdx.x == 0) atomicCAS(err, 0, -7);
       continue;
     }
+    // a blob of a smaller precision class copies only its own chunks; the
+    // slot records the class of what it now holds
+    const int cls = F.class_of_key ? F.class_of_key[f.y] : 0;
+    if (part == 0 && threadIdx.x == 0 && F.slot_class) F.slot_class[f.x] = (uint8_t)cls;
+    if (F.class_of_key && part >= F.cls_chunks[cls]) continue;
     const uint4* src = reinterpret_cast<const uint4*>(F.store + (long long)f.y * F.blob + part * 16384);
     uint4* dst = reinterpret_cast<uint4*>(F.arena + (long long)f.x * F.blob + part * 16384);
     uint4 v[4];

@@ -11,6 +11,7 @@ The blob is padded to a whole number of 16 KiB pages (repack_gptoss.py:159).
 The HBM slot arena uses the same layout, so a slot fill is one contiguous
 copy and slot s of component c is at ``arena + s*blob_bytes + offset(c)``.
 """
+import dataclasses
 from dataclasses import dataclass, field
 
 from . import _lib
@@ -18,6 +19,16 @@ from . import _lib
 PAGE = 16384
 PROJS = ("gate_proj", "up_proj", "down_proj")
 PARTS = ("weight", "scales", "biases", "bias")
+# precision classes: component parts in ms_prec order
+PREC_PARTS = ("weight", "scales", "biases", "bias", "scales_exp", "biases_exp")
+CODE_BITS = (2, 3, 4, 8)
+SCALE_FMTS = ("bf16", "fp8")
+
+
+def code_row_bytes(n_in, bits):
+    """Bytes of one row of codes: n_in*bits/8, rounded up to 16 (only 3-bit
+    rows whose n_in is not a multiple of 128 carry padding)."""
+    return -(-(n_in * bits // 8) // 16) * 16
 
 
 @dataclass(frozen=True)
@@ -31,6 +42,7 @@ class Geometry:
     group_size: int = 64
     bits: int = 4
     norm_topk_prob: bool = True
+    scale_fmt: str = "bf16"
     components: tuple = field(default=(), compare=False)
     payload_bytes: int = 0
     blob_bytes: int = 0
@@ -76,22 +88,67 @@ class Geometry:
         return g
 
 
-def layout(d_model, d_ff, group_size=64, bits=4, proj_bias=False):
-    """(components, payload_bytes, blob_bytes) for one expert."""
-    parts = PARTS if proj_bias else PARTS[:3]
+def layout(d_model, d_ff, group_size=64, bits=4, proj_bias=False, scale_fmt="bf16"):
+    """(components, payload_bytes, blob_bytes) for one expert. The default
+    (4 bits, bf16) is the reference's layout; other precision classes keep
+    the component order and add, for fp8 scales, the per-row exponents
+    (scales_exp, biases_exp) after the biases. Offsets are 16-byte aligned."""
+    fp8 = scale_fmt == "fp8"
+    parts = ["weight", "scales", "biases"] + (["scales_exp", "biases_exp"] if fp8 else [])
+    parts += ["bias"] if proj_bias else []
     comps, off = [], 0
     for proj in PROJS:
         n_out, n_in = (d_model, d_ff) if proj == "down_proj" else (d_ff, d_model)
+        G = n_in // group_size
         for part in parts:
             if part == "weight":
-                dt, shape, nb = "U32", [n_out, n_in * bits // 32], n_out * n_in * bits // 8
+                rb = code_row_bytes(n_in, bits)
+                dt, shape, nb = "U32", [n_out, rb // 4], n_out * rb
             elif part == "bias":
                 dt, shape, nb = "BF16", [n_out], n_out * 2
+            elif part in ("scales_exp", "biases_exp"):
+                dt, shape, nb = "U8", [n_out], n_out
+            elif fp8:
+                dt, shape, nb = "F8E4M3", [n_out, G], n_out * G
             else:
-                dt, shape, nb = "BF16", [n_out, n_in // group_size], n_out * (n_in // group_size) * 2
+                dt, shape, nb = "BF16", [n_out, G], n_out * G * 2
             comps.append(dict(proj=proj, part=part, dtype=dt, shape=shape, offset=off, nbytes=nb))
-            off += nb
+            off += -(-nb // 16) * 16
     return tuple(comps), off, -(-off // PAGE) * PAGE
+
+
+def precision(geom, bits, scale_fmt="bf16"):
+    """The geometry of geom's experts stored as precision class (bits,
+    scale_fmt): same shapes, that class's blob layout and size."""
+    if bits not in CODE_BITS or scale_fmt not in SCALE_FMTS:
+        raise ValueError(f"unsupported precision class ({bits}, {scale_fmt})")
+    comps, payload, blob = layout(geom.d_model, geom.d_ff, geom.group_size, bits, geom.proj_bias,
+                                  scale_fmt)
+    return dataclasses.replace(geom, bits=bits, scale_fmt=scale_fmt, components=comps,
+                               payload_bytes=payload, blob_bytes=blob)
+
+
+def slot_geometry(base, classes):
+    """The pool geometry for experts in `classes` (precision geometries of
+    base): base's own 4-bit layout, with the slot and store stride of the
+    largest class."""
+    blob = max([base.blob_bytes] + [c.blob_bytes for c in classes])
+    return dataclasses.replace(base, blob_bytes=blob)
+
+
+def to_prec_c(cg):
+    """ms_prec of a precision geometry (precision())."""
+    p = _lib.MsPrec()
+    p.bits = cg.bits
+    p.scale_fmt = _lib.SCALE_FP8 if cg.scale_fmt == "fp8" else _lib.SCALE_BF16
+    p.payload_bytes = -(-cg.payload_bytes // 16) * 16
+    for i, proj in enumerate(PROJS):
+        for j, part in enumerate(PREC_PARTS):
+            try:
+                p.comp_offset[i][j] = cg.comp(proj, part)["offset"]
+            except KeyError:
+                p.comp_offset[i][j] = -1
+    return p
 
 
 def make(model, d_model, d_ff, n_experts, n_layers, top_k, norm_topk_prob=True):

@@ -33,7 +33,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .geometry import PROJS, PARTS, Geometry, from_index
+from .geometry import PROJS, PARTS, Geometry, from_index, to_prec_c
 
 
 def _stream_ptr(stream):
@@ -235,6 +235,23 @@ class ExpertPool:
         """engine_v3.py:215: {(layer, expert): slot}."""
         return {(int(k) // self.n_experts, int(k) % self.n_experts): s
                 for s, k in enumerate(self.table()) if k >= 0}
+
+    def set_precision(self, classes, class_of_key):
+        """Per-expert precision: blob (layer, expert) is stored as precision
+        class classes[class_of_key[layer * n_experts + expert]] (geometries
+        from geometry.precision of this pool's geometry; the pool's blob
+        stride must hold the largest, see geometry.slot_geometry). Call
+        before the first slot fill. Store blobs keep the pool's stride; each
+        holds its class's payload from its start."""
+        classes = list(classes)
+        arr = (_lib.MsPrec * len(classes))(*[to_prec_c(c) for c in classes])
+        cok = np.ascontiguousarray(class_of_key, dtype=np.uint8)
+        if cok.size != self.geom.n_keys:
+            raise ValueError(f"class_of_key has {cok.size} entries, the pool {self.geom.n_keys} keys")
+        _lib.check(self._lib.ms_pool_set_precision(self._h, len(classes), ctypes.byref(arr),
+                                                   ctypes.c_void_p(cok.ctypes.data)))
+        self.classes = classes
+        self.class_of_key = cok.copy()
 
     def status(self, stream=None):
         """Raise the first device-side error of earlier asynchronous calls."""

@@ -47,6 +47,90 @@ def quantize(w, group_size=64, bits=4):
             biases.reshape(sshape).to(torch.bfloat16))
 
 
+def _affine_params(g, bits):
+    """MLX affine scales and biases (float32, unrounded) of groups g [..., gs]."""
+    n_bins = torch.tensor(float((1 << bits) - 1), dtype=torch.float32, device=g.device)
+    eps = torch.tensor(1e-7, dtype=torch.float32, device=g.device)
+    w_max = g.amax(dim=-1, keepdim=True)
+    w_min = g.amin(dim=-1, keepdim=True)
+    mask = w_min.abs() > w_max.abs()
+    scales = torch.maximum((w_max - w_min) / n_bins, eps)
+    scales = torch.where(mask, scales, -scales)
+    edge = torch.where(mask, w_min, w_max)
+    q0 = torch.round(edge / scales)
+    scales = torch.where(q0 != 0, edge / q0, scales)
+    biases = torch.where(q0 == 0, torch.zeros_like(edge), edge)
+    return scales, biases
+
+
+def fp8_rows(v):
+    """Per-row fp8 storage of v [rows, G] (float32): OCP E4M3 codes (uint8)
+    of v * 2^(127 - E) and one exponent byte E per row, E the smallest with
+    max|v_row| * 2^(127 - E) <= 448 (127 for an all-zero row). Returns
+    (codes, exps, decoded float32 values)."""
+    amax = v.abs().amax(dim=-1)
+    m, e = torch.frexp(amax / 448.0)
+    up = torch.where(m > 0.5, e, e - 1)                 # ceil(log2(amax / 448))
+    E = torch.where(amax > 0, 127 + up, torch.full_like(up, 127)).clamp(1, 254)
+    scaled = torch.ldexp(v, (127 - E).unsqueeze(-1).to(v.dtype))
+    codes8 = scaled.to(torch.float8_e4m3fn)
+    dec = torch.ldexp(codes8.to(torch.float32), (E - 127).unsqueeze(-1).to(v.dtype))
+    return codes8.view(torch.uint8), E.to(torch.uint8), dec
+
+
+def pack_codes(q, bits, row_bytes):
+    """Codes q [..., K] (int64 in [0, 2^bits)) as each row's little-endian
+    bit stream (code j at bit bits*j), rows padded to row_bytes: uint8."""
+    shp = q.shape
+    K = shp[-1]
+    if bits == 3:
+        q = q.reshape(*shp[:-1], K // 8, 8)
+        v = (q << (torch.arange(8, device=q.device, dtype=torch.int64) * 3)).sum(-1)
+        by = torch.stack([(v >> (8 * i)) & 0xFF for i in range(3)], dim=-1)
+    else:
+        per = 8 // bits
+        q = q.reshape(*shp[:-1], K // per, per)
+        by = (q << (torch.arange(per, device=q.device, dtype=torch.int64) * bits)).sum(-1)
+    by = by.reshape(*shp[:-1], -1).to(torch.uint8)
+    pad = row_bytes - by.shape[-1]
+    if pad:
+        by = torch.cat([by, torch.zeros(*shp[:-1], pad, dtype=torch.uint8, device=q.device)], -1)
+    return by
+
+
+def quantize_class(w, group_size=64, bits=4, scale_fmt="bf16"):
+    """Affine quantisation of w [..., K] into precision class (bits,
+    scale_fmt). bf16: mx.quantize (codes from the unrounded float32 scales,
+    scales and biases stored as bf16). fp8: scales and biases stored per row
+    as E4M3 times 2^(E - 127) (fp8_rows), and the codes computed against
+    those stored values, so the codes fit what the kernels will decode.
+    Returns {part: tensor} with weight as uint8 [..., row_bytes]."""
+    from .geometry import code_row_bytes
+    w = w.to(torch.float32)
+    shp = w.shape
+    K = shp[-1]
+    g = w.reshape(-1, K // group_size, group_size)
+    scales, biases = _affine_params(g, bits)
+    out = {}
+    if scale_fmt == "fp8":
+        rows = g.shape[0]
+        sc, se, sd = fp8_rows(scales.reshape(rows, -1))
+        bc, be, bd = fp8_rows(biases.reshape(rows, -1))
+        scales, biases = sd.unsqueeze(-1), bd.unsqueeze(-1)
+        out.update(scales=sc.reshape(*shp[:-1], -1), biases=bc.reshape(*shp[:-1], -1),
+                   scales_exp=se.reshape(shp[:-1]), biases_exp=be.reshape(shp[:-1]))
+        safe = torch.where(scales != 0, scales, torch.ones_like(scales))
+        q = torch.where(scales != 0, torch.round((g - biases) / safe), torch.zeros_like(g))
+    else:
+        sshape = (*shp[:-1], K // group_size)
+        out.update(scales=scales.reshape(sshape).to(torch.bfloat16),
+                   biases=biases.reshape(sshape).to(torch.bfloat16))
+        q = torch.round((g - biases) / scales)
+    q = torch.clamp(q, 0, float((1 << bits) - 1)).to(torch.int64).reshape(shp)
+    out["weight"] = pack_codes(q, bits, code_row_bytes(K, bits))
+    return out
+
+
 def _gen(seed, layer, expert, device):
     g = torch.Generator(device=device)
     g.manual_seed(seed * 1_000_003 + layer * 1009 + expert)
@@ -72,9 +156,13 @@ def pack_blob(geom, weights):
     """One expert's blob (uint8 tensor [blob_bytes]) from its weights."""
     dev = next(iter(weights.values())).device
     blob = torch.zeros(geom.blob_bytes, dtype=torch.uint8, device=dev)
+    default = geom.bits == 4 and geom.scale_fmt == "bf16"
     for proj in PROJS:
-        q, s, b = quantize(weights[proj], geom.group_size, geom.bits)
-        parts = {"weight": q, "scales": s, "biases": b}
+        if default:
+            q, s, b = quantize(weights[proj], geom.group_size, geom.bits)
+            parts = {"weight": q, "scales": s, "biases": b}
+        else:
+            parts = quantize_class(weights[proj], geom.group_size, geom.bits, geom.scale_fmt)
         if geom.proj_bias:
             parts["bias"] = weights[proj + ".bias"]
         for part, t in parts.items():
@@ -100,6 +188,23 @@ def fill_store(geom, host_u8, seed, layers=None, experts=None, device="cpu", bat
             key = layer * geom.n_experts + e
             blob = make_blob(geom, seed, layer, e, device)
             view[key * geom.blob_bytes:(key + 1) * geom.blob_bytes].copy_(blob, non_blocking=False)
+
+
+def fill_store_classes(slot_geom, classes, class_of_key, host_u8, seed, layers=None, experts=None,
+                       device="cpu"):
+    """fill_store for a pool with precision classes: blob (layer, expert) is
+    make_blob of its class geometry (same seeded weights as the 4-bit
+    store), written at the pool's stride slot_geom.blob_bytes."""
+    layers = range(slot_geom.n_layers) if layers is None else layers
+    experts = range(slot_geom.n_experts) if experts is None else experts
+    view = torch.from_numpy(host_u8) if isinstance(host_u8, np.ndarray) else host_u8
+    stride = slot_geom.blob_bytes
+    for layer in layers:
+        for e in experts:
+            key = layer * slot_geom.n_experts + e
+            cg = classes[int(class_of_key[key])]
+            blob = make_blob(cg, seed, layer, e, device)
+            view[key * stride:key * stride + cg.blob_bytes].copy_(blob, non_blocking=False)
 
 
 def router_weights(geom, seed, layer, device="cpu", std=0.02, zipf_s=None, bias_std=None):

@@ -21,7 +21,7 @@ therefore compare index SETS and accept differences only at exact ties.
 import numpy as np
 
 from . import bf16
-from .quant import dequantize_f32, dequantize_bf16
+from .quant import dequantize_f32, dequantize_bf16, dequantize_class_f32
 
 PAGE = 16384
 PROJS = ("gate_proj", "up_proj", "down_proj")
@@ -54,6 +54,8 @@ def blob_views(blob, comps):
         raw = blob[c["offset"]:c["offset"] + c["nbytes"]]
         if c["dtype"] == "U32":
             a = np.frombuffer(raw.tobytes(), dtype=np.uint32)
+        elif c["dtype"] in ("F8E4M3", "U8"):
+            a = np.frombuffer(raw.tobytes(), dtype=np.uint8)
         else:
             a = np.frombuffer(raw.tobytes(), dtype=np.uint16)
         out[f"{c['proj']}.{c['part']}"] = a.reshape(c["shape"])
@@ -115,9 +117,29 @@ def predict(x, w_r_next, kp, bias_next=None):
 
 
 # ------------------------------------------------------------ expert math
-def _deq(v, name, group_size, rounded=False):
+def _deq(v, name, group_size, rounded=False, prec=None):
+    """Dequantised weight of projection `name`. prec: None for the default
+    4-bit bf16 blob, else (bits, scale_fmt, n_in) of a precision class."""
+    if prec is not None:
+        bits, fmt, K = prec
+        parts = {p: v[f"{name}.{p}"] for p in ("weight", "scales", "biases", "scales_exp", "biases_exp")
+                 if f"{name}.{p}" in v}
+        parts["weight"] = parts["weight"].view(np.uint8)
+        w = dequantize_class_f32(parts, K, bits, fmt, group_size)
+        return bf16.r(w) if rounded else w
     f = dequantize_bf16 if rounded else dequantize_f32
     return f(v[f"{name}.weight"], v[f"{name}.scales"], v[f"{name}.biases"], group_size)
+
+
+def _views_prec(blobs, comps, prec, e, d_model, d_ff):
+    """Component views of expert e's blob and a function giving each
+    projection's precision argument for _deq (prec: {e: (comps, bits, fmt)}
+    for experts stored in a precision class)."""
+    if prec is not None and e in prec:
+        ce, bits, fmt = prec[e]
+        n_in = {"gate_proj": d_model, "up_proj": d_model, "down_proj": d_ff}
+        return blob_views(blobs[e], ce), (lambda name: (bits, fmt, n_in[name]))
+    return blob_views(blobs[e], comps), (lambda name: None)
 
 
 def _mm_bf16(inp, w):
@@ -159,37 +181,43 @@ def _pairs_by_expert(inds):
     return by
 
 
-def expert_block(x, inds, scores, blobs, comps, model, group_size=64):
+def expert_block(x, inds, scores, blobs, comps, model, group_size=64, prec=None):
     """MLX-path block output for tokens x [T,d] (bf16 values).
 
     inds [T,k] select blobs (blobs[e] is a uint8 blob); scores [T,k] bf16
     values. Returns y [T,d] as bf16 values. Each expert is dequantised once.
     Qwen3: engine_v3.py:588-600. gpt-oss: engine_120b.py:130-145.
+    prec: {e: (comps, bits, scale_fmt)} for experts stored in a precision
+    class (their products use the class's unrounded s*q + b, as the 4-bit
+    path does).
     """
     x = np.asarray(x, np.float32)
     T, K = inds.shape
     d = x.shape[-1]
     parts = np.zeros((T, K, d), np.float32)
     for e, prs in _pairs_by_expert(inds).items():
-        v = blob_views(blobs[e], comps)
+        d_ff = None
+        if prec is not None and e in prec:
+            d_ff = [c for c in prec[e][0] if c["proj"] == "down_proj" and c["part"] == "scales"][0]["shape"][1] * group_size
+        v, pa = _views_prec(blobs, comps, prec, e, d, d_ff)
         xt = x[[t for t, _ in prs]]
-        up = _mm_bf16(xt, _deq(v, "up_proj", group_size))
-        gate = _mm_bf16(xt, _deq(v, "gate_proj", group_size))
+        up = _mm_bf16(xt, _deq(v, "up_proj", group_size, prec=pa("up_proj")))
+        gate = _mm_bf16(xt, _deq(v, "gate_proj", group_size, prec=pa("gate_proj")))
         if model == "gptoss":
             up = bf16.r(up + bf16.from_bits(v["up_proj.bias"]))
             gate = bf16.r(gate + bf16.from_bits(v["gate_proj.bias"]))
             h = swiglu_gptoss(up, gate)
-            yj = _mm_bf16(h, _deq(v, "down_proj", group_size))
+            yj = _mm_bf16(h, _deq(v, "down_proj", group_size, prec=pa("down_proj")))
             yj = bf16.r(yj + bf16.from_bits(v["down_proj.bias"]))
         else:
             h = swiglu_qwen3(gate, up)
-            yj = _mm_bf16(h, _deq(v, "down_proj", group_size))
+            yj = _mm_bf16(h, _deq(v, "down_proj", group_size, prec=pa("down_proj")))
         for i, (t, j) in enumerate(prs):
             parts[t, j] = bf16.r(yj[i] * np.float32(scores[t, j]))
     return bf16.r(parts.sum(axis=1, dtype=np.float32))
 
 
-def fp32_reference(x, inds, scores, blobs, comps, model, group_size=64):
+def fp32_reference(x, inds, scores, blobs, comps, model, group_size=64, prec=None):
     """test_kernel.py:52-65: dequantise (bf16 weights, as mx.dequantize
     returns them), then the whole MLP in fp32 (float64 here). gpt-oss adds
     its biases and the clamped activation at full precision as well."""
@@ -197,8 +225,11 @@ def fp32_reference(x, inds, scores, blobs, comps, model, group_size=64):
     T, K = inds.shape
     y = np.zeros((T, x.shape[-1]), np.float64)
     for e, prs in _pairs_by_expert(inds).items():
-        v = blob_views(blobs[e], comps)
-        w = {p: _deq(v, p, group_size, rounded=True).astype(np.float64) for p in PROJS}
+        d_ff = None
+        if prec is not None and e in prec:
+            d_ff = [c for c in prec[e][0] if c["proj"] == "down_proj" and c["part"] == "scales"][0]["shape"][1] * group_size
+        v, pa = _views_prec(blobs, comps, prec, e, x.shape[-1], d_ff)
+        w = {p: _deq(v, p, group_size, rounded=True, prec=pa(p)).astype(np.float64) for p in PROJS}
         xt = x[[t for t, _ in prs]]
         gate = xt @ w["gate_proj"].T
         up = xt @ w["up_proj"].T
