@@ -57,6 +57,8 @@ def parse():
                     help="most untimed pre-roll tokens")
     ap.add_argument("--no-ep", action="store_true",
                     help="skip the expert-parallel measurement of the default run")
+    ap.add_argument("--no-mixed", action="store_true",
+                    help="skip the per-expert mixed-precision decode measurement")
     ap.add_argument("--case", choices=["stack", "layer", "prefill", "ep"], default="stack",
                     help="layer: a 2-layer Qwen3 stack with every expert resident (a small "
                          "case for ncu section captures); prints per-call timings only. "
@@ -563,6 +565,101 @@ def profile_traffic():
 
 
 # -------------------------------------------------------------- GPU arm
+MIXED_CLASSES = ((4, "bf16"), (4, "fp8"), (3, "fp8"), (2, "fp8"))
+MIXED_FRACS = (0.30, 0.30, 0.25, 0.15)
+
+
+def mixed_measure(args, dev, K, W):
+    """The config-1 decode stack with per-expert precision classes: each
+    (layer, expert) drawn into 4-bit bf16 / 4-bit fp8 / 3-bit fp8 / 2-bit
+    fp8 scales with probabilities MIXED_FRACS (a seeded stand-in for the
+    sensitivity-keyed allocation the reference plans: the weights here are
+    random, so no expert is more sensitive than another). Same weights,
+    routers, hidden states, pool size and steady-state pre-roll as the main
+    line; reports tok/s and the expert bytes the kernels read per token."""
+    import numpy as np
+    import torch
+    from moe_stream_b200 import geometry, store as S
+    from moe_stream_b200.block import DecodeGraph, MoEBlock, route
+    from moe_stream_b200.pool import ExpertPool
+
+    geom = geometry.qwen3(N_LAYERS)
+    classes = [geometry.precision(geom, b, f) for b, f in MIXED_CLASSES]
+    sg = geometry.slot_geometry(geom, classes)
+    cok = np.random.default_rng(SEED + 77).choice(len(classes), size=geom.n_keys,
+                                                  p=MIXED_FRACS).astype(np.uint8)
+    pool = ExpertPool(sg, N_SLOTS, evict="lfu", depths=(1,), pf_widen=1, max_tokens=1)
+    pool.set_precision(classes, cok)
+    store = pool.alloc_store()
+    st_t = torch.from_numpy(store).view(geom.n_keys, sg.blob_bytes)
+    E = geom.n_experts
+    for layer in range(N_LAYERS):
+        blobs = S.make_layer_blobs_classes(sg, classes, cok[layer * E:(layer + 1) * E], SEED, layer,
+                                           device=dev)
+        st_t[layer * E:(layer + 1) * E].copy_(blobs)
+        del blobs
+    torch.cuda.synchronize()
+    routers = [S.router_weights(geom, SEED, l, zipf_s=1.1) for l in range(N_LAYERS)]
+    blocks = [MoEBlock(pool, l, w, b) for l, (w, b) in enumerate(routers)]
+    PR = args.preroll_max
+    X = S.decode_inputs(PR + W + K, N_LAYERS, geom.d_model, SEED + 1000 * 0).to(dev)
+    for layer, b in enumerate(blocks):
+        b(X[0, layer:layer + 1])
+    torch.cuda.synchronize()
+    g = DecodeGraph(blocks, T=1)
+    used, hist, roll = 1, [pool.stats()], 0.0
+    while used < PR:
+        n = min(16, PR - used)
+        for t in range(used, used + n):
+            g.step(X[t].unsqueeze(1))
+        used += n
+        hist.append(pool.stats())
+        back = hist[max(0, len(hist) - 3)]
+        roll = (hist[-1]["cache"] - back["cache"]) / max(1, hist[-1]["total"] - back["total"])
+        if used >= 64 and roll >= args.hit_target:
+            break
+    for t in range(used, used + W):
+        g.step(X[t].unsqueeze(1))
+    t0 = used + W
+    torch.cuda.synchronize()
+    pool.status()
+    s0 = pool.stats()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for t in range(t0, t0 + K):
+        g.step(X[t].unsqueeze(1))
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    pool.status()
+    s1 = pool.stats()
+    # bytes the expert kernels read: the payload of every routed expert's
+    # class (routing only: ms_route leaves the pool untouched)
+    pay = torch.tensor([classes[c].payload_bytes for c in cok], dtype=torch.float64, device=dev)
+    nbytes = torch.zeros((), dtype=torch.float64, device=dev)
+    for t in range(t0, t0 + K):
+        for layer, b in enumerate(blocks):
+            inds, _ = route(b, X[t, layer:layer + 1])
+            nbytes += pay[layer * E + inds.long()].sum()
+    bpt = float(nbytes.item()) / K
+    uniform = N_LAYERS * geom.top_k * geom.payload_bytes
+    frac = np.bincount(cok, minlength=len(classes)) / cok.size
+    out = {"classes": [f"{b}-bit {f}" for b, f in MIXED_CLASSES],
+           "class_fraction": [round(float(v), 4) for v in frac],
+           "tok_s": K / (ms / 1e3), "ms_per_token": ms / K, "steps": K,
+           "expert_bytes_per_token": bpt,
+           "expert_bytes_per_token_uniform_4bit": uniform,
+           "bytes_ratio_vs_uniform": bpt / uniform,
+           "cache_hit": (s1["cache"] - s0["cache"]) / max(1, s1["total"] - s0["total"]),
+           "h2d_fill_bytes_per_token": (s1["gb"] - s0["gb"]) * 2 ** 30 / K,
+           "preroll_tokens": used,
+           "kernels": "k_up_mx / k_down_mx (per-class decode kernels)"}
+    pool.close()
+    del store, st_t, X
+    torch.cuda.empty_cache()
+    return out
+
+
 def gpu_arm(args):
     import ctypes
     import torch
@@ -743,6 +840,10 @@ def gpu_arm(args):
     del store, st_t, X
     torch.cuda.empty_cache()
 
+    mixed = None
+    if not args.no_mixed and TB == 1:
+        mixed = mixed_measure(args, dev, max(3, min(K, 64)), max(3, min(W, 8)))
+
     ep = None
     if not args.no_ep and TB == 1:
         ep = ep_measure(args, world, rank, dev, max(3, min(K, 10)), 3)
@@ -763,6 +864,7 @@ def gpu_arm(args):
                        "l2": "inputs larger than L2: 1.02 GB of expert weights per step"},
             "hit_rate": hit,
             "expert_hbm_gbs": achieved,
+            "expert_bytes_per_token": bytes_per_layer * N_LAYERS,
             "per_layer_us": {"router_table": per_layer[0] * 1e3, "fill": per_layer[1] * 1e3,
                              "experts": expert_ms * 1e3},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
@@ -780,6 +882,8 @@ def gpu_arm(args):
             "clocks": clk,
             "setup_s": {"store_generation": t_gen},
         }
+        if mixed is not None:
+            line["mixed_precision"] = mixed
         if ep is not None:
             line["expert_parallel"] = ep
         print(json.dumps(line))

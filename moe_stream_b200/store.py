@@ -264,6 +264,43 @@ def make_layer_blobs(geom, seed, layer, device="cuda", std=0.02, chunk=32):
     return out
 
 
+def make_layer_blobs_classes(geom, classes, cls_of_e, seed, layer, device="cuda", std=0.02,
+                             chunk=32):
+    """make_layer_blobs for experts stored in precision classes: the same
+    weights (same generator and draw order), each expert quantised into
+    classes[cls_of_e[e]] and laid out at the start of its row of the result
+    (uint8 [n_experts, geom.blob_bytes], geom the pool's slot geometry)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1_000_003 + layer * 1009 + 977)
+    E = geom.n_experts
+    cls_of_e = torch.as_tensor(np.asarray(cls_of_e, np.int64), device=device)
+    out = torch.zeros(E, geom.blob_bytes, dtype=torch.uint8, device=device)
+    for e0 in range(0, E, chunk):
+        n = min(chunk, E - e0)
+        cl = cls_of_e[e0:e0 + n]
+        for proj in PROJS:
+            n_out, n_in = (geom.d_model, geom.d_ff) if proj == "down_proj" else (geom.d_ff, geom.d_model)
+            w = (torch.randn(n, n_out, n_in, generator=g, device=device) * std)
+            w = w.to(torch.bfloat16).to(torch.float32)
+            bias = None
+            if geom.proj_bias:
+                bias = (torch.randn(n, n_out, generator=g, device=device) * std).to(torch.bfloat16)
+            for c, cg in enumerate(classes):
+                idx = torch.nonzero(cl == c).flatten()
+                if idx.numel() == 0:
+                    continue
+                parts = quantize_class(w[idx], cg.group_size, cg.bits, cg.scale_fmt)
+                if bias is not None:
+                    parts["bias"] = bias[idx]
+                rows = e0 + idx
+                for part, t in parts.items():
+                    comp = cg.comp(proj, part)
+                    raw = t.contiguous().view(torch.uint8).reshape(idx.numel(), -1)
+                    out[rows, comp["offset"]:comp["offset"] + comp["nbytes"]] = raw
+            del w
+    return out
+
+
 def decode_inputs(n_steps, n_layers, d, seed, step_sigma=0.1):
     """Config-1 hidden states: per decode step an i.i.d. h_0 ~ N(0,1), then
     h_{l+1} = h_l + step_sigma * N(0,1); the block input of layer l is
