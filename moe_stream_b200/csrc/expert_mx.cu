@@ -7,13 +7,14 @@
 //   k_up_mx   one CTA per (16-row tile of d_ff, group of pairs sharing a
 //             slot), the input dimension over 8 warps, SwiGLU in the
 //             epilogue, h in the frag layout with its per-tile sums.
-//   k_down_mx one CTA per (16-row tile of d_model, group); the last CTA of a
-//             row tile combines each token's k expert rows in a fixed order.
+//   k_down_mx one CTA per (RT 16-row tiles of d_model, group); the last CTA
+//             of a row tile combines each token's k expert rows in a fixed
+//             order.
 //
-// A tile's bytes shrink with its class (16 rows x d*bits/8 codes), and the
-// copies move exactly those bytes: one per row into padded shared-memory
-// rows when a row is whole 16-byte units, else the tile as one copy. The
-// uniform 4-bit bf16 pools keep the tuned kernels of expert.cu.
+// A tile's bytes shrink with its class (16 rows x d*bits/8 codes, rows
+// padded to 16 bytes), and the copies move exactly those bytes, one per row
+// into padded shared-memory rows. The uniform 4-bit bf16 pools keep the
+// tuned kernels of expert.cu.
 #include "ms_common.cuh"
 #include "frag.cuh"
 #include "tma.cuh"
@@ -64,26 +65,26 @@ __device__ __forceinline__ void tile_dot_mx(float* tot, const uint8_t* At, int s
   }
 }
 
-// Copies of a tile of `rows` rows (from row r0 of projection proj) issued by
-// one lane of warp 0, `l` being its index among the lanes serving this
-// tile: lane l < rows copies code row l into its padded shared-memory row;
-// lanes rows .. rows+3 copy the scales, the biases and (fp8) their row
-// exponents. Lane 0 of the warp has armed `bar` for stage_bytes.
+// Copies of a tile of `rows` rows (from row r0 of projection proj) into
+// shared memory, issued by the lanes of warp 0: this lane copies code row
+// `row` (when in [0, rows)) into its padded row, and copy `sbc` (0 scales,
+// 1 biases, fp8: 2 and 3 their row exponents) when in [0, 4). Lane 0 of the
+// warp has armed `bar` for stage_bytes.
 template <int BITS>
 __device__ __forceinline__ void stage_rows(uint8_t* sA, uint8_t* sS, uint8_t* sB, uint8_t* sE,
                                            const uint8_t* blob, const PrecDev& pc, int proj,
                                            int r0, int rows, int K, uint64_t* bar, uint64_t pol,
-                                           int l) {
+                                           int row, int sbc) {
   const int rb = code_row_bytes(K, BITS), stride = mx_stride(K, BITS), G = K / 64;
   const uint8_t* W = blob + pc.off[proj][P_W] + (long long)r0 * rb;
-  if (l >= 0 && l < rows) bulk_g2s_hint(sA + l * stride, W + (long long)l * rb, rb, bar, pol);
+  if (row >= 0 && row < rows) bulk_g2s_hint(sA + row * stride, W + (long long)row * rb, rb, bar, pol);
   const int esz = pc.fmt == SF_FP8 ? 1 : 2;
   const unsigned sbn = (unsigned)(rows * G * esz);
-  if (l == rows) bulk_g2s_hint(sS, blob + pc.off[proj][P_S] + (long long)r0 * G * esz, sbn, bar, pol);
-  if (l == rows + 1) bulk_g2s_hint(sB, blob + pc.off[proj][P_B] + (long long)r0 * G * esz, sbn, bar, pol);
+  if (sbc == 0) bulk_g2s_hint(sS, blob + pc.off[proj][P_S] + (long long)r0 * G * esz, sbn, bar, pol);
+  if (sbc == 1) bulk_g2s_hint(sB, blob + pc.off[proj][P_B] + (long long)r0 * G * esz, sbn, bar, pol);
   if (pc.fmt == SF_FP8) {
-    if (l == rows + 2) bulk_g2s_hint(sE, blob + pc.off[proj][P_SE] + r0, (unsigned)rows, bar, pol);
-    if (l == rows + 3) bulk_g2s_hint(sE + rows, blob + pc.off[proj][P_BE] + r0, (unsigned)rows, bar, pol);
+    if (sbc == 2) bulk_g2s_hint(sE, blob + pc.off[proj][P_SE] + r0, (unsigned)rows, bar, pol);
+    if (sbc == 3) bulk_g2s_hint(sE + rows, blob + pc.off[proj][P_BE] + r0, (unsigned)rows, bar, pol);
   }
 }
 
@@ -123,9 +124,10 @@ __device__ __forceinline__ void up_body(const ExpArgs& A, const PrecDev& pc, int
     const uint64_t pol = l2_evict_first();
     // gate: rows on lanes 0-15, its scale copies on lanes 16-19; up: rows
     // on lanes 16-31, its scale copies on lanes 0-3
-    stage_rows<BITS>(sA[0], sS[0], sB[0], sE, blob, pc, 0, rt * 16, 16, K, bar, pol, lane);
+    stage_rows<BITS>(sA[0], sS[0], sB[0], sE, blob, pc, 0, rt * 16, 16, K, bar, pol,
+                     lane < 16 ? lane : -1, lane - 16);
     stage_rows<BITS>(sA[1], sS[1], sB[1], sE + 32, blob, pc, 1, rt * 16, 16, K, bar, pol,
-                     (lane + 16) & 31);
+                     lane >= 16 ? lane - 16 : -1, lane);
   }
   __syncthreads();
   bool ok = true, waited = false;
@@ -206,9 +208,11 @@ __device__ __forceinline__ void up_body(const ExpArgs& A, const PrecDev& pc, int
   }
 }
 
+// Qwen3 shapes: three CTAs per SM, so a batch-1 layer's 384 tiles fit one
+// wave (as k_up).
 template <int MODEL, int KPW>
-__global__ void __launch_bounds__(EX_THREADS, 2) k_up_mx(ExpArgs A, const __grid_constant__ ClassTab C,
-                                                          int a_cap) {
+__global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2)
+    k_up_mx(ExpArgs A, const __grid_constant__ ClassTab C, int a_cap) {
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_wait();
   pdl_trigger();
@@ -227,21 +231,25 @@ __global__ void __launch_bounds__(EX_THREADS, 2) k_up_mx(ExpArgs A, const __grid
   }
 }
 
-template <int MODEL, int KPW, int BITS>
+template <int MODEL, int KPW, int RT, int BITS>
 __device__ __forceinline__ void down_body(const ExpArgs& A, const PrecDev& pc, int slot, int m,
                                           int start, uint8_t* smem, int a_cap) {
+  constexpr int WPT = EX_WARPS / RT;            // warps per row tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g4 = lane >> 2, c = lane & 3;
-  const int rt = blockIdx.x;
+  const int sub = warp / WPT, wk = warp % WPT;
+  const int rt = blockIdx.x * RT + sub;
   const int K = A.geo.d_ff, G = K / 64, D = A.geo.d_model;
   const int stride = mx_stride(K, BITS);
-  const int kg0 = min(G, warp * KPW), kg1 = min(G, kg0 + KPW);
+  const int kg0 = min(G, wk * KPW), kg1 = min(G, kg0 + KPW);
   const int nt_ff = K / 16;
+  const int esz = pc.fmt == SF_FP8 ? 1 : 2;
+  // [codes | scales | biases | exps (s, b) | red | sums | bar]
   uint8_t* sA = smem;
-  const int sbb = MxTile::sb_bytes(K, 16);
+  const int sbb = MxTile::sb_bytes(K, RT * 16);
   uint8_t* sS = smem + a_cap;
   uint8_t* sB = sS + sbb;
-  uint8_t* sE = sB + sbb;                      // [s/b][16]
-  float* red = reinterpret_cast<float*>(sE + 32);
+  uint8_t* sE = sB + sbb;
+  float* red = reinterpret_cast<float*>(sE + 32 * RT);
   float* s_sums = red + EX_WARPS * 4 * 32;      // [8][G][2]
   uint64_t* bar = reinterpret_cast<uint64_t*>(s_sums + 8 * G * 2);
 
@@ -250,16 +258,21 @@ __device__ __forceinline__ void down_body(const ExpArgs& A, const PrecDev& pc, i
     if (lane == 0) {
       mbar_init(bar, 1);
       fence_barrier_init();
-      mbar_expect_tx(bar, stage_bytes<BITS>(K, 16, pc.fmt));
+      mbar_expect_tx(bar, stage_bytes<BITS>(K, RT * 16, pc.fmt));
     }
     __syncwarp();
-    stage_rows<BITS>(sA, sS, sB, sE, blob, pc, 2, rt * 16, 16, K, bar, l2_evict_first(), lane);
+    // the RT*16 rows one or two per lane, the scale copies on lanes 0-3
+    const uint64_t pol = l2_evict_first();
+    for (int r = lane; r < RT * 16; r += 32)
+      stage_rows<BITS>(sA, sS, sB, sE, blob, pc, 2, blockIdx.x * RT * 16, RT * 16, K, bar, pol, r,
+                       r == lane ? lane : -1);
   }
   pdl_wait();                                   // h and its sums come from k_up_mx
   __syncthreads();
   bool ok = true;
   if (slot >= 0) ok = mbar_wait(bar, 0, A.status);
-  const SBTile sb{sS, sB, sE, sE + 16, G, pc.fmt == SF_FP8};
+  const SBTile sb{sS + sub * 16 * G * esz, sB + sub * 16 * G * esz, sE + sub * 16, sE + RT * 16 + sub * 16,
+                  G, pc.fmt == SF_FP8};
 
   for (int n0 = 0; n0 < m; n0 += 8) {
     const int* pairs = A.grp.grp_pairs + start + n0;
@@ -282,16 +295,16 @@ __device__ __forceinline__ void down_body(const ExpArgs& A, const PrecDev& pc, i
                    (2 * c + 1 < nn) ? s_sums + (2 * c + 1) * G * 2 : nullptr, kg0, kg1);
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
     if (slot >= 0 && ok && kg0 < kg1)
-      tile_dot_mx<KPW, BITS>(tot, sA, stride, kg0, kg1, g4, c, sb, b0, b1, v0, v1);
+      tile_dot_mx<KPW, BITS>(tot, sA + sub * 16 * stride, stride, kg0, kg1, g4, c, sb, b0, b1, v0, v1);
 #pragma unroll
     for (int i = 0; i < 4; ++i) red[(warp * 4 + i) * 32 + lane] = tot[i];
     __syncthreads();
-    if (warp == 0) {
+    if (wk == 0) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < EX_WARPS; ++w) v += red[(w * 4 + i) * 32 + lane];
+        for (int w = 0; w < WPT; ++w) v += red[((sub * WPT + w) * 4 + i) * 32 + lane];
         const int row = rt * 16 + g4 + ((i < 2) ? 0 : 8);
         const int col = 2 * c + (i & 1);
         if (col < nn) {
@@ -308,11 +321,11 @@ __device__ __forceinline__ void down_body(const ExpArgs& A, const PrecDev& pc, i
   }
 }
 
-template <int MODEL, int KPW>
+template <int MODEL, int KPW, int RT>
 __global__ void __launch_bounds__(EX_THREADS, 2) k_down_mx(ExpArgs A, const __grid_constant__ ClassTab C,
                                                             int a_cap) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int s_last;
+  __shared__ int s_last[RT];
   const int g = blockIdx.y;
   const int n_groups = *A.grp.n_groups;
   const int slot = A.grp.grp_slot[g];
@@ -324,33 +337,39 @@ __global__ void __launch_bounds__(EX_THREADS, 2) k_down_mx(ExpArgs A, const __gr
   const int cls = slot >= 0 ? min((int)A.slot_class[slot], C.n - 1) : 0;
   const PrecDev& pc = C.c[cls];
   switch (pc.bits) {
-    case 2: down_body<MODEL, KPW, 2>(A, pc, slot, m, start, smem, a_cap); break;
-    case 3: down_body<MODEL, KPW, 3>(A, pc, slot, m, start, smem, a_cap); break;
-    case 8: down_body<MODEL, KPW, 8>(A, pc, slot, m, start, smem, a_cap); break;
-    default: down_body<MODEL, KPW, 4>(A, pc, slot, m, start, smem, a_cap); break;
+    case 2: down_body<MODEL, KPW, RT, 2>(A, pc, slot, m, start, smem, a_cap); break;
+    case 3: down_body<MODEL, KPW, RT, 3>(A, pc, slot, m, start, smem, a_cap); break;
+    case 8: down_body<MODEL, KPW, RT, 8>(A, pc, slot, m, start, smem, a_cap); break;
+    default: down_body<MODEL, KPW, RT, 4>(A, pc, slot, m, start, smem, a_cap); break;
   }
   pdl_trigger();
-  // ---- arrival: the last CTA of the row tile combines all tokens' k parts
+  // ---- arrival: the last CTA of a row tile combines all tokens' k parts
   const int D = A.geo.d_model, k = A.geo.top_k;
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&A.cnt[blockIdx.x], 1u);
-    s_last = (prev == (unsigned)n_groups - 1u);
+  if (threadIdx.x < RT) {
+    const unsigned prev = atomicAdd(&A.cnt[blockIdx.x * RT + threadIdx.x], 1u);
+    s_last[threadIdx.x] = (prev == (unsigned)n_groups - 1u);
   }
   __syncthreads();
-  if (!s_last) return;
+  bool any = false;
+  for (int r = 0; r < RT; ++r) any |= s_last[r] != 0;
+  if (!any) return;
   __threadfence();
-  for (int i = threadIdx.x; i < A.T * 16; i += EX_THREADS) {
-    const int t = i >> 4, row = blockIdx.x * 16 + (i & 15);
-    float acc = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const long long p = (long long)t * k + j;
-      acc += bfr(A.scores[p] * __ldcg(A.ypart + p * D + row));
+  for (int r = 0; r < RT; ++r) {
+    if (!s_last[r]) continue;
+    const int rtile = blockIdx.x * RT + r;
+    for (int i = threadIdx.x; i < A.T * 16; i += EX_THREADS) {
+      const int t = i >> 4, row = rtile * 16 + (i & 15);
+      float acc = 0.f;
+      for (int j = 0; j < k; ++j) {
+        const long long p = (long long)t * k + j;
+        acc += bfr(A.scores[p] * __ldcg(A.ypart + p * D + row));
+      }
+      A.y[(long long)t * D + row] = f2bf(acc);
     }
-    A.y[(long long)t * D + row] = f2bf(acc);
+    if (threadIdx.x == 0) A.cnt[rtile] = 0u;
   }
-  if (threadIdx.x == 0) A.cnt[blockIdx.x] = 0u;
 }
 
 template <typename Kern, typename... Args>
@@ -370,18 +389,19 @@ cudaError_t launch_mx(Kern kern, dim3 grid, int smem, cudaStream_t s, const Args
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-template <int MODEL, int KPW_UP, int KPW_DN>
+template <int MODEL, int KPW_UP, int KPW_DN, int RT>
 cudaError_t launch_mx_pair(const ExpArgs& a, const ClassTab& C, int max_bits, int max_groups,
                            cudaStream_t s) {
   const int K = a.geo.d_model, F = a.geo.d_ff;
-  const int cap_u = MxTile::a_bytes(K, max_bits, 16), cap_d = MxTile::a_bytes(F, max_bits, 16);
+  const int cap_u = MxTile::a_bytes(K, max_bits, 16), cap_d = MxTile::a_bytes(F, max_bits, RT * 16);
   // rounded so that every region after the codes stays 16-byte aligned
   const int cu = (cap_u + 15) & ~15, cd = (cap_d + 15) & ~15;
   const int su = 2 * cu + 4 * MxTile::sb_bytes(K, 16) + 64 + EX_WARPS * 2 * 4 * 32 * 4 + 16;
-  const int sd = cd + 2 * MxTile::sb_bytes(F, 16) + 32 + EX_WARPS * 4 * 32 * 4 + 8 * (F / 64) * 2 * 4 + 16;
+  const int sd = cd + 2 * MxTile::sb_bytes(F, RT * 16) + 32 * RT + EX_WARPS * 4 * 32 * 4 +
+                 8 * (F / 64) * 2 * 4 + 16;
   cudaError_t e = launch_mx(k_up_mx<MODEL, KPW_UP>, dim3(F / 16, max_groups), su, s, a, C, cu);
   if (e != cudaSuccess) return e;
-  return launch_mx(k_down_mx<MODEL, KPW_DN>, dim3(K / 16, max_groups), sd, s, a, C, cd);
+  return launch_mx(k_down_mx<MODEL, KPW_DN, RT>, dim3(K / (16 * RT), max_groups), sd, s, a, C, cd);
 }
 
 }  // namespace
@@ -399,11 +419,12 @@ cudaError_t launch_expert_mx(const ExpArgs& a, const ClassTab& C, int max_groups
   const int G = a.geo.d_model / 64, GF = a.geo.d_ff / 64;
   cudaError_t e;
   if (a.geo.model == 1) {
-    e = launch_mx_pair<1, 6, 6>(a, C, mb, max_groups, s);
-  } else if (G <= 32 && GF <= 16) {
-    e = launch_mx_pair<0, 4, 2>(a, C, mb, max_groups, s);
+    e = launch_mx_pair<1, 6, 6, 1>(a, C, mb, max_groups, s);
+  } else if (G <= 32 && GF <= 12 && (a.geo.d_model / 16) % 2 == 0) {
+    // Qwen3 2048/768: two 16-row tiles of down rows per CTA, 4 warps x 3 groups each
+    e = launch_mx_pair<0, 4, 3, 2>(a, C, mb, max_groups, s);
   } else {
-    e = launch_mx_pair<0, 8, 8>(a, C, mb, max_groups, s);
+    e = launch_mx_pair<0, 8, 8, 1>(a, C, mb, max_groups, s);
   }
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
