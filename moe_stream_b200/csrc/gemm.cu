@@ -486,7 +486,6 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     uint32_t rs[SCALE_AHEAD], rb[SCALE_AHEAD], rmeta[SCALE_AHEAD];
 #pragma unroll
     for (int i = 0; i < SCALE_AHEAD; ++i) fetch(rs[i], rb[i], rmeta[i]);
-    const float2 magic_off = make_float2(-8388608.f, -8388608.f);
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const int n_it = ((total - (int)blockIdx.x + step - 1) / step) * KT;   // K tiles of this CTA
     bool ok = true;
@@ -532,19 +531,34 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           wl[idx] = h2_bits(lo.x, lo.y);
         };
         if (!MIXED || bits == 4) {
+          // One LOP3 turns two nibbles into the f16x2 {1024 + q, 1024 + q'}
+          // (1024 + 16 q at the odd nibbles), and
+          //   s*q + b = s*(1024 + q) + (b - 1024 s) = (s/16)*(1024 + 16 q) + (b - 64 s):
+          // one FFMA2 on the converted pair gives the same correctly rounded
+          // float as fma(q, s, b) (1024 s and s/16 are exact, and so is the
+          // shifted bias for any scale/bias within 2^15 of each other), with
+          // the integer work of the unpacking cut to one LOP3 per pair.
+          const float2 s_ev = s2, b_ev = make_float2(bi - 1024.f * sc, bi - 1024.f * sc);
+          const float so = sc * 0.0625f, bo = bi - 64.f * sc;
+          const float2 s_od = make_float2(so, so), b_od = make_float2(bo, bo);
+          auto put_h = [&](int idx, uint32_t h, float2 sv, float2 bv) {
+            const float2 q = __half22float2(*reinterpret_cast<const __half2*>(&h));
+            const float2 wv = __ffma2_rn(q, sv, bv);
+            const __half2 hi = __floats2half2_rn(wv.x, wv.y);
+            const float2 hf = __half22float2(hi);
+            const float2 lo = __fadd2_rn(wv, make_float2(-hf.x, -hf.y));
+            wh[idx] = *reinterpret_cast<const uint32_t*>(&hi);
+            wl[idx] = h2_bits(lo.x, lo.y);
+          };
           const uint2 pw2 = *reinterpret_cast<const uint2*>(sP(sx) + prow * 32 + part * 8);
           const uint32_t words[2] = {pw2.x, pw2.y};
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
-            const uint32_t u = words[i];
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              // q and q+4 of this word as exact floats (2^23 + q, minus 2^23)
-              const uint32_t m = (u >> (4 * q4)) & 0x000F000Fu;
-              put(i * 4 + q4, __fadd2_rn(make_float2(__uint_as_float((m & 0xFu) | 0x4B000000u),
-                                                     __uint_as_float((m >> 16) | 0x4B000000u)),
-                                         magic_off));
-            }
+            const uint32_t u = words[i], us = u >> 8;
+            put_h(i * 4 + 0, lop_or(u, 0x000F000Fu), s_ev, b_ev);    // q0, q4
+            put_h(i * 4 + 1, lop_or(u, 0x00F000F0u), s_od, b_od);    // q1, q5
+            put_h(i * 4 + 2, lop_or(us, 0x000F000Fu), s_ev, b_ev);   // q2, q6
+            put_h(i * 4 + 3, lop_or(us, 0x00F000F0u), s_od, b_od);   // q3, q7
           }
         } else {
           const uint8_t* row = sP(sx) + prow * gemm_tile_row_bytes(bits);
