@@ -262,10 +262,12 @@ int ms_block_debug(ms_pool* pool, const int32_t** inds, const void** scores,
 
 /* Per-layer CUDA-event timing of ms_moe_block (off by default). When on,
  * every block call records four events on its stream -- before the router,
- * after the router/table step, after the fills, after the expert kernels --
- * also inside a CUDA graph capture (they become event nodes). ms_pool_timing
- * reads the last recorded interval of `layer`, in milliseconds:
- * out[0] router+table, out[1] fills, out[2] expert kernels. */
+ * after the router/table step, after the fills and the wait for the previous
+ * call's prefetch fills, after the expert kernels -- also inside a CUDA
+ * graph capture (they become event nodes). ms_pool_timing reads the last
+ * recorded interval of `layer`, in milliseconds: out[0] router+table,
+ * out[1] fills (this call's demand fills and the prefetch join), out[2]
+ * expert kernels. */
 int ms_pool_profile(ms_pool* pool, int enable);
 int ms_pool_timing(ms_pool* pool, int layer, float* out3);
 

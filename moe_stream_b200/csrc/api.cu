@@ -927,9 +927,11 @@ int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* str
     }
   }
   CK(launch_fill(fa, FILL_CTAS, s));
-  if (ev) CK(cudaEventRecordWithFlags(ev[2], s, rec_flags));
   // the previous call's prefetch fills must land before any expert kernel
   rc = join_side(p, s);
+  // (profiling: the fill interval ends after that join, so the expert
+  // interval times the expert kernels alone)
+  if (ev && !rc) CK(cudaEventRecordWithFlags(ev[2], s, rec_flags));
   if (fork) {
     p->pf_pending = true;
     p->pf_slot = q;
