@@ -59,13 +59,14 @@ def parse():
                     help="skip the expert-parallel measurement of the default run")
     ap.add_argument("--no-mixed", action="store_true",
                     help="skip the per-expert mixed-precision decode measurement")
-    ap.add_argument("--case", choices=["stack", "layer", "prefill", "ep"], default="stack",
+    ap.add_argument("--case", choices=["stack", "layer", "prefill", "ep", "fill"], default="stack",
                     help="layer: a 2-layer Qwen3 stack with every expert resident (a small "
                          "case for ncu section captures); prints per-call timings only. "
                          "prefill: one MoE layer on a large token batch (qwen3 T=4096, "
                          "gptoss T=512 or 16384), the grouped tcgen05 GEMM path. ep: only "
                          "the expert-parallel measurement (gpt-oss layer, T=16384, experts "
-                         "sharded over the ranks under torchrun)")
+                         "sharded over the ranks under torchrun). fill: host->HBM slot fill "
+                         "bandwidth, SM loads (k_fill) against the copy engine")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--batch", type=int, default=1,
                     help="stack case: tokens per decode step (a multi-token verify batch); "
@@ -107,6 +108,48 @@ def layer_case(args):
     print(json.dumps({"case": "layer", "tokens": T, "calls": args.steps,
                       "us_per_call": e0.elapsed_time(e1) * 1e3 / args.steps}))
     pool.close()
+
+
+def fill_case(args):
+    """Host -> HBM slot fills, the two ways the library has them: k_fill
+    (32 CTAs reading the mapped pinned store with SM loads, the path block
+    calls use, driven by the device slot table) and cudaMemcpyAsync on the
+    copy engine (ms_pool_read, one call per blob, issued by the host). Same
+    64 Qwen3 blobs (170 MB) into empty slots each way, CUDA events around
+    each batch; prints GB/s for both."""
+    import torch
+    from moe_stream_b200 import geometry, store as S
+    from moe_stream_b200.pool import ExpertPool
+    torch.cuda.set_device(0)
+    geom = geometry.qwen3(1)
+    n = 64
+    out = {"case": "fill", "blobs": n, "blob_bytes": geom.blob_bytes}
+    import numpy as np
+    # a host array the caller owns, registered (page-locked, mapped) by each pool
+    host = np.empty(geom.n_keys * geom.blob_bytes, np.uint8)
+    torch.from_numpy(host).view(geom.n_keys, geom.blob_bytes).copy_(S.make_layer_blobs(geom, SEED, 0).cpu())
+    res = {"k_fill": [], "copy_engine": []}
+    for rep in range(args.warmup + args.steps):
+        for how in ("k_fill", "copy_engine"):
+            pool = ExpertPool(geom, geom.n_experts, depths=(), max_tokens=1)
+            pool.attach_store(host)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            if how == "k_fill":
+                pool.prefetch(0, list(range(n)))      # one table step + one k_fill of n blobs
+            else:
+                for e in range(n):
+                    pool._read(e, 0, e)
+            e1.record()
+            torch.cuda.synchronize()
+            pool.status()
+            if rep >= args.warmup:
+                res[how].append(n * geom.blob_bytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+            pool.close()
+    for how, v in res.items():
+        out[how + "_gbs"] = float(statistics.median(v))
+    print(json.dumps(out))
 
 
 def prefill_case(args):
@@ -897,6 +940,9 @@ def main():
         if int(os.environ.get("RANK", "0")) != 0:
             return
         reference_arm(args)
+        return
+    if args.case == "fill":
+        fill_case(args)
         return
     if args.case == "layer":
         layer_case(args)
