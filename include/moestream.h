@@ -194,6 +194,18 @@ int ms_route(ms_pool* pool, int layer, const void* x, int T, int32_t* inds,
 int ms_moe_block(ms_pool* pool, int layer, const void* x, int T, void* y,
                  void* stream);
 
+/* The block fused with its layer's non-expert pieces on either side: the
+ * post-attention RMSNorm in front (mlx_lm's Qwen3 / gpt-oss decoder layer:
+ * x = rms_norm(h) * norm_w, mx.fast.rms_norm's rounding) and the residual
+ * add behind it: out = h + block(x), every value bf16. h is the residual
+ * stream (bf16 [T, d_model]), norm_w bf16 [d_model], eps > 0; out may be h.
+ * Decode calls of up to 8 tokens normalise inside the route step and add
+ * the residual inside the expert kernels' combine (no extra kernel); larger
+ * calls normalise with one kernel first. Same asynchronous, capture-safe
+ * contract as ms_moe_block. */
+int ms_moe_block_fused(ms_pool* pool, int layer, const void* h, const void* norm_w, float eps, int T,
+                       void* out, void* stream);
+
 /* Sticky device-side status of asynchronous block calls (MS_OK or the first
  * MS_E_* seen since the last call); clears it. Synchronises `stream`. */
 int ms_pool_status(ms_pool* pool, void* stream);

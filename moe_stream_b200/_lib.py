@@ -92,6 +92,8 @@ EXPORTS = {
     "ms_pool_load_state": [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p],
     "ms_pool_selftest_wait": [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p],
     "ms_pool_set_precision": [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p],
+    "ms_moe_block_fused": [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                           ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p],
     "ms_kernel_arch": [ctypes.c_int, ctypes.POINTER(ctypes.c_int)],
     "ms_block_debug": [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p),
                        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)],

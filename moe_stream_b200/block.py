@@ -40,7 +40,8 @@ class MoEBlock:
     pool in the module global _POOL and the blocks in _BLOCKS,
     engine_v3.py:489-495)."""
 
-    def __init__(self, pool: ExpertPool, layer, gate_weight, gate_bias=None):
+    def __init__(self, pool: ExpertPool, layer, gate_weight, gate_bias=None, norm_weight=None,
+                 norm_eps=1e-6):
         self.pool = pool
         self._layer = int(layer)
         self.top_k = pool.top_k
@@ -51,9 +52,28 @@ class MoEBlock:
                           gate_bias.to(device=f"cuda:{pool.device}", dtype=torch.bfloat16).contiguous())
         _lib.check(pool._lib.ms_set_router(pool._h, self._layer, _ptr(self.gate_weight),
                                            _ptr(self.gate_bias) if self.gate_bias is not None else None))
+        # the layer's post-attention RMSNorm weight, for fused()
+        self.norm_weight = (None if norm_weight is None else
+                            norm_weight.to(device=f"cuda:{pool.device}", dtype=torch.bfloat16).contiguous())
+        self.norm_eps = float(norm_eps)
 
     def __call__(self, x, out=None, stream=None):
         return streaming_call(self, x, out=out, stream=stream)
+
+    def fused(self, h, out=None, stream=None):
+        """h + block(rms_norm(h) * norm_weight): the block with the decoder
+        layer's post-attention norm and residual add (mlx_lm's layer,
+        ``h + mlp(post_attention_layernorm(h))``) in the same library call.
+        out may be h (in place)."""
+        if self.norm_weight is None:
+            raise ValueError("the block has no norm_weight")
+        pool = self.pool
+        h2 = _check_tokens(pool, h)
+        T = h2.shape[0]
+        y = out if out is not None else torch.empty_like(h2)
+        _lib.check(pool._lib.ms_moe_block_fused(pool._h, self._layer, _ptr(h2), _ptr(self.norm_weight),
+                                                self.norm_eps, T, _ptr(y), _stream_ptr(stream)))
+        return y.reshape(h.shape)
 
 
 def streaming_call(self, x, out=None, stream=None):

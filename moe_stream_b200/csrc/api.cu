@@ -195,6 +195,11 @@ struct ms_pool {
   uint8_t* class_of_key = nullptr;            // [n_keys]
   uint8_t* slot_class = nullptr;              // [n_slots]
   std::vector<uint8_t> h_class_of_key;
+  // the fused block (ms_moe_block_fused): set for the duration of one call
+  const uint16_t* cur_norm_w = nullptr;       // route step normalises its input
+  float cur_norm_eps = 0.f;
+  const uint16_t* cur_resid = nullptr;        // combines add it to the output
+  uint16_t* xnorm = nullptr;                  // [max_tokens, d_model]: normalised input (wide path)
 };
 
 namespace {
@@ -405,6 +410,7 @@ int ms_pool_create(const ms_geom* geom, const ms_pool_config* cfg, int device, m
   if ((rc = palloc(p, &t.pend_list, t.n_slots))) return bail(rc);
   if ((rc = palloc(p, &t.fills, t.max_fills))) return bail(rc);
   if ((rc = palloc(p, &t.ctr, 1))) return bail(rc);
+  if ((rc = palloc(p, &p->xnorm, (size_t)cfg->max_tokens * geom->d_model))) return bail(rc);
   if ((rc = palloc(p, &p->class_of_key, t.n_keys))) return bail(rc);
   if ((rc = palloc(p, &p->slot_class, t.n_slots))) return bail(rc);
   CKB(cudaMemset(p->class_of_key, 0, t.n_keys));
@@ -755,6 +761,10 @@ static int route_common(ms_pool* p, int layer, const void* x, int T, cudaStream_
   a.do_groups = block ? 1 : 0;
   a.grp = p->grp;
   a.pair_slot = block ? p->pair_slot : nullptr;
+  if (block && !wide && p->cur_norm_w) {
+    a.norm_w = p->cur_norm_w;
+    a.norm_eps = p->cur_norm_eps;
+  }
   if (ring >= 0) {
     a.pf_ring = p->pf_ring + (size_t)ring * p->tab.max_fills;
     a.pf_cnt = p->pf_cnt + ring;
@@ -803,6 +813,7 @@ static ExpArgs exp_args(ms_pool* p, const void* x, int T, void* y, const float* 
   e.y = static_cast<uint16_t*>(y);
   e.status = &p->tab.ctr->status;
   e.slot_class = p->slot_class;
+  e.resid = p->cur_resid;
   return e;
 }
 
@@ -867,6 +878,7 @@ static int wide_experts(ms_pool* p, const void* x, int T, int k, const int* keys
   c.T = T;
   c.k = k;
   c.d = p->geom.d_model;
+  c.resid = p->cur_resid;
   const long long chunks = (long long)T * (c.d / 8);
   CK(launch_combine(c, (int)std::min<long long>((chunks + 255) / 256, p->sm_count * 8), s));
   return MS_OK;
@@ -948,6 +960,38 @@ int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* str
   }
   if (ev) CK(cudaEventRecordWithFlags(ev[3], s, rec_flags));
   return MS_OK;
+}
+
+// Token rows up to which the route step normalises its own input; larger
+// decode batches and the wide path normalise with one kernel first.
+constexpr int FUSED_NORM_MAX_T = 8;
+
+int ms_moe_block_fused(ms_pool* p, int layer, const void* h, const void* norm_w, float eps, int T,
+                       void* out, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (!h || !aligned16(h) || !norm_w || !aligned16(norm_w))
+    return fail(MS_E_INVALID, "h and norm_w must be 16-byte aligned device pointers");
+  if (!(eps > 0.f)) return fail(MS_E_INVALID, "eps must be positive");
+  if (T <= 0 || T > p->cfg.max_tokens)
+    return fail(MS_E_INVALID, "T=%d outside [1, max_tokens=%d]", T, p->cfg.max_tokens);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int k = p->geom.top_k;
+  const bool wide = p->wide && (T * k >= p->wide_min_pairs || T > p->narrow_tokens);
+  const void* x = h;
+  CK(cudaSetDevice(p->device));
+  if (!wide && T <= FUSED_NORM_MAX_T) {
+    p->cur_norm_w = static_cast<const uint16_t*>(norm_w);
+    p->cur_norm_eps = eps;
+  } else {
+    CK(launch_rmsnorm(static_cast<const uint16_t*>(h), static_cast<const uint16_t*>(norm_w), eps, T,
+                      p->geom.d_model, p->xnorm, s));
+    x = p->xnorm;
+  }
+  p->cur_resid = static_cast<const uint16_t*>(h);
+  const int rc = ms_moe_block(p, layer, x, T, out, stream);
+  p->cur_norm_w = nullptr;
+  p->cur_resid = nullptr;
+  return rc;
 }
 
 int ms_pool_status(ms_pool* p, void* stream) {

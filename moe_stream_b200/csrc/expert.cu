@@ -303,7 +303,9 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A, const __grid_con
         // (y * scores) is a bf16 product before the sum (engine_v3.py:600)
         acc += bfr(A.scores[p] * __ldcg(A.ypart + p * D + row));
       }
-      A.y[(long long)t * D + row] = f2bf(acc);
+      // the block's bf16 output; the fused block adds it to the residual
+      A.y[(long long)t * D + row] =
+          A.resid ? f2bf(bf2f(A.resid[(long long)t * D + row]) + bfr(acc)) : f2bf(acc);
     }
     if (threadIdx.x == 0) A.cnt[rtile] = 0u;
   }

@@ -366,7 +366,9 @@ __global__ void __launch_bounds__(EX_THREADS, 2) k_down_mx(ExpArgs A, const __gr
         const long long p = (long long)t * k + j;
         acc += bfr(A.scores[p] * __ldcg(A.ypart + p * D + row));
       }
-      A.y[(long long)t * D + row] = f2bf(acc);
+      // the block's bf16 output; the fused block adds it to the residual
+      A.y[(long long)t * D + row] =
+          A.resid ? f2bf(bf2f(A.resid[(long long)t * D + row]) + bfr(acc)) : f2bf(acc);
     }
     if (threadIdx.x == 0) A.cnt[rtile] = 0u;
   }

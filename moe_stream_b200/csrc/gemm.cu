@@ -704,6 +704,16 @@ __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
         acc[2 * q + 1] += __uint_as_float(w[q] & 0xffff0000u);
       }
     }
+    if (a.resid) {
+      // the fused block: residual + the block's bf16 output
+      const uint4 hv = *reinterpret_cast<const uint4*>(a.resid + (long long)t * a.d + c * 8);
+      const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] = __uint_as_float(hw[q] << 16) + bfr(acc[2 * q]);
+        acc[2 * q + 1] = __uint_as_float(hw[q] & 0xffff0000u) + bfr(acc[2 * q + 1]);
+      }
+    }
     uint4 o;
     o.x = (uint32_t)f2bf(acc[0]) | ((uint32_t)f2bf(acc[1]) << 16);
     o.y = (uint32_t)f2bf(acc[2]) | ((uint32_t)f2bf(acc[3]) << 16);

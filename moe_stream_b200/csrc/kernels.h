@@ -52,6 +52,10 @@ struct RouteArgs {
   int* pair_slot;             // [T, k] or null
   int2* pf_ring;              // this call's half of the prefetch-fill ring, or null
   int* pf_cnt;                // its fill count
+  // fused post-attention norm: x is the residual stream h and the block
+  // routes rms_norm(h) * norm_w (null: x is the block input as it is)
+  const uint16_t* norm_w;     // bf16 [d_model]
+  float norm_eps;
 };
 
 struct PoolReq {
@@ -108,6 +112,7 @@ struct ExpArgs {
   uint16_t* y;                // bf16 [T, d_model]
   int* status;                // sticky pool status (bounded waits report here)
   const uint8_t* slot_class;  // [n_slots] precision class of each slot's blob (mixed pools)
+  const uint16_t* resid;      // bf16 [T, d_model] added to the output (fused residual), or null
 };
 
 // ------------------------------------------------ wide batches (prefill)
@@ -170,7 +175,12 @@ struct CombineArgs {
   const int* inv;             // [T, k]
   uint16_t* y;                // bf16 [T, d]
   int T, k, d;
+  const uint16_t* resid;      // bf16 [T, d] added to the output (fused residual), or null
 };
+
+// rms_norm(h) * w, bf16 [T, d] (the fused block's input on the wide path).
+cudaError_t launch_rmsnorm(const uint16_t* h, const uint16_t* w, float eps, int T, int d, uint16_t* out,
+                           cudaStream_t s);
 
 // ms_expert_mlp on a wide batch: pairs grouped by the slot they read.
 struct MlpWideArgs {

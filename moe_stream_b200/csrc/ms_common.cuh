@@ -84,6 +84,28 @@ struct Geo {
 __device__ __forceinline__ float bf2f(uint16_t b) {
   return __uint_as_float(((uint32_t)b) << 16);
 }
+
+// 1/sqrt(mean(h^2) + eps) of a bf16 row of d values, by the whole CTA
+// (blockDim.x a multiple of 32); red: >= 32 floats of shared scratch. As
+// mlx's RMSNorm (mx.fast.rms_norm): fp32 sum of squares, correctly rounded
+// sqrt and division.
+__device__ __forceinline__ float cta_rms_factor(const uint16_t* h, int d, float eps, float* red) {
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float v = __uint_as_float(((uint32_t)h[i]) << 16);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < nw; ++w) tot += red[w];
+  __syncthreads();
+  return 1.f / sqrtf(tot / (float)d + eps);
+}
 // round-to-nearest-even float -> bf16 bits (the hardware conversion)
 __device__ __forceinline__ uint16_t f2bf(float f) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(f));

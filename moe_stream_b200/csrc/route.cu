@@ -174,6 +174,23 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
   // previous layer's k_down triggers once its dot products are done): wait
   // for that grid before touching anything
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // fused post-attention norm (A.norm_w): the block input is
+  // rms_norm(h) * w of the residual stream h = A.x, computed by every CTA
+  // into shared memory, as mlx's fast rms_norm rounds it: bf16(bf16(h * r) * w)
+  // with r = 1/sqrt(mean(h^2) + eps)
+  extern __shared__ __align__(16) uint16_t s_xn[];   // [T][d] when A.norm_w
+  const uint16_t* xin = A.x;
+  if (A.norm_w) {
+    __shared__ float s_red[32];
+    for (int t = 0; t < T; ++t) {
+      const uint16_t* h = A.x + (long long)t * d;
+      const float rn = cta_rms_factor(h, d, A.norm_eps, s_red);
+      for (int i = threadIdx.x; i < d; i += RT_THREADS)
+        s_xn[t * d + i] = f2bf(bfr(bf2f(h[i]) * rn) * bf2f(A.norm_w[i]));
+    }
+    __syncthreads();
+    xin = s_xn;
+  }
   // ---------------------------------------------------------------- phase 1
   for (int r = gw; r < rows; r += nwarps_total) {
     const int which = r / E, e = r % E;
@@ -181,12 +198,13 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
     const uint16_t* b = (which == 0 ? A.b_r : A.b_p[which - 1]);
     const float bias = b ? bf2f(b[e]) : 0.f;
     for (int t = 0; t < T; ++t) {
-      const uint16_t* x = A.x + (long long)t * d;
+      const uint16_t* x = xin + (long long)t * d;
       float acc = 0.f;
 #pragma unroll 8
       for (int ch = lane; ch < nchunk; ch += 32) {
         const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w) + ch);
-        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x) + ch);
+        const uint4 xv = A.norm_w ? reinterpret_cast<const uint4*>(x)[ch]
+                                  : __ldg(reinterpret_cast<const uint4*>(x) + ch);
         const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w};
         const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
@@ -200,7 +218,7 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
     }
   }
   if (A.xfrag)
-    frag_write_rows(A.x, T, d, A.xfrag, A.xsum, blockIdx.x * RT_THREADS + threadIdx.x,
+    frag_write_rows(xin, T, d, A.xfrag, A.xsum, blockIdx.x * RT_THREADS + threadIdx.x,
                     gridDim.x * RT_THREADS, &A.tab.ctr->status);
 
   // ----------------------------------------------------- arrival: last CTA
@@ -753,9 +771,17 @@ cudaError_t route_step_attributes(cudaFuncAttributes* attr) {
 }
 
 cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s) {
+  // the fused norm's input rows in dynamic shared memory, beside the
+  // kernel's static arrays
+  const int smem = a.norm_w ? a.T * a.geo.d_model * 2 : 0;
+  if (smem > 0) {
+    cudaError_t e = cudaFuncSetAttribute(k_route_step, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(RT_THREADS);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -763,6 +789,23 @@ cudaError_t launch_route_step(const RouteArgs& a, int grid, cudaStream_t s) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, k_route_step, a);
+}
+
+// rms_norm(h) * w for the fused block's wide path: one CTA per token row.
+__global__ void __launch_bounds__(256) k_rmsnorm(const uint16_t* h, const uint16_t* w, float eps, int d,
+                                                 uint16_t* out) {
+  __shared__ float s_red[32];
+  const uint16_t* hr = h + (long long)blockIdx.x * d;
+  const float rn = cta_rms_factor(hr, d, eps, s_red);
+  uint16_t* o = out + (long long)blockIdx.x * d;
+  for (int i = threadIdx.x; i < d; i += 256) o[i] = f2bf(bfr(bf2f(hr[i]) * rn) * bf2f(w[i]));
+}
+
+cudaError_t launch_rmsnorm(const uint16_t* h, const uint16_t* w, float eps, int T, int d, uint16_t* out,
+                           cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  k_rmsnorm<<<T, 256, 0, s>>>(h, w, eps, d, out);
+  return cudaGetLastError();
 }
 cudaError_t launch_route_wide(const RouteArgs& a, const WideArgs& w, cudaStream_t s) {
   const int rows = a.geo.n_experts * (1 + a.n_pred);

@@ -217,6 +217,16 @@ def expert_block(x, inds, scores, blobs, comps, model, group_size=64, prec=None)
     return bf16.r(parts.sum(axis=1, dtype=np.float32))
 
 
+def rms_norm(h, w, eps):
+    """mlx_lm's post-attention RMSNorm (mx.fast.rms_norm, MLX 0.32, a
+    third-party dependency outside the reference): r = 1/sqrt(mean(h^2) +
+    eps) in fp32, out = bf16(bf16(h * r) * w). h, w: bf16 values."""
+    h = np.asarray(h, np.float32)
+    ms_ = (h.astype(np.float64) ** 2).mean(axis=-1, keepdims=True).astype(np.float32)
+    r = (np.float32(1.0) / np.sqrt(ms_ + np.float32(eps))).astype(np.float32)
+    return bf16.r(bf16.r(h * r) * np.asarray(w, np.float32))
+
+
 def fp32_reference(x, inds, scores, blobs, comps, model, group_size=64, prec=None):
     """test_kernel.py:52-65: dequantise (bf16 weights, as mx.dequantize
     returns them), then the whole MLP in fp32 (float64 here). gpt-oss adds

@@ -80,7 +80,8 @@ def test_every_entry_point_rejects_a_null_handle(lib):
     for name, argtypes in _lib.EXPORTS.items():
         if name in skip:
             continue
-        args = [0 if a in ints else None for a in argtypes]
+        args = [0 if a in ints else (0.0 if a in (ctypes.c_float, ctypes.c_double) else None)
+                for a in argtypes]
         rc = getattr(lib, name)(*args)
         assert rc == _lib.MS_E_INVALID, (name, rc)
         assert "NULL" in _lib.last_error(), (name, _lib.last_error())
