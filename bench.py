@@ -59,6 +59,8 @@ def parse():
                     help="skip the expert-parallel measurement of the default run")
     ap.add_argument("--no-mixed", action="store_true",
                     help="skip the per-expert mixed-precision decode measurement")
+    ap.add_argument("--no-fused", action="store_true",
+                    help="skip the fused norm + block + residual decode measurement")
     ap.add_argument("--case", choices=["stack", "layer", "prefill", "ep", "fill"], default="stack",
                     help="layer: a 2-layer Qwen3 stack with every expert resident (a small "
                          "case for ncu section captures); prints per-call timings only. "
@@ -608,6 +610,78 @@ def profile_traffic():
 
 
 # -------------------------------------------------------------- GPU arm
+def fused_measure(pool, blocks, routers, X, t0, K, dev):
+    """Decode tokens through the fused block (ms_moe_block_fused: the
+    layer's post-attention RMSNorm in the route step, the residual add in
+    the combine) against the same block with the norm and the add as torch
+    ops around it, both captured as CUDA graphs and replayed on the same
+    tokens from the same pool checkpoint; CUDA events."""
+    import torch
+    from moe_stream_b200.block import MoEBlock
+    L, d = len(blocks), X.shape[-1]
+    eps = 1e-6
+    g = torch.Generator().manual_seed(SEED + 5)
+    norm_w = [(1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16).to(dev) for _ in range(L)]
+    fb = [MoEBlock(pool, l, w, b, norm_weight=norm_w[l], norm_eps=eps) for l, (w, b) in enumerate(routers)]
+    h = torch.zeros(L, 1, d, dtype=torch.bfloat16, device=dev)
+    out = torch.zeros_like(h)
+
+    def fused_step():
+        for l in range(L):
+            fb[l].fused(h[l], out=out[l])
+
+    def unfused_step():
+        for l in range(L):
+            hf = h[l].float()
+            xn = ((hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + eps)).to(torch.bfloat16)
+                  * norm_w[l]).to(torch.bfloat16)
+            y = blocks[l](xn)
+            out[l].copy_(h[l] + y)
+
+    def capture(fn):
+        fn()                                  # eager once (fills, allocations)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=dev)
+        pool.join(torch.cuda.current_stream(dev))
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.graph(graph, stream=s):
+            fn()
+            pool.join(s)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        return graph
+
+    res = {}
+    snap = pool.save_state(with_arena=True)
+    for name, fn in (("fused", fused_step), ("unfused_torch_norm_add", unfused_step)):
+        graph = capture(fn)
+        pool.load_state(snap, with_arena=True)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for t in range(t0, t0 + K):
+            h.copy_(X[t], non_blocking=True)
+            pool.join(torch.cuda.current_stream(dev))
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        pool.status()
+        res[name] = K / (e0.elapsed_time(e1) / 1e3)
+        del graph
+    pool.load_state(snap, with_arena=True)
+    del snap
+    torch.cuda.synchronize()
+    # the pool's routers back to the main blocks' tensors (fb's go away)
+    import ctypes
+    from moe_stream_b200 import _lib
+    for b in blocks:
+        _lib.check(pool._lib.ms_set_router(
+            pool._h, b._layer, ctypes.c_void_p(b.gate_weight.data_ptr()),
+            ctypes.c_void_p(b.gate_bias.data_ptr()) if b.gate_bias is not None else None))
+    return {"tok_s": res["fused"], "tok_s_norm_and_add_as_torch_ops": res["unfused_torch_norm_add"],
+            "tokens": K, "what": "out = h + block(rms_norm(h) * w) per layer, 48 layers, CUDA graphs"}
+
+
 MIXED_CLASSES = ((4, "bf16"), (4, "fp8"), (3, "fp8"), (2, "fp8"))
 MIXED_FRACS = (0.30, 0.30, 0.25, 0.15)
 
@@ -875,6 +949,13 @@ def gpu_arm(args):
     del gp
     pool.status()
 
+    # ------------------- the block fused with its layer's norm and residual
+    # (same pool state and tokens for both; each layer's hidden state is the
+    # residual stream h, out = h + block(rms_norm(h) * w))
+    fused = None
+    if TB == 1 and not args.no_fused:
+        fused = fused_measure(pool, blocks, routers, X, t0, min(K, 64), dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and TB == 1:
         blob_of = lambda key: store[int(key) * geom.blob_bytes:(int(key) + 1) * geom.blob_bytes]
@@ -925,6 +1006,8 @@ def gpu_arm(args):
             "clocks": clk,
             "setup_s": {"store_generation": t_gen},
         }
+        if fused is not None:
+            line["fused_norm_residual"] = fused
         if mixed is not None:
             line["mixed_precision"] = mixed
         if ep is not None:
