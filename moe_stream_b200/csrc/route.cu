@@ -259,6 +259,12 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
 
   const int kp = A.kp;
   const bool small = T * k <= SMALL_P;
+  // one token: its k experts and each speculation's kp experts are distinct,
+  // so the routing warps sort them into the acquire / prefetch lists
+  // directly (a lane's rank = how many of the selection are smaller), and a
+  // lane's rank is its expert's group -- no masks, no list building
+  const bool one = T == 1 && k <= 32 && kp <= 32;
+  __shared__ int s_rank1[32];
   // one task per (token, router): task part 0 routes the token, part d >= 1
   // is the speculation of prefetch depth d-1 -- top-(k*widen) of the target
   // layer's raw logits (engine_v3.py:476-483, 509-514). Tasks go to warps
@@ -271,20 +277,38 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
     int* sel = s_sel[warp];
     if (part == 0) {
       const float sc = route_token(lg, A.geo, vals, sel, lane);
+      const int e = lane < k ? sel[lane] : 0x7fffffff;
       if (lane < k) {
-        const int e = sel[lane];
         A.inds[t * k + lane] = e;
         A.scores[t * k + lane] = f2bf(sc);
         A.scores_f[t * k + lane] = sc;
         if (small) s_inds[t * k + lane] = e;
-        atomicOr(&s_acq_mask[e >> 5], 1u << (e & 31));
+        if (!one) atomicOr(&s_acq_mask[e >> 5], 1u << (e & 31));
+      }
+      if (one) {
+        int rank = 0;
+        for (int j = 0; j < k; ++j) rank += __shfl_sync(MS_FULL, e, j) < e;
+        if (lane < k) {
+          s_acq[rank] = e;
+          s_rank1[lane] = rank;
+        }
       }
     } else {
       const int dd = part - 1;
       predict_token(lg + part * E, E, kp, vals, sel, lane);
-      for (int j = lane; j < kp; j += 32) {
-        atomicOr(&s_pred_mask[dd][sel[j] >> 5], 1u << (sel[j] & 31));
-        if (dd == 0 && A.pred_out) A.pred_out[t * kp + j] = sel[j];
+      if (one) {
+        const int e = lane < kp ? sel[lane] : 0x7fffffff;
+        int rank = 0;
+        for (int j = 0; j < kp; ++j) rank += __shfl_sync(MS_FULL, e, j) < e;
+        if (lane < kp) {
+          s_pred[dd][rank] = e;
+          if (dd == 0 && A.pred_out) A.pred_out[lane] = e;
+        }
+      } else {
+        for (int j = lane; j < kp; j += 32) {
+          atomicOr(&s_pred_mask[dd][sel[j] >> 5], 1u << (sel[j] & 31));
+          if (dd == 0 && A.pred_out) A.pred_out[t * kp + j] = sel[j];
+        }
       }
     }
     __syncwarp();
@@ -292,11 +316,20 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
   __syncthreads();
 
   if (warp == 0) {
-    const int n_acq = warp_small_mask_to_list(s_acq_mask, (E + 31) / 32, s_acq, lane);
-    if (lane == 0) s_n_acq = n_acq;
-    for (int dd = 0; dd < A.n_pred; ++dd) {
-      const int n = warp_small_mask_to_list(s_pred_mask[dd], (E + 31) / 32, s_pred[dd], lane);
-      if (lane == 0) s_n_pred[dd] = n;
+    int n_acq;
+    if (one) {
+      n_acq = k;
+      if (lane == 0) {
+        s_n_acq = k;
+        for (int dd = 0; dd < A.n_pred; ++dd) s_n_pred[dd] = kp;
+      }
+    } else {
+      n_acq = warp_small_mask_to_list(s_acq_mask, (E + 31) / 32, s_acq, lane);
+      if (lane == 0) s_n_acq = n_acq;
+      for (int dd = 0; dd < A.n_pred; ++dd) {
+        const int n = warp_small_mask_to_list(s_pred_mask[dd], (E + 31) / 32, s_pred[dd], lane);
+        if (lane == 0) s_n_pred[dd] = n;
+      }
     }
     __syncwarp();
     if (A.do_pool) {
@@ -305,14 +338,12 @@ __global__ void __launch_bounds__(RT_THREADS) k_route_step(RouteArgs A) {
       for (int i = lane; i < n_acq; i += 32) s_slots[i] = -1;
     }
     __syncwarp();
-    if (A.do_groups && T == 1) {
+    if (A.do_groups && one) {
       // one token: its k experts are distinct, so group g is the g-th
-      // smallest of them with that one pair; g is the expert's rank in the
-      // acquired mask
+      // smallest of them with that one pair; g is the expert's rank
       if (lane < k) {
         const int e = s_inds[lane];
-        int g = __popc(s_acq_mask[e >> 5] & ((1u << (e & 31)) - 1u));
-        for (int w = 0; w < (e >> 5); ++w) g += __popc(s_acq_mask[w]);
+        const int g = s_rank1[lane];
         A.grp.grp_start[g] = g;
         A.grp.grp_count[g] = 1;
         A.grp.grp_key[g] = e;
