@@ -61,14 +61,15 @@ def parse():
                     help="skip the per-expert mixed-precision decode measurement")
     ap.add_argument("--no-fused", action="store_true",
                     help="skip the fused norm + block + residual decode measurement")
-    ap.add_argument("--case", choices=["stack", "layer", "prefill", "ep", "fill"], default="stack",
+    ap.add_argument("--case", choices=["stack", "layer", "prefill", "ep", "fill", "stack3"], default="stack",
                     help="layer: a 2-layer Qwen3 stack with every expert resident (a small "
                          "case for ncu section captures); prints per-call timings only. "
                          "prefill: one MoE layer on a large token batch (qwen3 T=4096, "
                          "gptoss T=512 or 16384), the grouped tcgen05 GEMM path. ep: only "
                          "the expert-parallel measurement (gpt-oss layer, T=16384, experts "
                          "sharded over the ranks under torchrun). fill: host->HBM slot fill "
-                         "bandwidth, SM loads (k_fill) against the copy engine")
+                         "bandwidth, SM loads (k_fill) against the copy engine. stack3: config 3's "
+                         "36-layer gpt-oss decode stack")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--batch", type=int, default=1,
                     help="stack case: tokens per decode step (a multi-token verify batch); "
@@ -109,6 +110,99 @@ def layer_case(args):
     pool.status()
     print(json.dumps({"case": "layer", "tokens": T, "calls": args.steps,
                       "us_per_call": e0.elapsed_time(e1) * 1e3 / args.steps}))
+    pool.close()
+
+
+def gptoss_stack_case(args):
+    """Config 3's decode stack: 36 gpt-oss-shape layers (d = ff = 2880, top-4
+    of 128, projection biases, clamped SwiGLU), 2304 of 4608 experts
+    resident, LFU, next-layer prefetch, batch 1; Zipf(1.1) router biases and
+    the config-1 hidden-state process (the config fixes neither). Same
+    method as the default line: steady-state pre-roll, CUDA-graph token
+    replay timed with CUDA events, per-layer intervals by events for the
+    expert kernels' roofline. 32 GB arena, 65 GB pinned store."""
+    import ctypes
+    import torch
+    from moe_stream_b200 import _lib, geometry, store as S
+    from moe_stream_b200.block import DecodeGraph, MoEBlock
+    from moe_stream_b200.pool import ExpertPool
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    L, n_slots = 36, 2304
+    geom = geometry.gptoss(L)
+    pool = ExpertPool(geom, n_slots, evict="lfu", depths=(1,), pf_widen=1, max_tokens=1)
+    st = torch.from_numpy(pool.alloc_store()).view(geom.n_keys, geom.blob_bytes)
+    t_gen = time.perf_counter()
+    for layer in range(L):
+        st[layer * 128:(layer + 1) * 128].copy_(S.make_layer_blobs(geom, SEED, layer, device=dev))
+    torch.cuda.synchronize()
+    t_gen = time.perf_counter() - t_gen
+    routers = [S.router_weights(geom, SEED, l, zipf_s=1.1) for l in range(L)]
+    blocks = [MoEBlock(pool, l, w, b) for l, (w, b) in enumerate(routers)]
+    K, W, PR = args.steps, args.warmup, args.preroll_max
+    X = S.decode_inputs(PR + W + K + 16, L, geom.d_model, SEED + 1).to(dev)
+    for l, b in enumerate(blocks):
+        b(X[0, l:l + 1])
+    torch.cuda.synchronize()
+    g = DecodeGraph(blocks)
+    used, hist, roll = 1, [pool.stats()], 0.0
+    while used < PR:
+        for t in range(used, min(PR, used + 16)):
+            g.step(X[t].unsqueeze(1))
+        used = min(PR, used + 16)
+        hist.append(pool.stats())
+        back = hist[max(0, len(hist) - 3)]
+        roll = (hist[-1]["cache"] - back["cache"]) / max(1, hist[-1]["total"] - back["total"])
+        if used >= 64 and roll >= args.hit_target:
+            break
+    for t in range(used, used + W):
+        g.step(X[t].unsqueeze(1))
+    t0 = used + W
+    torch.cuda.synchronize()
+    s0 = pool.stats()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for t in range(t0, t0 + K):
+        g.step(X[t].unsqueeze(1))
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    pool.status()
+    s1 = pool.stats()
+    d = {k: s1[k] - s0[k] for k in ("total", "prefetch", "cache", "miss")}
+    _lib.check(pool._lib.ms_pool_profile(pool._h, 1))
+    gp = DecodeGraph(blocks)
+    acc = [0.0, 0.0, 0.0]
+    buf = (ctypes.c_float * 3)()
+    for t in range(t0 + K, t0 + K + 16):
+        gp.step(X[t].unsqueeze(1))
+        torch.cuda.synchronize()
+        for layer in range(L):
+            _lib.check(pool._lib.ms_pool_timing(pool._h, layer, buf))
+            for i in range(3):
+                acc[i] += buf[i] / (16 * L)
+    _lib.check(pool._lib.ms_pool_profile(pool._h, 0))
+    peaks, peak_kind = measured_peaks()
+    bytes_per_layer = geom.top_k * geom.payload_bytes
+    achieved = bytes_per_layer / (acc[2] * 1e-3) / 1e9
+    print(json.dumps({
+        "case": "stack3", "metric": "MoE-block decode tok/s (gpt-oss-120b shape, 36 layers, batch 1)",
+        "value": K / (ms / 1e3), "unit": "tok/s", "steps": K, "warmup": W, "ms_per_step": ms / K,
+        "config": {"workload": "config3: gpt-oss 36-layer expert stack, batch-1 decode, 2304 of 4608 "
+                               "experts resident, LFU, next-layer prefetch, Zipf(1.1) router bias",
+                   "n_layers": L, "n_slots": n_slots},
+        "hit_rate": {"cache": d["cache"] / max(1, d["total"]),
+                     "resident_at_acquire": (d["cache"] + d["prefetch"]) / max(1, d["total"]),
+                     "h2d_fill_bytes_per_token": (s1["gb"] - s0["gb"]) * 2 ** 30 / K,
+                     "preroll_tokens": used, "preroll_window_cache_hit": roll},
+        "expert_bytes_per_token": bytes_per_layer * L,
+        "per_layer_us": {"router_table": acc[0] * 1e3, "fill": acc[1] * 1e3, "experts": acc[2] * 1e3},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind,
+                     "kernel": "k_up + k_down (expert MLP of one layer)",
+                     "algorithmic_bytes_per_launch": bytes_per_layer},
+        "setup_s": {"store_generation": t_gen}}))
+    del gp, g
     pool.close()
 
 
@@ -1026,6 +1120,9 @@ def main():
         return
     if args.case == "fill":
         fill_case(args)
+        return
+    if args.case == "stack3":
+        gptoss_stack_case(args)
         return
     if args.case == "layer":
         layer_case(args)
