@@ -956,7 +956,11 @@ int ms_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* str
     if ((rc = wide_experts(p, x, T, k, p->inds, p->scores_f, p->pair_slot, y, s))) return rc;
   } else {
     const int max_groups = std::min(T * k, p->geom.n_experts);
-    CK(run_experts(p, exp_args(p, x, T, y, p->scores_f), max_groups, s));
+    ExpArgs e = exp_args(p, x, T, y, p->scores_f);
+    // one token: the route step groups the token's k distinct experts one
+    // per group, in rank order (its k <= 32 path)
+    if (T == 1 && k <= 32 && std::min(k * p->cfg.pf_widen, p->geom.n_experts) <= 32) e.cl_k = k;
+    CK(run_experts(p, e, max_groups, s));
   }
   if (ev) CK(cudaEventRecordWithFlags(ev[3], s, rec_flags));
   return MS_OK;

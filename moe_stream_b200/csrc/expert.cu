@@ -166,8 +166,34 @@ __global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2)
 }
 
 
+// Largest cluster of k_down's one-token combine (the portable cluster size).
+constexpr int CL_MAX = 8;
+
+// DSMEM address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(const void* p, unsigned rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
 // TMA: the RT*16 down rows of the unit come as one tensor-map box.
-template <int MODEL, int KPW, int RT, bool TMA>
+// CL (one token, launched as clusters of the k CTAs that share a row tile,
+// one per expert): each CTA writes its rows into the shared memory of the
+// cluster's first CTA, which combines them after one cluster barrier --
+// instead of the global partials, fence and arrival counter of the general
+// path. Same values, same j order.
+template <int MODEL, int KPW, int RT, bool TMA, bool CL>
 __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A, const __grid_constant__ CUtensorMap tmD) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + (TMA ? ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) : 0u);
@@ -175,12 +201,18 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A, const __grid_con
   // filled slots can be read now; only h (k_up's output) needs pdl_wait
   const int g = blockIdx.y;
   const int n_groups = *A.grp.n_groups;
-  const int slot = A.grp.grp_slot[g];           // one round trip, as in k_up
-  const int m = A.grp.grp_count[g], start = A.grp.grp_start[g];
-  if (g >= n_groups) {
+  // (CL: a CTA past the groups -- never launched so by the block call --
+  // still reaches the cluster barrier, with no slot and no pairs)
+  const bool live = g < n_groups;
+  const int slot = live ? A.grp.grp_slot[g] : -1;   // one round trip, as in k_up
+  const int m = live ? A.grp.grp_count[g] : 0, start = A.grp.grp_start[g];
+  // CL: the cluster's y extent is the token's k experts, one group each
+  __shared__ float s_y[CL ? CL_MAX : 1][RT * 16];
+  if (!CL && !live) {
     pdl_wait();
     return;
   }
+  const bool cl_ok = !CL || n_groups == (int)gridDim.y;
   constexpr int WPT = EX_WARPS / RT;            // warps per row tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g4 = lane >> 2, c = lane & 3;
   const int sub = warp / WPT, wk = warp % WPT;
@@ -270,7 +302,14 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A, const __grid_con
             const uint16_t* bdp = reinterpret_cast<const uint16_t*>(blob + A.geo.off[2][3]);
             v = bfr(v + bf2f(bdp[row]));
           }
-          A.ypart[(long long)pairs[col] * D + row] = (slot >= 0 && ok) ? v : 0.f;
+          v = (slot >= 0 && ok) ? v : 0.f;
+          if (CL) {
+            const int j = pairs[col];            // one token: the pair is its j
+            if (cl_ok && j >= 0 && j < (int)gridDim.y)
+              st_cluster_f32(cluster_map(&s_y[j][row - blockIdx.x * RT * 16], 0), v);
+          } else {
+            A.ypart[(long long)pairs[col] * D + row] = v;
+          }
         }
       }
     }
@@ -280,6 +319,21 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A, const __grid_con
   // the next kernel in the stream (the next layer's route step) may launch
   // while the arrivals and combines finish; it waits for this grid itself
   pdl_trigger();
+  if (CL) {
+    // every CTA of the cluster has written its rows into the first one's
+    // s_y; that CTA adds them in j order
+    cluster_sync();
+    if (cluster_rank() != 0) return;
+    if (!cl_ok && threadIdx.x == 0) atomicCAS(A.status, 0, ST_E_INVALID);
+    for (int i = threadIdx.x; i < RT * 16; i += EX_THREADS) {
+      const int row = blockIdx.x * RT * 16 + i;
+      float acc = 0.f;
+      for (int j = 0; j < (int)gridDim.y; ++j)
+        acc += cl_ok ? bfr(A.scores[j] * s_y[j][i]) : 0.f;   // engine_v3.py:600
+      A.y[row] = A.resid ? f2bf(bf2f(A.resid[row]) + bfr(acc)) : f2bf(acc);
+    }
+    return;
+  }
   // ---- arrival: the last CTA of a row tile combines all tokens' k parts
   __threadfence();
   __syncthreads();
@@ -311,8 +365,10 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A, const __grid_con
   }
 }
 
+// cluster_y > 0: clusters of (1, cluster_y, 1) CTAs
 template <typename Kern, typename... Args>
-static cudaError_t launch_pdl(Kern kern, dim3 grid, int smem, cudaStream_t s, const Args&... args) {
+static cudaError_t launch_pdl(Kern kern, dim3 grid, int smem, cudaStream_t s, int cluster_y,
+                              const Args&... args) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
@@ -320,11 +376,18 @@ static cudaError_t launch_pdl(Kern kern, dim3 grid, int smem, cudaStream_t s, co
   cfg.blockDim = dim3(EX_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (cluster_y > 0) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = cluster_y;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
@@ -351,16 +414,20 @@ static cudaError_t launch_pair(const ExpArgs& a, int max_groups, cudaStream_t s,
   const int K = a.geo.d_model, F = a.geo.d_ff;
   const dim3 gu(F / 16, max_groups), gd(K / (16 * RT), max_groups);
   const int su = UpSmem::total(K, maps != nullptr), sd = DownSmem::total(F, RT, maps != nullptr);
+  // one-token block call: the k CTAs of a row tile combine as a cluster
+  const int cl = (a.cl_k > 0 && a.cl_k <= CL_MAX && max_groups == a.cl_k) ? a.cl_k : 0;
   cudaError_t e;
   if (maps) {
-    e = launch_pdl(k_up<MODEL, KPW_UP, true>, gu, su, s, a, maps[0], maps[1]);
+    e = launch_pdl(k_up<MODEL, KPW_UP, true>, gu, su, s, 0, a, maps[0], maps[1]);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_down<MODEL, KPW_DN, RT, true>, gd, sd, s, a, maps[2]);
+    if (cl) return launch_pdl(k_down<MODEL, KPW_DN, RT, true, true>, gd, sd, s, cl, a, maps[2]);
+    return launch_pdl(k_down<MODEL, KPW_DN, RT, true, false>, gd, sd, s, 0, a, maps[2]);
   }
   CUtensorMap none{};
-  e = launch_pdl(k_up<MODEL, KPW_UP, false>, gu, su, s, a, none, none);
+  e = launch_pdl(k_up<MODEL, KPW_UP, false>, gu, su, s, 0, a, none, none);
   if (e != cudaSuccess) return e;
-  return launch_pdl(k_down<MODEL, KPW_DN, RT, false>, gd, sd, s, a, none);
+  if (cl) return launch_pdl(k_down<MODEL, KPW_DN, RT, false, true>, gd, sd, s, cl, a, none);
+  return launch_pdl(k_down<MODEL, KPW_DN, RT, false, false>, gd, sd, s, 0, a, none);
 }
 
 cudaError_t launch_expert(const ExpArgs& a, int max_groups, cudaStream_t s, const CUtensorMap* maps) {

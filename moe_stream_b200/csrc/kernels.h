@@ -113,6 +113,10 @@ struct ExpArgs {
   int* status;                // sticky pool status (bounded waits report here)
   const uint8_t* slot_class;  // [n_slots] precision class of each slot's blob (mixed pools)
   const uint16_t* resid;      // bf16 [T, d_model] added to the output (fused residual), or null
+  // k of a one-token block call, whose route step leaves exactly k groups
+  // (the token's distinct experts): k_down then combines within clusters of
+  // k CTAs; 0 for the general arrival-counter combine
+  int cl_k;
 };
 
 // ------------------------------------------------ wide batches (prefill)
