@@ -169,24 +169,6 @@ __global__ void __launch_bounds__(EX_THREADS, (MODEL == 0 && KPW == 4) ? 3 : 2)
 // Largest cluster of k_down's one-token combine (the portable cluster size).
 constexpr int CL_MAX = 8;
 
-// DSMEM address of the same shared variable in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t cluster_map(const void* p, unsigned rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ unsigned cluster_rank() {
-  unsigned r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
 // TMA: the RT*16 down rows of the unit come as one tensor-map box.
 // CL (one token, launched as clusters of the k CTAs that share a row tile,
 // one per expert): each CTA writes its rows into the shared memory of the

@@ -122,6 +122,27 @@ __device__ __forceinline__ bool timed_out(const int* status) {
   return status && *reinterpret_cast<const volatile int*>(status) == -4;
 }
 
+// Thread-block clusters (distributed shared memory within one GPU).
+// DSMEM address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(const void* p, unsigned rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// every thread of every CTA of the cluster: writes before it (shared
+// memory of any CTA of the cluster included) are visible after it
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
