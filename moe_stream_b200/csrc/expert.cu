@@ -237,13 +237,16 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A, const __grid_con
       bulk_g2s_hint(lane ? sB : sS, blob + A.geo.off[2][1 + lane] + (long long)blockIdx.x * RT * 16 * G * 2,
                     DownSmem::sb_bytes(G, RT), bar, pol);
   }
+  // the first pass's pairs come from the route step, so they are read
+  // before the wait for k_up: after it, h is one round trip away, not two
+  __shared__ int s_pairs[8];
+  if (threadIdx.x < 8) s_pairs[threadIdx.x] = (int)threadIdx.x < m ? A.grp.grp_pairs[start + threadIdx.x] : -1;
+  __syncthreads();                              // (also the mbarrier's init)
   pdl_wait();                                   // h and its sums come from k_up
-  __syncthreads();
-  bool ok = true;
-  if (slot >= 0) ok = mbar_wait(bar, 0, A.status);
+  bool ok = true, waited = false;
 
   for (int n0 = 0; n0 < m; n0 += 8) {
-    const int* pairs = A.grp.grp_pairs + start + n0;
+    const int* pairs = s_pairs;
     const int nn = min(8, m - n0);
     const int pb = (g4 < nn) ? pairs[g4] : -1;
     // h fragments requested before the sums' round trip, so the two overlap
@@ -258,6 +261,11 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A, const __grid_con
       const float4 a = hp4[0], b = hp4[1];
       s_sums[(col * G + kg) * 2] = (a.x + a.z) + (b.x + b.z);
       s_sums[(col * G + kg) * 2 + 1] = (a.y + a.w) + (b.y + b.w);
+    }
+    // the weights (copied since the kernel's start) after h was requested
+    if (!waited) {
+      if (slot >= 0) ok = mbar_wait(bar, 0, A.status);
+      waited = true;
     }
     __syncthreads();
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
@@ -296,6 +304,11 @@ __global__ void __launch_bounds__(EX_THREADS) k_down(ExpArgs A, const __grid_con
       }
     }
     __syncthreads();
+    if (n0 + 8 < m) {                           // the next pass's pairs
+      if (threadIdx.x < 8)
+        s_pairs[threadIdx.x] = n0 + 8 + (int)threadIdx.x < m ? A.grp.grp_pairs[start + n0 + 8 + threadIdx.x] : -1;
+      __syncthreads();
+    }
   }
 
   // the next kernel in the stream (the next layer's route step) may launch
