@@ -311,6 +311,43 @@ int ms_ep_pack(ms_pool* pool, const void* x, int T, const int32_t* inds, const v
 int ms_ep_combine(ms_pool* pool, const void* back, const int32_t* pair_pos, int T, void* y,
                   void* stream);
 
+/* The expert-parallel block through the C ABI alone (no torch.distributed):
+ * NCCL is loaded at run time (dlopen of libnccl.so.2, the copy a process
+ * already holds if any), so the library needs no NCCL at link time.
+ *
+ * ms_ep_unique_id: a new NCCL unique id (128 bytes) in out; one rank makes
+ * it and the host hands it to every rank by any channel. The calling
+ * process runs NCCL's bootstrap root, so it must live until every rank has
+ * called ms_ep_init.
+ *
+ * ms_ep_init: joins this pool (its device, one process or thread per GPU)
+ * to a group of `world` ranks; blocks until every rank has joined. The pool
+ * holds this rank's experts of the layer resident (ms_pool_read). placement
+ * (host int32 [n_experts][1 + 2*max_rep], as ms_ep_pack reads it; NULL for
+ * plain sharding: expert e on rank e / (n_experts / world), slot e % that)
+ * is copied. MS_E_STATE if the pool already has a group; MS_E_CUDA with the
+ * message when NCCL is missing or fails.
+ *
+ * ms_ep_moe_block: the expert-parallel block on this rank's T tokens x
+ * (bf16 [T, d_model], device) -> y (bf16 [T, d_model]), the multi-GPU form
+ * of ms_moe_block on `layer` (whose router must be set): route (ms_route),
+ * pack (ms_ep_pack), exchange the pair counts and then the rows with NCCL
+ * send/recv on `stream`, run the received rows through this rank's experts
+ * (ms_expert_mlp, k = 1), send them back and combine (ms_ep_combine). Every
+ * rank calls it for the same layer, each with its own T (which may differ);
+ * the result equals the single-GPU block bit for bit. One host
+ * synchronisation of `stream` per call (the split sizes); the rows a rank
+ * receives (up to every rank's T * top_k) must fit the pool's max_tokens.
+ * Scratch buffers grow on demand, so the first call at a new size allocates.
+ *
+ * ms_ep_finalize: leaves the group (destroys the communicator, frees the
+ * scratch); ms_pool_destroy does it too. */
+int ms_ep_unique_id(uint8_t out[128]);
+int ms_ep_init(ms_pool* pool, const uint8_t id[128], int rank, int world, const int32_t* placement,
+               int max_rep);
+int ms_ep_moe_block(ms_pool* pool, int layer, const void* x, int T, void* y, void* stream);
+int ms_ep_finalize(ms_pool* pool);
+
 /* ms_expert_mlp without a pool and without any allocation. This entry point
  * has no counterpart in the reference. It is for callers that may not call
  * cudaMalloc when they run the block -- a runtime that reserved all device

@@ -103,6 +103,12 @@ EXPORTS = {
                    ctypes.c_void_p],
     "ms_ep_combine": [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                       ctypes.c_void_p, ctypes.c_void_p],
+    "ms_ep_unique_id": [ctypes.c_void_p],
+    "ms_ep_init": [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                   ctypes.c_int],
+    "ms_ep_moe_block": [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                        ctypes.c_void_p, ctypes.c_void_p],
+    "ms_ep_finalize": [ctypes.c_void_p],
 }
 
 _LIB = None

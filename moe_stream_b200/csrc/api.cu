@@ -13,6 +13,7 @@
 #include "../../include/moestream.h"
 #include "host_wait.h"
 #include "kernels.h"
+#include "nccl_rt.h"
 
 using namespace ms;
 
@@ -200,7 +201,61 @@ struct ms_pool {
   float cur_norm_eps = 0.f;
   const uint16_t* cur_resid = nullptr;        // combines add it to the output
   uint16_t* xnorm = nullptr;                  // [max_tokens, d_model]: normalised input (wide path)
+  // expert-parallel group of the C-ABI block (ms_ep_init), or null
+  struct EpState* ep = nullptr;
 };
+
+// A pool's expert-parallel group: the communicator, the placement, and
+// scratch sized by the largest call so far.
+struct EpState {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1, e_local = 0, max_rep = 0;
+  int32_t* placement = nullptr;   // device [n_experts][1 + 2*max_rep], or null
+  int cap_T = 0;                  // local tokens the send side holds
+  int32_t* inds = nullptr;        // [cap_T * k]
+  uint16_t* scores = nullptr;     // [cap_T * k] bf16
+  uint16_t* send_x = nullptr;     // [cap_T * k][d]
+  int32_t* send_meta = nullptr;   // [cap_T * k][2]
+  int32_t* pair_pos = nullptr;    // [cap_T * k]
+  uint16_t* back = nullptr;       // [cap_T * k][d]
+  int32_t* counts = nullptr;      // [2][world]: send, receive
+  long long cap_recv = 0;         // rows the receive side holds
+  uint16_t* recv_x = nullptr;     // [cap_recv][d]
+  int32_t* recv_meta = nullptr;   // [cap_recv][2]
+  int32_t* recv_slots = nullptr;  // [cap_recv]
+  float* recv_scores = nullptr;   // [cap_recv]
+  uint16_t* y_recv = nullptr;     // [cap_recv][d]
+  int32_t* h_counts = nullptr;    // pinned [2][world]
+};
+
+static void ep_free_send(EpState* e) {
+  for (void* b : {(void*)e->inds, (void*)e->scores, (void*)e->send_x, (void*)e->send_meta,
+                  (void*)e->pair_pos, (void*)e->back})
+    if (b) cudaFree(b);
+  e->inds = nullptr, e->scores = nullptr, e->send_x = nullptr, e->send_meta = nullptr;
+  e->pair_pos = nullptr, e->back = nullptr;
+  e->cap_T = 0;
+}
+
+static void ep_free_recv(EpState* e) {
+  for (void* b : {(void*)e->recv_x, (void*)e->recv_meta, (void*)e->recv_slots, (void*)e->recv_scores,
+                  (void*)e->y_recv})
+    if (b) cudaFree(b);
+  e->recv_x = nullptr, e->recv_meta = nullptr, e->recv_slots = nullptr, e->recv_scores = nullptr;
+  e->y_recv = nullptr;
+  e->cap_recv = 0;
+}
+
+static void ep_release(EpState* e) {
+  if (!e) return;
+  if (e->comm && nccl_rt().ok) nccl_rt().CommDestroy(e->comm);
+  ep_free_send(e);
+  ep_free_recv(e);
+  if (e->placement) cudaFree(e->placement);
+  if (e->counts) cudaFree(e->counts);
+  if (e->h_counts) cudaFreeHost(e->h_counts);
+  delete e;
+}
 
 namespace {
 
@@ -492,6 +547,7 @@ int ms_pool_destroy(ms_pool* p) {
   if (!p) return MS_OK;
   cudaSetDevice(p->device);
   cudaDeviceSynchronize();
+  ep_release(p->ep);
   for (void* b : p->dev_blocks) cudaFree(b);
   for (cudaEvent_t e : p->prof_ev) cudaEventDestroy(e);
   if (p->ev_fork) cudaEventDestroy(p->ev_fork);
@@ -1125,6 +1181,184 @@ int ms_ep_combine(ms_pool* p, const void* back, const int32_t* pair_pos, int T, 
   const long long chunks = (long long)T * (c.d / 8);
   CK(launch_combine(c, (int)std::min<long long>((chunks + 255) / 256, p->sm_count * 8), s));
   return MS_OK;
+}
+
+// ------------------------------------------------- expert parallelism, C ABI
+#define NCK(call)                                                                      \
+  do {                                                                                 \
+    const ncclResult_t r_ = (call);                                                    \
+    if (r_ != ncclSuccess)                                                             \
+      return fail(MS_E_CUDA, "%s failed: %s", #call, nccl_rt().GetErrorString(r_));   \
+  } while (0)
+
+int ms_ep_unique_id(uint8_t out[128]) {
+  if (!out) return fail(MS_E_INVALID, "NULL argument");
+  const NcclRt& rt = nccl_rt();
+  if (!rt.ok) return fail(MS_E_CUDA, "NCCL unavailable: %s", rt.why);
+  ncclUniqueId id;
+  NCK(rt.GetUniqueId(&id));
+  static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+  memcpy(out, &id, sizeof(id));
+  return MS_OK;
+}
+
+int ms_ep_init(ms_pool* p, const uint8_t id[128], int rank, int world, const int32_t* placement,
+               int max_rep) {
+  if (!p || !id) return fail(MS_E_INVALID, "NULL argument");
+  if (p->ep) return fail(MS_E_STATE, "the pool already belongs to an expert-parallel group");
+  if (world < 1 || world > 64 || rank < 0 || rank >= world)
+    return fail(MS_E_INVALID, "rank=%d / world=%d outside 0 <= rank < world <= 64", rank, world);
+  const int E = p->geom.n_experts;
+  if (!placement && E % world) return fail(MS_E_INVALID, "%d experts do not shard over %d ranks", E, world);
+  if (placement && (max_rep < 1 || max_rep > world))
+    return fail(MS_E_INVALID, "max_rep=%d outside [1, world=%d]", max_rep, world);
+  if (placement) {
+    // every replica's (rank, slot) inside the group and the pool
+    for (int e = 0; e < E; ++e) {
+      const int32_t* row = placement + (size_t)e * (1 + 2 * max_rep);
+      if (row[0] < 1 || row[0] > max_rep)
+        return fail(MS_E_INVALID, "placement: expert %d has %d replicas", e, row[0]);
+      for (int i = 0; i < row[0]; ++i)
+        if (row[1 + 2 * i] < 0 || row[1 + 2 * i] >= world || row[2 + 2 * i] < 0 ||
+            row[2 + 2 * i] >= p->cfg.n_slots)
+          return fail(MS_E_INVALID, "placement: expert %d replica %d outside the ranks or slots", e, i);
+    }
+  }
+  const NcclRt& rt = nccl_rt();
+  if (!rt.ok) return fail(MS_E_CUDA, "NCCL unavailable: %s", rt.why);
+  CK(cudaSetDevice(p->device));
+  EpState* e = new EpState();
+  e->rank = rank;
+  e->world = world;
+  e->e_local = E / world;
+  auto bail = [&](int rc) {
+    ep_release(e);
+    return rc;
+  };
+  if (placement) {
+    e->max_rep = max_rep;
+    const size_t n = (size_t)E * (1 + 2 * max_rep);
+    if (int rc = dalloc(&e->placement, n)) return bail(rc);
+    if (cudaMemcpy(e->placement, placement, n * sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess)
+      return bail(fail(MS_E_CUDA, "placement copy failed"));
+  }
+  if (int rc = dalloc(&e->counts, 2 * (size_t)world)) return bail(rc);
+  if (cudaMallocHost(reinterpret_cast<void**>(&e->h_counts), 2 * world * sizeof(int32_t)) != cudaSuccess)
+    return bail(fail(MS_E_NOMEM, "pinned counts"));
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  const ncclResult_t r = rt.CommInitRank(&e->comm, world, uid, rank);
+  if (r != ncclSuccess) {
+    e->comm = nullptr;
+    return bail(fail(MS_E_CUDA, "ncclCommInitRank failed: %s", rt.GetErrorString(r)));
+  }
+  p->ep = e;
+  return MS_OK;
+}
+
+int ms_ep_finalize(ms_pool* p) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  if (!p->ep) return MS_OK;
+  CK(cudaSetDevice(p->device));
+  CK(cudaDeviceSynchronize());
+  ep_release(p->ep);
+  p->ep = nullptr;
+  return MS_OK;
+}
+
+int ms_ep_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* stream) {
+  if (!p) return fail(MS_E_INVALID, "NULL pool");
+  EpState* e = p->ep;
+  if (!e) return fail(MS_E_STATE, "no expert-parallel group (ms_ep_init)");
+  if (!x || !y) return fail(MS_E_INVALID, "NULL argument");
+  if (T <= 0) return fail(MS_E_INVALID, "T=%d must be positive", T);
+  const NcclRt& rt = nccl_rt();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CK(cudaSetDevice(p->device));
+  const int k = p->geom.top_k, d = p->geom.d_model, W = e->world;
+  const long long P = (long long)T * k;
+  // send-side scratch for T local tokens
+  if (T > e->cap_T) {
+    CK(cudaStreamSynchronize(s));
+    ep_free_send(e);
+    int rc;
+    if ((rc = dalloc(&e->inds, P)) || (rc = dalloc(&e->scores, P)) || (rc = dalloc(&e->send_x, P * d)) ||
+        (rc = dalloc(&e->send_meta, 2 * P)) || (rc = dalloc(&e->pair_pos, P)) ||
+        (rc = dalloc(&e->back, P * d))) {
+      ep_free_send(e);
+      return rc;
+    }
+    e->cap_T = T;
+  }
+  // 1-2. route and pack (destination-major)
+  if (int rc = ms_route(p, layer, x, T, e->inds, e->scores, nullptr, stream)) return rc;
+  if (int rc = ms_ep_pack(p, x, T, e->inds, e->scores, W, e->e_local, e->placement,
+                          e->placement ? e->max_rep : 0, e->send_x, e->send_meta, e->counts,
+                          e->pair_pos, stream))
+    return rc;
+  // 3. pair counts, then (once the host knows them) the rows and metadata
+  int32_t* recv_counts = e->counts + W;
+  NCK(rt.GroupStart());
+  for (int r = 0; r < W; ++r) {
+    NCK(rt.Send(e->counts + r, 1, ncclInt32, r, e->comm, s));
+    NCK(rt.Recv(recv_counts + r, 1, ncclInt32, r, e->comm, s));
+  }
+  NCK(rt.GroupEnd());
+  CK(cudaMemcpyAsync(e->h_counts, e->counts, 2 * W * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  HWAIT(stream_wait_bounded(s));
+  const int32_t* sc = e->h_counts;
+  const int32_t* rcn = e->h_counts + W;
+  std::vector<long long> soff(W + 1, 0), roff(W + 1, 0);
+  for (int r = 0; r < W; ++r) {
+    if (sc[r] < 0 || rcn[r] < 0) return fail(MS_E_CUDA, "expert-parallel counts corrupt");
+    soff[r + 1] = soff[r] + sc[r];
+    roff[r + 1] = roff[r] + rcn[r];
+  }
+  if (soff[W] != P) return fail(MS_E_CUDA, "ms_ep_pack sent %lld of %lld pairs", soff[W], P);
+  const long long n_recv = roff[W];
+  if (n_recv > p->cfg.max_tokens)
+    return fail(MS_E_INVALID, "%lld rows received, more than the pool's max_tokens=%d", n_recv,
+                p->cfg.max_tokens);
+  if (n_recv > e->cap_recv) {
+    ep_free_recv(e);
+    int rc;
+    if ((rc = dalloc(&e->recv_x, n_recv * d)) || (rc = dalloc(&e->recv_meta, 2 * n_recv)) ||
+        (rc = dalloc(&e->recv_slots, n_recv)) || (rc = dalloc(&e->recv_scores, n_recv)) ||
+        (rc = dalloc(&e->y_recv, n_recv * d))) {
+      ep_free_recv(e);
+      return rc;
+    }
+    e->cap_recv = n_recv;
+  }
+  NCK(rt.GroupStart());
+  for (int r = 0; r < W; ++r) {
+    if (sc[r]) {
+      NCK(rt.Send(e->send_x + soff[r] * d, (size_t)sc[r] * d * 2, ncclUint8, r, e->comm, s));
+      NCK(rt.Send(e->send_meta + soff[r] * 2, (size_t)sc[r] * 2, ncclInt32, r, e->comm, s));
+    }
+    if (rcn[r]) {
+      NCK(rt.Recv(e->recv_x + roff[r] * d, (size_t)rcn[r] * d * 2, ncclUint8, r, e->comm, s));
+      NCK(rt.Recv(e->recv_meta + roff[r] * 2, (size_t)rcn[r] * 2, ncclInt32, r, e->comm, s));
+    }
+  }
+  NCK(rt.GroupEnd());
+  // 4. the received rows through this rank's experts, k = 1 (score folded in)
+  if (n_recv > 0) {
+    CK(cudaMemcpy2DAsync(e->recv_slots, 4, e->recv_meta, 8, 4, n_recv, cudaMemcpyDeviceToDevice, s));
+    CK(cudaMemcpy2DAsync(e->recv_scores, 4, e->recv_meta + 1, 8, 4, n_recv, cudaMemcpyDeviceToDevice, s));
+    if (int rc = ms_expert_mlp(p, e->recv_slots, e->recv_scores, e->recv_x, (int)n_recv, 1, e->y_recv,
+                               stream))
+      return rc;
+  }
+  // 5. the rows back to their senders
+  NCK(rt.GroupStart());
+  for (int r = 0; r < W; ++r) {
+    if (rcn[r]) NCK(rt.Send(e->y_recv + roff[r] * d, (size_t)rcn[r] * d * 2, ncclUint8, r, e->comm, s));
+    if (sc[r]) NCK(rt.Recv(e->back + soff[r] * d, (size_t)sc[r] * d * 2, ncclUint8, r, e->comm, s));
+  }
+  NCK(rt.GroupEnd());
+  // 6. y[t] = sum_j back[pair_pos[t, j]] in j order
+  return ms_ep_combine(p, e->back, e->pair_pos, T, y, stream);
 }
 
 int ms_pool_profile(ms_pool* p, int enable) {

@@ -190,6 +190,45 @@ class DeviceOps:
         return y
 
 
+def ep_unique_id():
+    """A new NCCL unique id (bytes) for EpGroup; one rank makes it and hands it to the
+    others. The calling process hosts NCCL's bootstrap root until every rank has
+    joined."""
+    lib = _lib.load()
+    buf = (ctypes.c_uint8 * 128)()
+    _lib.check(lib.ms_ep_unique_id(buf))
+    return bytes(buf)
+
+
+class EpGroup:
+    """The expert-parallel block through the C ABI alone (ms_ep_init /
+    ms_ep_moe_block): NCCL send/recv inside the library, no torch.distributed.
+    block: this rank's MoEBlock (router set on its pool, the rank's experts
+    resident, e.g. load_local_experts); placement: a plan_placement table or
+    None for plain sharding. __call__(x) is ep_forward(x, DeviceOps(...)) in one
+    library call."""
+
+    def __init__(self, block, unique_id, rank, world, placement=None):
+        self.block = block
+        self.pool = block.pool
+        table, max_rep = None, 0
+        if placement is not None:
+            self._table = np.ascontiguousarray(placement, np.int32)
+            max_rep = (self._table.shape[1] - 1) // 2
+            table = self._table.ctypes.data_as(ctypes.c_void_p)
+        idb = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id)
+        _lib.check(self.pool._lib.ms_ep_init(self.pool._h, idb, rank, world, table, max_rep))
+
+    def __call__(self, x, stream=None):
+        y = torch.empty_like(x)
+        _lib.check(self.pool._lib.ms_ep_moe_block(self.pool._h, self.block._layer, _ptr(x),
+                                                  x.shape[0], _ptr(y), _stream_ptr(stream)))
+        return y
+
+    def close(self):
+        _lib.check(self.pool._lib.ms_ep_finalize(self.pool._h))
+
+
 def load_local_experts(pool, layer, rank, world, slots=None):
     """Fill this rank's slots from the attached store (ExpertPool._read),
     once: slot i <- expert slots[i] of `layer` (a plan_placement row), or
