@@ -159,8 +159,18 @@ def test_c_abi_expert_parallel_matches_one_gpu(replicated, lib, cuda, tmp_path):
     world = 2
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.start_processes(_rank_main_cabi, args=(world, _free_port(), str(tmp_path), replicated),
-                       nprocs=world, start_method="spawn")
+    ctx = mp.start_processes(_rank_main_cabi, args=(world, _free_port(), str(tmp_path), replicated),
+                             nprocs=world, start_method="spawn", join=False)
+    # the ranks get a deadline: a rank stuck in the library's NCCL calls must
+    # fail this test, not stall the run (ending a process ends its GPU work)
+    import time
+    deadline = time.monotonic() + 900
+    while not ctx.join(timeout=5):
+        if time.monotonic() > deadline:
+            for proc in ctx.processes:
+                if proc.is_alive():
+                    proc.kill()
+            pytest.fail("the expert-parallel ranks did not finish within 900 s")
     y_ep = torch.load(tmp_path / "y_ep.pt")
     y_ref = torch.load(tmp_path / "y_ref.pt")
     assert torch.isfinite(y_ep.float()).all()
