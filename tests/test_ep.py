@@ -215,3 +215,19 @@ def test_ep_rank_that_withholds_its_counts_times_out(tmp_path):
     assert msg.startswith("error after"), msg
     secs = float(msg.split()[2])
     assert 2.0 <= secs <= 30.0, msg
+
+
+def test_c_abi_group_id_from_run_time_nccl():
+    """ms_ep_unique_id reaches NCCL through the library's run-time loader
+    (no GPU needed): 128-byte ids, a new one per call. Run in a child process
+    so NCCL's bootstrap thread stays out of the test process."""
+    import subprocess
+    import sys
+    code = ("from moe_stream_b200.ep import ep_unique_id\n"
+            "a, b = ep_unique_id(), ep_unique_id()\n"
+            "assert len(a) == len(b) == 128 and a != b and any(a)\n"
+            "print('ok')\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
