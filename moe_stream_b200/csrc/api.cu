@@ -1279,7 +1279,7 @@ int ms_ep_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* 
   const long long P = (long long)T * k;
   // send-side scratch for T local tokens
   if (T > e->cap_T) {
-    CK(cudaStreamSynchronize(s));
+    HWAIT(stream_wait_bounded(s));       // the old buffers may still be in use on s
     ep_free_send(e);
     int rc;
     if ((rc = dalloc(&e->inds, P)) || (rc = dalloc(&e->scores, P)) || (rc = dalloc(&e->send_x, P * d)) ||
