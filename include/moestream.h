@@ -340,6 +340,11 @@ int ms_ep_combine(ms_pool* pool, const void* back, const int32_t* pair_pos, int 
  * receives (up to every rank's T * top_k) must fit the pool's max_tokens.
  * Scratch buffers grow on demand, so the first call at a new size allocates.
  *
+ * An exchange that fails or runs past the host wait limit (MS_E_CUDA,
+ * MS_E_TIMEOUT: e.g. a rank that died) breaks the group: later calls return
+ * MS_E_STATE, and ms_ep_finalize aborts the communicator rather than
+ * waiting on its stuck operations.
+ *
  * ms_ep_finalize: leaves the group (destroys the communicator, frees the
  * scratch); ms_pool_destroy does it too. */
 int ms_ep_unique_id(uint8_t out[128]);

@@ -226,6 +226,9 @@ struct EpState {
   float* recv_scores = nullptr;   // [cap_recv]
   uint16_t* y_recv = nullptr;     // [cap_recv][d]
   int32_t* h_counts = nullptr;    // pinned [2][world]
+  // an exchange failed or timed out: operations may be stuck in the
+  // communicator, so it is aborted, not destroyed, and not used again
+  bool broken = false;
 };
 
 static void ep_free_send(EpState* e) {
@@ -248,7 +251,10 @@ static void ep_free_recv(EpState* e) {
 
 static void ep_release(EpState* e) {
   if (!e) return;
-  if (e->comm && nccl_rt().ok) nccl_rt().CommDestroy(e->comm);
+  if (e->comm && nccl_rt().ok) {
+    if (e->broken) nccl_rt().CommAbort(e->comm);
+    else nccl_rt().CommDestroy(e->comm);
+  }
   ep_free_send(e);
   ep_free_recv(e);
   if (e->placement) cudaFree(e->placement);
@@ -1266,10 +1272,22 @@ int ms_ep_finalize(ms_pool* p) {
   return MS_OK;
 }
 
+// inside ms_ep_moe_block: an NCCL failure also breaks the group
+#define NCKB(call)                                                                     \
+  do {                                                                                 \
+    const ncclResult_t r_ = (call);                                                    \
+    if (r_ != ncclSuccess) {                                                           \
+      e->broken = true;                                                                \
+      return fail(MS_E_CUDA, "%s failed: %s", #call, nccl_rt().GetErrorString(r_));   \
+    }                                                                                  \
+  } while (0)
+
 int ms_ep_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* stream) {
   if (!p) return fail(MS_E_INVALID, "NULL pool");
   EpState* e = p->ep;
   if (!e) return fail(MS_E_STATE, "no expert-parallel group (ms_ep_init)");
+  if (e->broken)
+    return fail(MS_E_STATE, "the expert-parallel group failed earlier; ms_ep_finalize it and join a new one");
   if (!x || !y) return fail(MS_E_INVALID, "NULL argument");
   if (T <= 0) return fail(MS_E_INVALID, "T=%d must be positive", T);
   const NcclRt& rt = nccl_rt();
@@ -1298,14 +1316,16 @@ int ms_ep_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* 
     return rc;
   // 3. pair counts, then (once the host knows them) the rows and metadata
   int32_t* recv_counts = e->counts + W;
-  NCK(rt.GroupStart());
+  NCKB(rt.GroupStart());
   for (int r = 0; r < W; ++r) {
-    NCK(rt.Send(e->counts + r, 1, ncclInt32, r, e->comm, s));
-    NCK(rt.Recv(recv_counts + r, 1, ncclInt32, r, e->comm, s));
+    NCKB(rt.Send(e->counts + r, 1, ncclInt32, r, e->comm, s));
+    NCKB(rt.Recv(recv_counts + r, 1, ncclInt32, r, e->comm, s));
   }
-  NCK(rt.GroupEnd());
+  NCKB(rt.GroupEnd());
   CK(cudaMemcpyAsync(e->h_counts, e->counts, 2 * W * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-  HWAIT(stream_wait_bounded(s));
+  const cudaError_t we = stream_wait_bounded(s);   // a rank that never sends ends here
+  if (we != cudaSuccess) e->broken = true;
+  HWAIT(we);
   const int32_t* sc = e->h_counts;
   const int32_t* rcn = e->h_counts + W;
   std::vector<long long> soff(W + 1, 0), roff(W + 1, 0);
@@ -1330,18 +1350,18 @@ int ms_ep_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* 
     }
     e->cap_recv = n_recv;
   }
-  NCK(rt.GroupStart());
+  NCKB(rt.GroupStart());
   for (int r = 0; r < W; ++r) {
     if (sc[r]) {
-      NCK(rt.Send(e->send_x + soff[r] * d, (size_t)sc[r] * d * 2, ncclUint8, r, e->comm, s));
-      NCK(rt.Send(e->send_meta + soff[r] * 2, (size_t)sc[r] * 2, ncclInt32, r, e->comm, s));
+      NCKB(rt.Send(e->send_x + soff[r] * d, (size_t)sc[r] * d * 2, ncclUint8, r, e->comm, s));
+      NCKB(rt.Send(e->send_meta + soff[r] * 2, (size_t)sc[r] * 2, ncclInt32, r, e->comm, s));
     }
     if (rcn[r]) {
-      NCK(rt.Recv(e->recv_x + roff[r] * d, (size_t)rcn[r] * d * 2, ncclUint8, r, e->comm, s));
-      NCK(rt.Recv(e->recv_meta + roff[r] * 2, (size_t)rcn[r] * 2, ncclInt32, r, e->comm, s));
+      NCKB(rt.Recv(e->recv_x + roff[r] * d, (size_t)rcn[r] * d * 2, ncclUint8, r, e->comm, s));
+      NCKB(rt.Recv(e->recv_meta + roff[r] * 2, (size_t)rcn[r] * 2, ncclInt32, r, e->comm, s));
     }
   }
-  NCK(rt.GroupEnd());
+  NCKB(rt.GroupEnd());
   // 4. the received rows through this rank's experts, k = 1 (score folded in)
   if (n_recv > 0) {
     CK(cudaMemcpy2DAsync(e->recv_slots, 4, e->recv_meta, 8, 4, n_recv, cudaMemcpyDeviceToDevice, s));
@@ -1351,12 +1371,12 @@ int ms_ep_moe_block(ms_pool* p, int layer, const void* x, int T, void* y, void* 
       return rc;
   }
   // 5. the rows back to their senders
-  NCK(rt.GroupStart());
+  NCKB(rt.GroupStart());
   for (int r = 0; r < W; ++r) {
-    if (rcn[r]) NCK(rt.Send(e->y_recv + roff[r] * d, (size_t)rcn[r] * d * 2, ncclUint8, r, e->comm, s));
-    if (sc[r]) NCK(rt.Recv(e->back + soff[r] * d, (size_t)sc[r] * d * 2, ncclUint8, r, e->comm, s));
+    if (rcn[r]) NCKB(rt.Send(e->y_recv + roff[r] * d, (size_t)rcn[r] * d * 2, ncclUint8, r, e->comm, s));
+    if (sc[r]) NCKB(rt.Recv(e->back + soff[r] * d, (size_t)sc[r] * d * 2, ncclUint8, r, e->comm, s));
   }
-  NCK(rt.GroupEnd());
+  NCKB(rt.GroupEnd());
   // 6. y[t] = sum_j back[pair_pos[t, j]] in j order
   return ms_ep_combine(p, e->back, e->pair_pos, T, y, stream);
 }

@@ -18,6 +18,7 @@ struct NcclRt {
   decltype(&ncclGetUniqueId) GetUniqueId = nullptr;
   decltype(&ncclCommInitRank) CommInitRank = nullptr;
   decltype(&ncclCommDestroy) CommDestroy = nullptr;
+  decltype(&ncclCommAbort) CommAbort = nullptr;
   decltype(&ncclGroupStart) GroupStart = nullptr;
   decltype(&ncclGroupEnd) GroupEnd = nullptr;
   decltype(&ncclSend) Send = nullptr;
@@ -47,6 +48,7 @@ inline const NcclRt& nccl_rt() {
     get(r.GetUniqueId, "ncclGetUniqueId");
     get(r.CommInitRank, "ncclCommInitRank");
     get(r.CommDestroy, "ncclCommDestroy");
+    get(r.CommAbort, "ncclCommAbort");
     get(r.GroupStart, "ncclGroupStart");
     get(r.GroupEnd, "ncclGroupEnd");
     get(r.Send, "ncclSend");
